@@ -1,0 +1,545 @@
+#!/usr/bin/env python
+"""Benchmark: quantized-KV decode attention on B200 (the pack_kv_attention path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|5] [--impl ours|reference]
+
+Default workload (the Llama-3-8B decode shape): per GPU a
+batch of 32 sequences, 32 query / 8 KV heads, head_dim 128, T = 8192 cached
+positions per sequence (+ the step's own new entry), 4-bit MLX-affine K/V,
+group 64, fp16 scales/biases, drawn N(0,1) fp32 -> fp16 -> canonical quantizer
+(seeded synthetic data; the reference measures on no dataset for this path).
+A step is one decode step of the whole batch. With N GPUs every rank runs its
+own batch (batch x KV-head work stays on one GPU: weak scaling, no collective
+on the data path).
+
+--config 5: the long-context sequence split (B=1, 64/8 heads, T=131072,
+4-bit g64): T is sharded into N equal contiguous ranges, each rank computes
+its shard's partial (O, m, l), the partials are all-gathered over NCCL and
+merged by log-sum-exp on every rank (strong scaling).
+
+Timing: W untimed warm-up steps, then exactly K steps between a barrier +
+cudaDeviceSynchronize on both sides, CUDA events on the launching stream, max
+over ranks. Cache sets rotate so that the bytes a step reads are never
+L2-resident (working set > 2 x 126 MB L2). rank 0 prints one JSON line.
+
+--impl reference times the reference's own CPU implementation of the path
+(the numpy port of kv_attention in oracle/, including its canonical
+quantization of the raw cache) on the host cores, a bounded sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L2_BYTES = 126 * 2 ** 20
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "qKV decode attention: µs/step, HBM GB/s & % of roofline at 1/2/4/8 B200"
+
+CONFIG2 = dict(B=32, H=32, HKV=8, DH=128, T=8192, bits=4, group=64)
+CONFIG5 = dict(B=1, H=64, HKV=8, DH=128, T=131072, bits=4, group=64)
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--config", type=int, default=2, choices=(2, 5))
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the batch size (small cases for ncu captures)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the bounded CPU-baseline sample of the ours arm")
+    return ap.parse_args(argv)
+
+
+def kv_bytes(cfg, t_total=None) -> int:
+    """Algorithmic K/V bytes of one step: 2 (K, V) x HKV x sum_b T_b x
+    (DH*bits/8 code bytes + DH/group x 2 fp16 scales/biases x 2 bytes)."""
+    t_sum = t_total if t_total is not None else cfg["B"] * cfg["T"]
+    per_row = cfg["DH"] * cfg["bits"] // 8 + (cfg["DH"] // cfg["group"]) * 4
+    return 2 * cfg["HKV"] * t_sum * per_row
+
+
+def io_bytes(cfg) -> int:
+    """q + new_k + new_v + out bytes (fp16) of one step."""
+    b, h, hkv, dh = cfg["B"], cfg["H"], cfg["HKV"], cfg["DH"]
+    return 2 * (b * h * dh + 2 * b * hkv * dh + b * h * dh)
+
+
+def measured_hbm():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(kernel_key: str):
+    """dram bytes per launch of the partial kernel from the committed ncu
+    summary (profiles/*.json), or None."""
+    path = ROOT / "profiles" / "traffic.json"
+    try:
+        return json.loads(path.read_text()).get(kernel_key)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self, t0: float, t1: float) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 10:
+                    continue
+                try:
+                    ts = time.mktime(time.strptime(parts[1].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                    frac = float("0." + parts[1].split(".")[1]) if "." in parts[1] else 0.0
+                    rows.append((ts + frac, float(parts[2]), float(parts[3]), parts[5:]))
+                except (ValueError, IndexError):
+                    continue
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        inside = [r for r in rows if t0 - 0.05 <= r[0] <= t1 + 0.05]
+        window = "timed region"
+        if not inside:
+            inside = rows
+            window = "warm-up + timed region (the timed region is shorter than the sampling interval)"
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in inside for n, v in zip(names, r[3][1:]) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[1] for r in inside),
+                "sm_max_mhz": max(r[2] for r in inside), "reasons": reasons,
+                "samples": len(inside), "window": window}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def dist_init(world: int, local: int):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    if world > 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return dist if world > 1 else None
+
+
+def max_over_ranks(value: float, dist) -> float:
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    import torch
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------
+# workload on the device
+# ---------------------------------------------------------------------------
+def device_caches(kva, shape, bits, group, seed, device):
+    """Packed (words, scales, biases) for an N(0,1) fp16 cache of `shape`,
+    quantized on the device by the library's canonical quantizer."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    raw = torch.randn(shape, dtype=torch.float32, device=device, generator=g).half()
+    words, scales, biases = kva.quantize(raw, bits, group)
+    del raw
+    return words, scales, biases
+
+
+def build_sets(kva, cfg, n_sets, seed, device, t_rows=None):
+    import torch
+    b, h, hkv, dh = cfg["B"], cfg["H"], cfg["HKV"], cfg["DH"]
+    t = t_rows or cfg["T"]
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    q = torch.randn((b, h, dh), generator=g, device=device).half()
+    nk = torch.randn((b, hkv, dh), generator=g, device=device).half()
+    nv = torch.randn((b, hkv, dh), generator=g, device=device).half()
+    sets = []
+    for i in range(n_sets):
+        kart = device_caches(kva, (b, hkv, t, dh), cfg["bits"], cfg["group"], seed * 1000 + 2 * i, device)
+        vart = device_caches(kva, (b, hkv, t, dh), cfg["bits"], cfg["group"], seed * 1000 + 2 * i + 1, device)
+        sets.append((*kart, *vart))
+    return q, nk, nv, sets
+
+
+# ---------------------------------------------------------------------------
+# the ours arm
+# ---------------------------------------------------------------------------
+def run_ours(args) -> dict | None:
+    import torch
+
+    from kernelverify_b200 import _native
+    from kernelverify_b200.pack import kv_attention as kva
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = dist_init(world, local)
+    lib = _native.lib()
+    cfg = dict(CONFIG2 if args.config == 2 else CONFIG5)
+    if args.batch:
+        cfg["B"] = args.batch
+
+    if args.config == 2:
+        t_rows = cfg["T"]
+        t_lo, t_hi, with_new = 0, cfg["T"], True
+        step_kv = kv_bytes(cfg)
+    else:
+        if cfg["T"] % world:
+            raise SystemExit("T must divide evenly across ranks")
+        t_rows = cfg["T"] // world
+        t_lo, t_hi, with_new = 0, t_rows, rank == world - 1
+        step_kv = kv_bytes(cfg)          # the whole sequence, summed over ranks
+    local_kv = kv_bytes(cfg, cfg["B"] * t_rows)
+    n_sets = max(2, math.ceil(2 * L2_BYTES / local_kv) + 1)
+    q, nk, nv, sets = build_sets(kva, cfg, n_sets, 1 + rank, device, t_rows)
+    out = torch.empty_like(q)
+    margs = []
+    for (kw, ks, kb, vw, vs, vb) in sets:
+        margs.append(kva._args(q, kw, ks, kb, vw, vs, vb, nk, nv, bits=cfg["bits"],
+                               t_cached=t_rows, t_begin=t_lo, t_end=t_hi, has_new_entry=with_new))
+    rows = cfg["B"] * cfg["H"]
+    n_splits = lib.kvq_split_count(margs[0])
+    po = torch.empty((n_splits, rows, cfg["DH"]), dtype=torch.float32, device=device)
+    pm = torch.empty((n_splits, rows), dtype=torch.float32, device=device)
+    pl = torch.empty((n_splits, rows), dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+    sp = stream.cuda_stream
+
+    if args.config == 5:
+        go = torch.empty((world, rows, cfg["DH"]), dtype=torch.float32, device=device)
+        gm = torch.empty((world, rows), dtype=torch.float32, device=device)
+        gl = torch.empty((world, rows), dtype=torch.float32, device=device)
+        lo_ = torch.empty((rows, cfg["DH"]), dtype=torch.float32, device=device)
+        lm_ = torch.empty((rows,), dtype=torch.float32, device=device)
+        ll_ = torch.empty((rows,), dtype=torch.float32, device=device)
+        ws_need = max(lib.kvq_workspace_bytes(a) for a in margs)
+        ws = torch.empty(max(ws_need, 256), dtype=torch.uint8, device=device)
+
+    launches_per_step = 2
+
+    def step(i, ev=None):
+        a = margs[i % n_sets]
+        if args.config == 2:
+            if ev is not None:
+                ev[0].record(stream)
+            _native.check(lib.kvq_decode_splits(a, po.data_ptr(), pm.data_ptr(), pl.data_ptr(), sp))
+            if ev is not None:
+                ev[1].record(stream)
+            _native.check(lib.kvq_lse_merge(po.data_ptr(), pm.data_ptr(), pl.data_ptr(), n_splits,
+                                            rows, cfg["DH"], 0, out.data_ptr(), sp))
+        else:
+            if ev is not None:
+                ev[0].record(stream)
+            _native.check(lib.kvq_decode_partial(a, lo_.data_ptr(), lm_.data_ptr(), ll_.data_ptr(),
+                                                 ws.data_ptr(), ws.numel(), sp))
+            if ev is not None:
+                ev[1].record(stream)
+            if dist is not None:
+                dist.all_gather_into_tensor(go, lo_)
+                dist.all_gather_into_tensor(gm, lm_)
+                dist.all_gather_into_tensor(gl, ll_)
+                src = (go, gm, gl, world)
+            else:
+                src = (lo_.view(1, rows, -1), lm_.view(1, -1), ll_.view(1, -1), 1)
+            _native.check(lib.kvq_lse_merge(src[0].data_ptr(), src[1].data_ptr(), src[2].data_ptr(),
+                                            src[3], rows, cfg["DH"], 0, out.data_ptr(), sp))
+
+    if args.config == 5:
+        launches_per_step = (3 if n_splits > 1 else 2)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    for i in range(args.warmup):
+        step(i)
+    barrier(dist)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(dist)
+    wall0 = time.time()
+    e0.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i, evs[i])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    barrier(dist)
+    clocks = sampler.stop(wall0, wall1)
+    local_ms = e0.elapsed_time(e1) / args.steps
+    kern_ms = statistics.fmean(a.elapsed_time(b) for a, b in evs)
+    step_ms = max_over_ranks(local_ms, dist)
+    kern_ms_max = max_over_ranks(kern_ms, dist)
+
+    # ---- e2e through the public API: pinned host inputs in, result out -------
+    e2e = None
+    if args.config == 2 and not args.no_e2e:
+        hq = q.cpu().pin_memory()
+        hnk = nk.cpu().pin_memory()
+        hnv = nv.cpu().pin_memory()
+        hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        dq, dnk, dnv = torch.empty_like(q), torch.empty_like(nk), torch.empty_like(nv)
+        e2e_args = []
+        for (kw, ks, kb, vw, vs, vb) in sets:
+            e2e_args.append((kw, ks, kb, vw, vs, vb))
+        wsd = kva.Workspace()
+
+        def e2e_step(i):
+            kw, ks, kb, vw, vs, vb = e2e_args[i % n_sets]
+            dq.copy_(hq, non_blocking=True)
+            dnk.copy_(hnk, non_blocking=True)
+            dnv.copy_(hnv, non_blocking=True)
+            res = kva.decode(dq, kw, ks, kb, vw, vs, vb, dnk, dnv, bits=cfg["bits"],
+                             t_cached=t_rows, out=out, workspace=wsd)
+            hout.copy_(res, non_blocking=True)
+
+        for i in range(max(3, args.warmup)):
+            e2e_step(i)
+        barrier(dist)
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for i in range(args.steps):
+            e2e_step(i)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, dist)
+        h2d = hq.numel() * 2 + hnk.numel() * 2 + hnv.numel() * 2
+        e2e = {"value": round(world * step_kv / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+               "us_per_step": round(e2e_ms * 1e3, 2),
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": hout.numel() * 2,
+               "path": "kernelverify_b200.pack.kv_attention.decode -> kvq_decode (C ABI)"}
+
+    if rank != 0:
+        if dist is not None:
+            dist.destroy_process_group()
+        return None
+
+    peak, peak_kind = measured_hbm()
+    alg_kernel = local_kv + io_bytes(cfg) if args.config == 2 else local_kv + io_bytes(cfg) // world
+    achieved = alg_kernel / (kern_ms_max * 1e-3) / 1e9
+    if args.config == 2:
+        value = world * step_kv / (step_ms * 1e-3) / 1e9
+        scaling, workload = "weak", "config2-llama3-8b-decode"
+    else:
+        value = step_kv / (step_ms * 1e-3) / 1e9
+        scaling, workload = "strong", "config5-long-context-tsplit"
+    traffic_key = f"partial_kernel_config{args.config}_n{world}"
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 5),
+        "us_per_step": round(step_ms * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": scaling,
+        "vs_baseline": None,
+        "dtype": "u4 codes, fp16 scales/q/out, fp32 accumulate",
+        "data": "synthetic: N(0,1) fp32 -> fp16 -> canonical MLX-affine quantizer on device, seeded",
+        "config": {"workload": workload, "B": cfg["B"], "n_heads": cfg["H"],
+                   "n_kv_heads": cfg["HKV"], "head_dim": cfg["DH"],
+                   "t_cached": cfg["T"], "bits": cfg["bits"], "group": cfg["group"],
+                   "per_rank_t": t_rows, "n_splits": n_splits,
+                   "l2": f"inputs larger than L2: {n_sets} cache sets of {local_kv / 1e6:.1f} MB rotated",
+                   "kv_bytes_per_step": step_kv, "parallelism": f"dp{world}" if args.config == 2 else f"tsplit{world}"},
+        "hbm_frac_step": round(value / world / peak, 4) if args.config == 2 else round(value / world / peak, 4),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "peak_kind": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+                     "kernel": "partial_kernel (kvq_decode_splits)",
+                     "kernel_us": round(kern_ms_max * 1e3, 2),
+                     "alg_bytes_per_launch": alg_kernel,
+                     "traffic": profiled_traffic(traffic_key)},
+        "clocks": clocks,
+        "e2e": e2e,
+        "gpu_launches": launches_per_step * args.steps,
+    }
+    if args.config == 2 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample(cfg, budget_s=12.0)
+    if dist is not None:
+        dist.destroy_process_group()
+    return line
+
+
+# ---------------------------------------------------------------------------
+# the reference CPU path (numpy port in oracle/)
+# ---------------------------------------------------------------------------
+def _cpu_unit(payload):
+    """One (sequence, KV head) unit of config 2 on the CPU: the reference's
+    fp32 kv_attention port over a raw cache (which it quantizes itself), r
+    query heads sharing the cache head by tiling. Returns seconds."""
+    seed, h_per, t, dh, bits, with_fp64 = payload
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+
+    from oracle import faults, kv
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((1, h_per, dh)).astype(np.float16)
+    kc = rng.standard_normal((1, t, dh)).astype(np.float32).astype(np.float16)
+    vc = rng.standard_normal((1, t, dh)).astype(np.float32).astype(np.float16)
+    nk = rng.standard_normal((1, 1, dh)).astype(np.float16)
+    nv = rng.standard_normal((1, 1, dh)).astype(np.float16)
+    with threadpool_limits(1):
+        inputs = kv.gqa_tiled_inputs(q, kc, vc, nk, nv, bits)
+        t0 = time.perf_counter()
+        faults.kv_attention(inputs)
+        t1 = time.perf_counter()
+        t64 = None
+        if with_fp64:
+            kv._memo.clear()
+            kv.kv_reference(inputs)
+            t64 = time.perf_counter() - t1
+    return t1 - t0, t64
+
+
+def cpu_baseline_sample(cfg, budget_s: float) -> dict:
+    """The oracle's fp32 port timed on one host core over whole (sequence, KV
+    head) units of the workload until `budget_s` of CPU work, scaled to GB/s."""
+    h_per = cfg["H"] // cfg["HKV"]
+    unit_bytes = kv_bytes(dict(cfg, B=1, HKV=1))
+    times, times64, n = [], [], 0
+    start = time.perf_counter()
+    while time.perf_counter() - start < budget_s and n < cfg["B"] * cfg["HKV"]:
+        t32, t64 = _cpu_unit((1000 + n, h_per, cfg["T"], cfg["DH"], cfg["bits"], n < 2))
+        times.append(t32)
+        if t64 is not None:
+            times64.append(t64)
+        n += 1
+    per_unit = statistics.fmean(times)
+    units = cfg["B"] * cfg["HKV"]
+    return {"value": round(unit_bytes / per_unit / 1e9, 4), "unit": "GB/s", "cores": 1,
+            "kind": "port",
+            "us_per_step": round(per_unit * units * 1e6, 0),
+            "fp64_reference_us_per_step": round(statistics.fmean(times64) * units * 1e6, 0) if times64 else None,
+            "sample": f"{n} of {units} (sequence, KV head) units of config 2, each {h_per} query "
+                      f"heads x T={cfg['T']} through the fp32 kv_attention port (oracle/faults.py, "
+                      f"restating kernelverify/reference/native_kernels.py:168-221) incl. its "
+                      f"canonical quantization of the raw cache, 1 thread; us_per_step scales "
+                      f"the per-unit time to all {units} units"}
+
+
+def run_reference(args) -> dict | None:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return None
+    import multiprocessing as mp
+    cfg = dict(CONFIG2)
+    h_per = cfg["H"] // cfg["HKV"]
+    cores = os.cpu_count() or 1
+    unit_bytes = kv_bytes(dict(cfg, B=1, HKV=1))
+    units_per_step = cores
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        def one_step(s):
+            payload = [(50_000 + s * units_per_step + i, h_per, cfg["T"], cfg["DH"], cfg["bits"], False)
+                       for i in range(units_per_step)]
+            t0 = time.perf_counter()
+            pool.map(_cpu_unit, payload)
+            return time.perf_counter() - t0
+        for s in range(args.warmup):
+            one_step(s)
+        times = [one_step(args.warmup + s) for s in range(args.steps)]
+    step_s = statistics.fmean(times)
+    value = units_per_step * unit_bytes / step_s / 1e9
+    sample = (f"{units_per_step} (sequence, KV head) units of config 2 per step ({h_per} query "
+              f"heads x T={cfg['T']} each, 1 of {cfg['B'] * cfg['HKV']} units of a full step), one "
+              f"per process over {cores} processes, fp32 kv_attention numpy port incl. canonical "
+              f"quantization")
+    full_step_us = step_s * (cfg["B"] * cfg["HKV"] / units_per_step) * 1e6
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_s * 1e3, 3), "us_per_full_step": round(full_step_us, 0),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 (numpy port)", "data": "synthetic, seeded, config-2 shapes",
+        "config": {"workload": "config2-llama3-8b-decode", "B": cfg["B"], "n_heads": cfg["H"],
+                   "n_kv_heads": cfg["HKV"], "head_dim": cfg["DH"], "t_cached": cfg["T"],
+                   "bits": cfg["bits"], "group": cfg["group"]},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    line = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,177 @@
+/*
+ * kvq_b200.h -- C ABI of the B200 (sm_100a) quantized-KV decode attention.
+ *
+ * One decode step of attention over an MLX-affine packed K/V cache: per
+ * (batch row b, query head h), scores q . dequant(K_t) / sqrt(DH) over the
+ * logical cached positions t plus the step's own new entry (new_k at full
+ * precision), an fp32 max-shifted softmax over T+1, and the combine
+ * sum_t p_t dequant(V_t) + p_new new_v, cast once to the output dtype.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * handle (a cudaStream_t passed as void*; NULL is the legacy default stream).
+ * The library never allocates device memory: scratch space ("workspace") is
+ * passed in, sized by kvq_workspace_bytes(). Calls are asynchronous on the
+ * given stream, reentrant, and return KVQ_OK or a negative status; the
+ * message of the calling thread's last failure is kvq_last_error().
+ * Nothing here aborts or traps.
+ *
+ * The packed-cache layout is the reference's (MLX affine):
+ *   wq     uint32 [rows, DH*bits/32]  contiguous little-endian code stream per
+ *                                     row, code i at bit i*bits (3- and 6-bit
+ *                                     codes straddle words)
+ *   scales dtype  [rows, DH/group]    per-group scale, stored in the cache's
+ *   biases dtype  [rows, DH/group]    dtype (fp16 caches: fp16)
+ * A row is one (cache head, position). Row index of (b, kv head hk, t):
+ *   b * cache_batch_stride + hk * t_stride + t
+ * cache_batch_stride = 0 is the reference's cache shared by every batch row;
+ * cache_batch_stride = n_kv_heads * t_stride is one cache per sequence.
+ * Query head h reads cache head h / (n_heads / n_kv_heads) (contiguous GQA
+ * blocks); new_k/new_v are [b_rows, n_kv_heads, DH].
+ */
+#ifndef KVQ_B200_H
+#define KVQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVQ_ABI_VERSION 1
+
+/* status codes */
+#define KVQ_OK 0
+#define KVQ_ERR_INVALID (-1)     /* bad shape, bits, group, dtype, alignment or size  */
+#define KVQ_ERR_LAUNCH (-2)      /* a CUDA launch or configuration error              */
+#define KVQ_ERR_UNSUPPORTED (-3) /* no device, or not an sm_100 device                */
+
+/* element type of q, new_k, new_v, out, scales and biases */
+#define KVQ_F16 0
+#define KVQ_F32 1
+
+/* "to the end of the sequence" for kvq_args.t_end */
+#define KVQ_T_END_ALL 0xFFFFFFFFu
+
+/*
+ * One decode step. Replaces the raw-door binding list of kernelverify's
+ * kv_attn_decode (kernelverify/pack/kv_attention.py:302-351: q, k_wq,
+ * k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, out, n_heads,
+ * t_cached, n_kv_heads, t_stride, grid extent b_rows) and extends it with the
+ * group size (the reference fixes 64), per-sequence caches, ragged lengths
+ * and a T-range shard.
+ */
+typedef struct kvq_args {
+    const void* q;            /* [b_rows, n_heads, head_dim] dtype            */
+    const uint32_t* k_wq;     /* packed K codes                                */
+    const void* k_scales;     /* K per-group scales, dtype                     */
+    const void* k_biases;     /* K per-group biases, dtype                     */
+    const uint32_t* v_wq;     /* packed V codes                                */
+    const void* v_scales;
+    const void* v_biases;
+    const void* new_k;        /* [b_rows, n_kv_heads, head_dim] dtype          */
+    const void* new_v;
+    const int32_t* seq_lens;  /* [b_rows] logical cached lengths, or NULL: every
+                                 row has t_cached                              */
+    uint32_t b_rows;
+    uint32_t n_heads;         /* query heads                                   */
+    uint32_t n_kv_heads;      /* cache heads; n_heads % n_kv_heads == 0         */
+    uint32_t t_cached;        /* logical cached positions (when seq_lens NULL)  */
+    uint32_t t_stride;        /* physical rows per cache head (>= every length) */
+    uint32_t head_dim;        /* 64 or 128                                     */
+    uint32_t bits;            /* 2, 3, 4, 6 or 8                               */
+    uint32_t group_size;      /* 32, 64 or 128; divides head_dim               */
+    uint32_t dtype;           /* KVQ_F16 or KVQ_F32                            */
+    uint32_t has_new_entry;   /* 1: the step's own K/V enter this call          */
+    uint64_t cache_batch_stride; /* rows between batch rows' caches; 0 = shared */
+    uint32_t t_begin;         /* first position of this call's T range          */
+    uint32_t t_end;           /* one past the last (clamped to each length)     */
+} kvq_args;
+
+/* Bytes of scratch `kvq_decode` / `kvq_decode_partial` need for these
+ * arguments (0 when none); `workspace` must be 256-byte aligned. */
+size_t kvq_workspace_bytes(const kvq_args* a);
+
+/*
+ * The full step: out [b_rows, n_heads, head_dim] in args->dtype.
+ * Long caches are split along T into chunks processed in parallel, each
+ * producing an unnormalised partial (O, m, l), merged by a log-sum-exp
+ * combine (the reference kernel's T <= 1024 capacity bound does not exist
+ * here). Reference: kv_attn_decode, kernelverify/pack/kv_attention.py:85-234.
+ */
+int kvq_decode(const kvq_args* a, void* out, void* workspace, size_t workspace_bytes,
+               void* stream);
+
+/*
+ * One T-range shard of the step (positions [t_begin, t_end) of every row,
+ * plus the new entry when has_new_entry): the merged partial of that shard,
+ *   part_o [b_rows, n_heads, head_dim] fp32, unnormalised, relative to part_m
+ *   part_m [b_rows, n_heads]           fp32, max score (-inf: empty shard)
+ *   part_l [b_rows, n_heads]           fp32, sum of exp(score - part_m)
+ * Sharding a sequence by T range across GPUs and merging the shards with
+ * kvq_lse_merge gives the same step as kvq_decode. No reference counterpart
+ * (the reference kernel is single-pass, kernelverify/pack/kv_attention.py:53-65).
+ */
+int kvq_decode_partial(const kvq_args* a, float* part_o, float* part_m, float* part_l,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Number of T splits kvq_decode_splits produces for these arguments (0 when
+ * the arguments are invalid). */
+uint32_t kvq_split_count(const kvq_args* a);
+
+/*
+ * The split stage of kvq_decode on its own: one unnormalised partial per
+ * (T split, row), part_o [n_splits, b_rows*n_heads, head_dim] fp32 and
+ * part_m/part_l [n_splits, b_rows*n_heads], n_splits = kvq_split_count(a).
+ * kvq_lse_merge over them with n_parts = n_splits is kvq_decode's output.
+ * Needs no workspace.
+ */
+int kvq_decode_splits(const kvq_args* a, float* part_o, float* part_m, float* part_l,
+                      void* stream);
+
+/*
+ * Log-sum-exp merge of n_parts partials of `rows` (= b_rows * n_heads) rows:
+ * part_o [n_parts, rows, head_dim], part_m/part_l [n_parts, rows]; part p
+ * starts at p * rows rows. m = max_p m_p, l = sum_p l_p e^(m_p - m),
+ * out = sum_p O_p e^(m_p - m) / l cast to out_dtype.
+ */
+int kvq_lse_merge(const float* part_o, const float* part_m, const float* part_l,
+                  uint32_t n_parts, uint32_t rows, uint32_t head_dim, uint32_t out_dtype,
+                  void* out, void* stream);
+
+/*
+ * fp32 dequantized values [rows, head_dim] of a packed artefact: scale * code
+ * + bias per group, a rounded multiply then a rounded add -- bit-exact to the
+ * reference's _cache_dequant (kernelverify/reference/native_kernels.py:153-165,
+ * kernelverify/schemas/quant_contract.py:107-113).
+ */
+int kvq_dequant(const uint32_t* wq, const void* scales, const void* biases,
+                uint64_t rows, uint32_t head_dim, uint32_t bits, uint32_t group_size,
+                uint32_t dtype, float* out, void* stream);
+
+/*
+ * The canonical MLX-affine quantizer and packer on the device, bit-exact to
+ * canonical_quantize + pack_codes
+ * (kernelverify/schemas/quant_contract.py:60-104,
+ * kernelverify/pack/wide_qmv.py:185-201, as composed by quantize_cache,
+ * kernelverify/pack/kv_attention.py:270-283): w [rows, head_dim] dtype in,
+ * wq/scales/biases out (scales and biases in dtype).
+ */
+int kvq_quantize(const void* w, uint64_t rows, uint32_t head_dim, uint32_t bits,
+                 uint32_t group_size, uint32_t dtype, uint32_t* wq, void* scales,
+                 void* biases, void* stream);
+
+/* 1 when this library carries a kernel for the combination, else 0. */
+int kvq_supports(uint32_t head_dim, uint32_t bits, uint32_t group_size, uint32_t dtype);
+
+/* The calling thread's last error message ("" when none). */
+const char* kvq_last_error(void);
+
+/* KVQ_ABI_VERSION of the loaded library. */
+int kvq_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVQ_B200_H */

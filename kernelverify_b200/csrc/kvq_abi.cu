@@ -1,0 +1,344 @@
+// The C ABI (include/kvq_b200.h): argument validation, the split plan, and
+// dispatch to the per-width launchers. Nothing here allocates device memory;
+// every failure returns a status and leaves a message for kvq_last_error().
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "kvq_b200.h"
+#include "kvq_launch.h"
+#include "kvq_partial.cuh"
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(KVQ_ERR_LAUNCH, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// sm_100 check of the current device, cached per device id.
+int device_ok() {
+    static thread_local int checked[64] = {0};  // 0 unknown, 1 ok, -1 not sm_100
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(KVQ_ERR_UNSUPPORTED, "no CUDA device: %s", cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64 && checked[dev] != 0)
+        return checked[dev] > 0 ? KVQ_OK
+                                : fail(KVQ_ERR_UNSUPPORTED, "device %d is not an sm_100 (B200) GPU", dev);
+    int major = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return fail(KVQ_ERR_UNSUPPORTED, "device query failed: %s", cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64) checked[dev] = major == 10 ? 1 : -1;
+    if (major != 10) return fail(KVQ_ERR_UNSUPPORTED, "device %d is sm_%d0, this library is built for sm_100a", dev, major);
+    return KVQ_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+bool bits_ok(uint32_t b) { return b == 2 || b == 3 || b == 4 || b == 6 || b == 8; }
+
+int check_format(uint32_t head_dim, uint32_t bits, uint32_t group, uint32_t dtype) {
+    if (head_dim != 64 && head_dim != 128)
+        return fail(KVQ_ERR_INVALID, "head_dim %u is not supported (64 or 128)", head_dim);
+    if (!bits_ok(bits)) return fail(KVQ_ERR_INVALID, "bits %u is not supported (2, 3, 4, 6 or 8)", bits);
+    if (group != 32 && group != 64 && group != 128)
+        return fail(KVQ_ERR_INVALID, "group_size %u is not supported (32, 64 or 128)", group);
+    if (head_dim % group)
+        return fail(KVQ_ERR_INVALID, "group_size %u does not divide head_dim %u", group, head_dim);
+    if (dtype != KVQ_F16 && dtype != KVQ_F32) return fail(KVQ_ERR_INVALID, "dtype %u is not KVQ_F16 or KVQ_F32", dtype);
+    return KVQ_OK;
+}
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t n) { return (n + kAlign - 1) / kAlign * kAlign; }
+
+// The number of resident CTAs the split plan aims to fill: 148 SMs x 4.
+constexpr uint64_t kTargetCtas = 148 * 4 * 2;
+constexpr uint32_t kMaxSplits = 4096;
+
+struct Plan {
+    kvq::Problem P;
+    int ht;
+    uint32_t rows;      // b_rows * n_heads
+    size_t part_bytes;  // one fp32 [n_splits, rows, DH] block
+    size_t ml_bytes;    // one fp32 [n_splits, rows] block
+};
+
+int plan(const kvq_args* a, Plan* pl) {
+    if (a == nullptr) return fail(KVQ_ERR_INVALID, "args is NULL");
+    int rc = check_format(a->head_dim, a->bits, a->group_size, a->dtype);
+    if (rc) return rc;
+    if (!a->q || !a->k_wq || !a->k_scales || !a->k_biases || !a->v_wq || !a->v_scales ||
+        !a->v_biases || (a->has_new_entry && (!a->new_k || !a->new_v)))
+        return fail(KVQ_ERR_INVALID, "a required tensor pointer is NULL");
+    if (a->b_rows == 0 || a->n_heads == 0 || a->n_kv_heads == 0)
+        return fail(KVQ_ERR_INVALID, "b_rows, n_heads and n_kv_heads must be positive");
+    if (a->n_heads % a->n_kv_heads)
+        return fail(KVQ_ERR_INVALID, "n_heads %u is not a multiple of n_kv_heads %u", a->n_heads, a->n_kv_heads);
+    if (a->b_rows > 65535) return fail(KVQ_ERR_INVALID, "b_rows %u above 65535", a->b_rows);
+    if (a->t_cached > a->t_stride)
+        return fail(KVQ_ERR_INVALID, "t_cached %u exceeds the physical row stride t_stride %u", a->t_cached, a->t_stride);
+    if (a->t_begin > a->t_end) return fail(KVQ_ERR_INVALID, "t_begin %u after t_end %u", a->t_begin, a->t_end);
+    const size_t esz = a->dtype == KVQ_F16 ? 2 : 4;
+    const void* ptrs[] = {a->q, a->k_scales, a->k_biases, a->v_scales, a->v_biases, a->new_k, a->new_v};
+    for (const void* p : ptrs)
+        if (p && !aligned(p, esz)) return fail(KVQ_ERR_INVALID, "a tensor pointer is not %zu-byte aligned", esz);
+    if (!aligned(a->k_wq, 4) || !aligned(a->v_wq, 4) || (a->seq_lens && !aligned(a->seq_lens, 4)))
+        return fail(KVQ_ERR_INVALID, "packed words and seq_lens must be 4-byte aligned");
+
+    kvq::Problem& P = pl->P;
+    P.q = a->q; P.k_wq = a->k_wq; P.k_scales = a->k_scales; P.k_biases = a->k_biases;
+    P.v_wq = a->v_wq; P.v_scales = a->v_scales; P.v_biases = a->v_biases;
+    P.new_k = a->new_k; P.new_v = a->new_v; P.seq_lens = a->seq_lens;
+    P.b_rows = a->b_rows; P.n_heads = a->n_heads; P.n_kv_heads = a->n_kv_heads;
+    P.t_cached = a->t_cached; P.t_stride = a->t_stride; P.group_size = a->group_size;
+    P.has_new_entry = a->has_new_entry ? 1u : 0u;
+    P.cache_batch_stride = a->cache_batch_stride;
+    P.t_begin = a->t_begin; P.t_end = a->t_end;
+    P.r = a->n_heads / a->n_kv_heads;
+    pl->ht = P.r == 1 ? 1 : (P.r <= 4 ? 4 : 8);
+    P.head_tiles = (P.r + pl->ht - 1) / pl->ht;
+    P.scale = 1.0f / sqrtf((float)a->head_dim);
+
+    const uint32_t end = a->t_end < a->t_cached ? a->t_end : a->t_cached;
+    const uint64_t span = end > a->t_begin ? end - a->t_begin : 0;
+    const uint64_t units = (uint64_t)a->b_rows * a->n_kv_heads * P.head_tiles;
+    uint64_t chunk = (span * units + kTargetCtas - 1) / kTargetCtas;
+    const uint64_t tile = kvq::P_TILE;
+    chunk = (chunk + tile - 1) / tile * tile;
+    if (chunk < tile) chunk = tile;
+    uint64_t splits = span ? (span + chunk - 1) / chunk : 1;
+    if (splits > kMaxSplits) {
+        chunk = ((span + kMaxSplits - 1) / kMaxSplits + tile - 1) / tile * tile;
+        splits = (span + chunk - 1) / chunk;
+    }
+    P.chunk = (uint32_t)chunk;
+    P.n_splits = (uint32_t)splits;
+    pl->rows = a->b_rows * a->n_heads;
+    pl->part_bytes = align_up((size_t)P.n_splits * pl->rows * a->head_dim * sizeof(float));
+    pl->ml_bytes = align_up((size_t)P.n_splits * pl->rows * sizeof(float));
+    return KVQ_OK;
+}
+
+cudaError_t launch_partial_any(const Plan& pl, uint32_t bits, uint32_t dtype, uint32_t dh,
+                               float* o, float* m, float* l, cudaStream_t s) {
+    switch (bits) {
+        case 2: return kvq::launch_partial<2>(pl.P, dtype, dh, pl.ht, o, m, l, s);
+        case 3: return kvq::launch_partial<3>(pl.P, dtype, dh, pl.ht, o, m, l, s);
+        case 4: return kvq::launch_partial<4>(pl.P, dtype, dh, pl.ht, o, m, l, s);
+        case 6: return kvq::launch_partial<6>(pl.P, dtype, dh, pl.ht, o, m, l, s);
+        case 8: return kvq::launch_partial<8>(pl.P, dtype, dh, pl.ht, o, m, l, s);
+    }
+    return cudaErrorInvalidValue;
+}
+
+int check_workspace(const void* ws, size_t have, size_t need) {
+    if (need == 0) return KVQ_OK;
+    if (ws == nullptr || have < need)
+        return fail(KVQ_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu this call needs", have, need);
+    if (!aligned(ws, kAlign)) return fail(KVQ_ERR_INVALID, "workspace is not 256-byte aligned");
+    return KVQ_OK;
+}
+
+}  // namespace
+
+namespace kvq {
+
+cudaError_t launch_merge(const float* part_o, const float* part_m, const float* part_l,
+                         uint32_t n_parts, uint32_t rows, uint32_t head_dim, int out_dtype,
+                         void* out, cudaStream_t stream) {
+    const unsigned blocks = (rows + 3) / 4;
+    if (out_dtype == KVQ_F16)
+        merge_kernel<__half, true><<<blocks, 128, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
+                                                               head_dim, static_cast<__half*>(out),
+                                                               nullptr, nullptr);
+    else
+        merge_kernel<float, true><<<blocks, 128, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
+                                                              head_dim, static_cast<float*>(out),
+                                                              nullptr, nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge_partial(const float* part_o, const float* part_m, const float* part_l,
+                                 uint32_t n_parts, uint32_t rows, uint32_t head_dim,
+                                 float* out_o, float* out_m, float* out_l, cudaStream_t stream) {
+    const unsigned blocks = (rows + 3) / 4;
+    merge_kernel<float, false><<<blocks, 128, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
+                                                           head_dim, out_o, out_m, out_l);
+    return cudaGetLastError();
+}
+
+}  // namespace kvq
+
+extern "C" {
+
+int kvq_abi_version(void) { return KVQ_ABI_VERSION; }
+
+const char* kvq_last_error(void) { return g_error.c_str(); }
+
+int kvq_supports(uint32_t head_dim, uint32_t bits, uint32_t group_size, uint32_t dtype) {
+    std::string keep = g_error;
+    const int ok = check_format(head_dim, bits, group_size, dtype) == KVQ_OK;
+    g_error = keep;
+    return ok;
+}
+
+size_t kvq_workspace_bytes(const kvq_args* a) {
+    Plan pl;
+    if (plan(a, &pl) != KVQ_OK) return 0;
+    return 2 * pl.ml_bytes + pl.part_bytes;
+}
+
+int kvq_decode(const kvq_args* a, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+    g_error.clear();
+    Plan pl;
+    int rc = plan(a, &pl);
+    if (rc) return rc;
+    if (!out) return fail(KVQ_ERR_INVALID, "out is NULL");
+    if (!aligned(out, a->dtype == KVQ_F16 ? 2 : 4)) return fail(KVQ_ERR_INVALID, "out is misaligned");
+    rc = check_workspace(workspace, workspace_bytes, 2 * pl.ml_bytes + pl.part_bytes);
+    if (rc) return rc;
+    rc = device_ok();
+    if (rc) return rc;
+    auto s = static_cast<cudaStream_t>(stream);
+    char* ws = static_cast<char*>(workspace);
+    float* po = reinterpret_cast<float*>(ws);
+    float* pm = reinterpret_cast<float*>(ws + pl.part_bytes);
+    float* pll = reinterpret_cast<float*>(ws + pl.part_bytes + pl.ml_bytes);
+    cudaError_t e = launch_partial_any(pl, a->bits, a->dtype, a->head_dim, po, pm, pll, s);
+    if (e != cudaSuccess) return cuda_fail(e, "partial kernel launch");
+    e = kvq::launch_merge(po, pm, pll, pl.P.n_splits, pl.rows, a->head_dim, (int)a->dtype, out, s);
+    if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
+    return KVQ_OK;
+}
+
+int kvq_decode_partial(const kvq_args* a, float* part_o, float* part_m, float* part_l,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+    g_error.clear();
+    Plan pl;
+    int rc = plan(a, &pl);
+    if (rc) return rc;
+    if (!part_o || !part_m || !part_l) return fail(KVQ_ERR_INVALID, "a partial output pointer is NULL");
+    if (!aligned(part_o, 4) || !aligned(part_m, 4) || !aligned(part_l, 4))
+        return fail(KVQ_ERR_INVALID, "partial outputs must be 4-byte aligned");
+    rc = device_ok();
+    if (rc) return rc;
+    auto s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (pl.P.n_splits == 1) {
+        e = launch_partial_any(pl, a->bits, a->dtype, a->head_dim, part_o, part_m, part_l, s);
+        if (e != cudaSuccess) return cuda_fail(e, "partial kernel launch");
+        return KVQ_OK;
+    }
+    rc = check_workspace(workspace, workspace_bytes, 2 * pl.ml_bytes + pl.part_bytes);
+    if (rc) return rc;
+    char* ws = static_cast<char*>(workspace);
+    float* po = reinterpret_cast<float*>(ws);
+    float* pm = reinterpret_cast<float*>(ws + pl.part_bytes);
+    float* pll = reinterpret_cast<float*>(ws + pl.part_bytes + pl.ml_bytes);
+    e = launch_partial_any(pl, a->bits, a->dtype, a->head_dim, po, pm, pll, s);
+    if (e != cudaSuccess) return cuda_fail(e, "partial kernel launch");
+    e = kvq::launch_merge_partial(po, pm, pll, pl.P.n_splits, pl.rows, a->head_dim, part_o, part_m,
+                                  part_l, s);
+    if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
+    return KVQ_OK;
+}
+
+uint32_t kvq_split_count(const kvq_args* a) {
+    std::string keep = g_error;
+    Plan pl;
+    const uint32_t n = plan(a, &pl) == KVQ_OK ? pl.P.n_splits : 0;
+    g_error = keep;
+    return n;
+}
+
+int kvq_decode_splits(const kvq_args* a, float* part_o, float* part_m, float* part_l, void* stream) {
+    g_error.clear();
+    Plan pl;
+    int rc = plan(a, &pl);
+    if (rc) return rc;
+    if (!part_o || !part_m || !part_l) return fail(KVQ_ERR_INVALID, "a partial output pointer is NULL");
+    if (!aligned(part_o, 4) || !aligned(part_m, 4) || !aligned(part_l, 4))
+        return fail(KVQ_ERR_INVALID, "partial outputs must be 4-byte aligned");
+    rc = device_ok();
+    if (rc) return rc;
+    cudaError_t e = launch_partial_any(pl, a->bits, a->dtype, a->head_dim, part_o, part_m, part_l,
+                                       static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "partial kernel launch");
+    return KVQ_OK;
+}
+
+int kvq_lse_merge(const float* part_o, const float* part_m, const float* part_l, uint32_t n_parts,
+                  uint32_t rows, uint32_t head_dim, uint32_t out_dtype, void* out, void* stream) {
+    g_error.clear();
+    if (!part_o || !part_m || !part_l || !out) return fail(KVQ_ERR_INVALID, "a pointer is NULL");
+    if (n_parts == 0 || rows == 0 || head_dim == 0) return fail(KVQ_ERR_INVALID, "empty merge");
+    if (out_dtype != KVQ_F16 && out_dtype != KVQ_F32) return fail(KVQ_ERR_INVALID, "bad out_dtype");
+    int rc = device_ok();
+    if (rc) return rc;
+    cudaError_t e = kvq::launch_merge(part_o, part_m, part_l, n_parts, rows, head_dim, (int)out_dtype,
+                                      out, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
+    return KVQ_OK;
+}
+
+int kvq_dequant(const uint32_t* wq, const void* scales, const void* biases, uint64_t rows,
+                uint32_t head_dim, uint32_t bits, uint32_t group_size, uint32_t dtype, float* out,
+                void* stream) {
+    g_error.clear();
+    int rc = check_format(head_dim, bits, group_size, dtype);
+    if (rc) return rc;
+    if (!wq || !scales || !biases || !out) return fail(KVQ_ERR_INVALID, "a pointer is NULL");
+    if (rows == 0) return KVQ_OK;
+    rc = device_ok();
+    if (rc) return rc;
+    auto s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaErrorInvalidValue;
+    switch (bits) {
+        case 2: e = kvq::launch_dequant<2>(wq, scales, biases, rows, head_dim, group_size, dtype, out, s); break;
+        case 3: e = kvq::launch_dequant<3>(wq, scales, biases, rows, head_dim, group_size, dtype, out, s); break;
+        case 4: e = kvq::launch_dequant<4>(wq, scales, biases, rows, head_dim, group_size, dtype, out, s); break;
+        case 6: e = kvq::launch_dequant<6>(wq, scales, biases, rows, head_dim, group_size, dtype, out, s); break;
+        case 8: e = kvq::launch_dequant<8>(wq, scales, biases, rows, head_dim, group_size, dtype, out, s); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "dequant kernel launch");
+    return KVQ_OK;
+}
+
+int kvq_quantize(const void* w, uint64_t rows, uint32_t head_dim, uint32_t bits, uint32_t group_size,
+                 uint32_t dtype, uint32_t* wq, void* scales, void* biases, void* stream) {
+    g_error.clear();
+    int rc = check_format(head_dim, bits, group_size, dtype);
+    if (rc) return rc;
+    if (!w || !wq || !scales || !biases) return fail(KVQ_ERR_INVALID, "a pointer is NULL");
+    if (rows == 0) return KVQ_OK;
+    rc = device_ok();
+    if (rc) return rc;
+    auto s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaErrorInvalidValue;
+    switch (bits) {
+        case 2: e = kvq::launch_quantize<2>(w, rows, head_dim, group_size, dtype, wq, scales, biases, s); break;
+        case 3: e = kvq::launch_quantize<3>(w, rows, head_dim, group_size, dtype, wq, scales, biases, s); break;
+        case 4: e = kvq::launch_quantize<4>(w, rows, head_dim, group_size, dtype, wq, scales, biases, s); break;
+        case 6: e = kvq::launch_quantize<6>(w, rows, head_dim, group_size, dtype, wq, scales, biases, s); break;
+        case 8: e = kvq::launch_quantize<8>(w, rows, head_dim, group_size, dtype, wq, scales, biases, s); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "quantize kernel launch");
+    return KVQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,37 @@
+// Internal launchers, one translation unit per code width (they compile in
+// parallel); the C ABI in kvq_abi.cu validates, plans and dispatches to them.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "kvq_common.cuh"
+
+namespace kvq {
+
+// Heads-per-CTA tiles carried by the library.
+constexpr int HEAD_TILES[] = {1, 4, 8};
+
+// Partial kernel over a planned Problem; returns the launch's cudaError_t.
+template <int BITS>
+cudaError_t launch_partial(const Problem& P, int dtype, int head_dim, int ht, float* part_o,
+                           float* part_m, float* part_l, cudaStream_t stream);
+
+template <int BITS>
+cudaError_t launch_quantize(const void* w, uint64_t rows, uint32_t head_dim, uint32_t group,
+                            int dtype, uint32_t* wq, void* scales, void* biases,
+                            cudaStream_t stream);
+
+template <int BITS>
+cudaError_t launch_dequant(const uint32_t* wq, const void* scales, const void* biases,
+                           uint64_t rows, uint32_t head_dim, uint32_t group, int dtype,
+                           float* out, cudaStream_t stream);
+
+cudaError_t launch_merge(const float* part_o, const float* part_m, const float* part_l,
+                         uint32_t n_parts, uint32_t rows, uint32_t head_dim, int out_dtype,
+                         void* out, cudaStream_t stream);
+
+cudaError_t launch_merge_partial(const float* part_o, const float* part_m, const float* part_l,
+                                 uint32_t n_parts, uint32_t rows, uint32_t head_dim,
+                                 float* out_o, float* out_m, float* out_l, cudaStream_t stream);
+
+}  // namespace kvq

@@ -1,0 +1,272 @@
+// Split-T partial kernel: one CTA per (T chunk, cache head x head tile, batch
+// row). It streams the chunk's packed K and V rows once for all HT query
+// heads that read this cache head (the GQA group), and leaves an unnormalised
+// partial (O, m, l) per query head for the log-sum-exp merge.
+//
+// Per tile of TILE positions (one per thread):
+//   scores   s[h,t] = (sum_d q[h,d] * (scale_g * code + bias_g)) / sqrt(DH)
+//   online softmax: m' = max(m, max_t s), alpha = e^(m - m'),
+//                   p = e^(s - m'), l' = alpha l + sum p
+//   combine  O[h,:] = alpha O[h,:] + sum_t p[h,t] * dequant(V_t)
+// and, in the last split, the step's own new entry (new_k / new_v at full
+// precision) as one more position. Every intermediate is fp32; the dequant is
+// a rounded multiply then a rounded add per element, the reference kernel's
+// arithmetic shape (kernelverify/pack/kv_attention.py:128-157,200-224).
+#pragma once
+
+#include "kvq_common.cuh"
+
+namespace kvq {
+
+constexpr int P_THREADS = 256;
+constexpr int P_WARPS = P_THREADS / 32;
+constexpr int P_TILE = P_THREADS;
+
+template <int HT, int DH>
+constexpr size_t partial_smem_bytes() {
+    // q[HT][DH] + p[HT][TILE] + red[HT][WARPS] + obuf[WARPS][HT][DH]
+    return sizeof(float) * (HT * DH + HT * P_TILE + HT * P_WARPS + P_WARPS * HT * DH);
+}
+
+template <typename T, int BITS, int DH, int HT>
+__global__ void __launch_bounds__(P_THREADS)
+partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m,
+               float* __restrict__ part_l) {
+    constexpr int W = DH * BITS / 32;           // words per row
+    constexpr int CC = Chunk<BITS>::CODES;
+    constexpr int CW = Chunk<BITS>::WORDS;
+    constexpr int L = DH / 32;                  // dims per lane in the combine
+
+    extern __shared__ __align__(16) float smem[];
+    float* qs = smem;                                   // [HT][DH]
+    float* ps = qs + HT * DH;                           // [HT][TILE]
+    float* red = ps + HT * P_TILE;                      // [HT][WARPS]
+    float* obuf = red + HT * P_WARPS;                   // [WARPS][HT][DH]
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t split = blockIdx.x;
+    const uint32_t hk = blockIdx.y / P.head_tiles;
+    const uint32_t tile_h = blockIdx.y % P.head_tiles;
+    const uint32_t b = blockIdx.z;
+    const uint32_t h0 = hk * P.r + tile_h * HT;
+    const int nh = min(HT, (int)(P.r - tile_h * HT));
+    const uint32_t H = P.n_heads;
+    const uint32_t G = DH / P.group_size;
+
+    const T* q = static_cast<const T*>(P.q);
+    for (int i = tid; i < HT * DH; i += P_THREADS) {
+        const int h = i / DH, d = i % DH;
+        qs[i] = h < nh ? to_f32(q[((size_t)b * H + h0 + h) * DH + d]) : 0.0f;
+    }
+
+    uint32_t len = P.t_cached;
+    if (P.seq_lens != nullptr) len = min((uint32_t)max(P.seq_lens[b], 0), P.t_cached);
+    const uint32_t end = min(P.t_end, len);
+    const uint32_t lo = P.t_begin + split * P.chunk;
+    const uint32_t hi = min(end, lo + P.chunk);
+    const bool with_new = P.has_new_entry && split == P.n_splits - 1;
+
+    const uint64_t rowbase = (uint64_t)b * P.cache_batch_stride + (uint64_t)hk * P.t_stride;
+    const T* ks = static_cast<const T*>(P.k_scales);
+    const T* kb = static_cast<const T*>(P.k_biases);
+    const T* vs = static_cast<const T*>(P.v_scales);
+    const T* vb = static_cast<const T*>(P.v_biases);
+
+    float m_run[HT], l_run[HT], acc[HT][L];
+#pragma unroll
+    for (int h = 0; h < HT; ++h) {
+        m_run[h] = -INFINITY;
+        l_run[h] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < L; ++j) acc[h][j] = 0.0f;
+    }
+    __syncthreads();
+
+    for (uint32_t t0 = lo; t0 < hi; t0 += P_TILE) {
+        // ---- scores: one thread per position ---------------------------------
+        const uint32_t t = t0 + tid;
+        const bool valid = t < hi;
+        float s[HT];
+#pragma unroll
+        for (int h = 0; h < HT; ++h) s[h] = 0.0f;
+        if (valid) {
+            const uint64_t row = rowbase + t;
+            const uint32_t* kw = P.k_wq + row * W;
+#pragma unroll 1
+            for (int c = 0; c < DH / CC; ++c) {
+                uint32_t w[CW];
+#pragma unroll
+                for (int i = 0; i < CW; ++i) w[i] = __ldg(kw + c * CW + i);
+                const int d0 = c * CC;
+                const int g = d0 / (int)P.group_size;
+                const float sg = to_f32(ks[row * G + g]);
+                const float bg = to_f32(kb[row * G + g]);
+                float v[CC];
+                static_for<CC>([&](auto J) {
+                    v[J.value] = dequant(sg, chunk_code<BITS, J.value>(w), bg);
+                });
+#pragma unroll
+                for (int h = 0; h < HT; ++h) {
+#pragma unroll
+                    for (int j = 0; j < CC; ++j) s[h] = fmaf(qs[h * DH + d0 + j], v[j], s[h]);
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < HT; ++h) s[h] = s[h] * P.scale;
+        } else {
+#pragma unroll
+            for (int h = 0; h < HT; ++h) s[h] = -INFINITY;
+        }
+
+        // ---- tile max, online rescale ----------------------------------------
+#pragma unroll
+        for (int h = 0; h < HT; ++h) {
+            const float mx = warp_max(s[h]);
+            if (lane == 0) red[h * P_WARPS + warp] = mx;
+        }
+        __syncthreads();
+        float m_new[HT], alpha[HT];
+#pragma unroll
+        for (int h = 0; h < HT; ++h) {
+            float mx = red[h * P_WARPS];
+#pragma unroll
+            for (int i = 1; i < P_WARPS; ++i) mx = fmaxf(mx, red[h * P_WARPS + i]);
+            m_new[h] = fmaxf(m_run[h], mx);
+            alpha[h] = m_run[h] == -INFINITY ? 0.0f : expf(m_run[h] - m_new[h]);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int h = 0; h < HT; ++h) {
+            const float p = valid ? expf(s[h] - m_new[h]) : 0.0f;
+            ps[h * P_TILE + tid] = p;
+            const float sum = warp_sum(p);
+            if (lane == 0) red[h * P_WARPS + warp] = sum;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int h = 0; h < HT; ++h) {
+            float sum = 0.0f;
+#pragma unroll
+            for (int i = 0; i < P_WARPS; ++i) sum += red[h * P_WARPS + i];
+            l_run[h] = l_run[h] * alpha[h] + sum;
+            m_run[h] = m_new[h];
+#pragma unroll
+            for (int j = 0; j < L; ++j) acc[h][j] *= alpha[h];
+        }
+
+        // ---- combine: warp w takes positions w, w+WARPS, ...; lane owns L dims
+        const int dl = lane * L;
+        const int g = dl / (int)P.group_size;
+        const int n_here = (int)min((uint32_t)P_TILE, hi - t0);
+#pragma unroll 1
+        for (int i = warp; i < n_here; i += P_WARPS) {
+            const uint64_t row = rowbase + t0 + i;
+            const uint32_t* vw = P.v_wq + row * W;
+            const float sg = to_f32(vs[row * G + g]);
+            const float bg = to_f32(vb[row * G + g]);
+            float v[L];
+#pragma unroll
+            for (int j = 0; j < L; ++j) v[j] = dequant(sg, row_code<BITS>(vw, dl + j), bg);
+#pragma unroll
+            for (int h = 0; h < HT; ++h) {
+                const float p = ps[h * P_TILE + i];
+#pragma unroll
+                for (int j = 0; j < L; ++j) acc[h][j] = fmaf(p, v[j], acc[h][j]);
+            }
+        }
+        __syncthreads();
+    }
+
+    // ---- the step's own entry: new_k / new_v at full precision ---------------
+    if (with_new) {
+        const T* nk = static_cast<const T*>(P.new_k) + ((size_t)b * P.n_kv_heads + hk) * DH;
+        const T* nv = static_cast<const T*>(P.new_v) + ((size_t)b * P.n_kv_heads + hk) * DH;
+        const int dl = lane * L;
+#pragma unroll
+        for (int h = 0; h < HT; ++h) {
+            float part = 0.0f;
+#pragma unroll
+            for (int j = 0; j < L; ++j) part = fmaf(qs[h * DH + dl + j], to_f32(nk[dl + j]), part);
+            const float s_new = warp_sum(part) * P.scale;
+            const float m_new = fmaxf(m_run[h], s_new);
+            const float alpha = m_run[h] == -INFINITY ? 0.0f : expf(m_run[h] - m_new);
+            const float p_new = expf(s_new - m_new);
+            l_run[h] = l_run[h] * alpha + p_new;
+            m_run[h] = m_new;
+#pragma unroll
+            for (int j = 0; j < L; ++j) {
+                acc[h][j] *= alpha;
+                if (warp == 0) acc[h][j] = fmaf(p_new, to_f32(nv[dl + j]), acc[h][j]);
+            }
+        }
+    }
+
+    // ---- cross-warp reduction and the partial's write ------------------------
+#pragma unroll
+    for (int h = 0; h < HT; ++h) {
+#pragma unroll
+        for (int j = 0; j < L; ++j) obuf[(warp * HT + h) * DH + lane * L + j] = acc[h][j];
+    }
+    __syncthreads();
+    const size_t rows = (size_t)P.b_rows * H;
+    for (int i = tid; i < nh * DH; i += P_THREADS) {
+        const int h = i / DH, d = i % DH;
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < P_WARPS; ++w) o += obuf[(w * HT + h) * DH + d];
+        part_o[((size_t)split * rows + (size_t)b * H + h0 + h) * DH + d] = o;
+    }
+    if (tid < nh) {
+        float mv = 0.0f, lv = 0.0f;
+#pragma unroll
+        for (int h = 0; h < HT; ++h) {
+            if (h == tid) { mv = m_run[h]; lv = l_run[h]; }
+        }
+        part_m[(size_t)split * rows + (size_t)b * H + h0 + tid] = mv;
+        part_l[(size_t)split * rows + (size_t)b * H + h0 + tid] = lv;
+    }
+}
+
+// Log-sum-exp merge of n_parts partials per row; one warp per row.
+// NORMALIZE: out = sum_p O_p e^(m_p - m) / l in TO. Otherwise the merged
+// partial (O unnormalised, m, l) in fp32.
+template <typename TO, bool NORMALIZE>
+__global__ void __launch_bounds__(128)
+merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
+             const float* __restrict__ part_l, uint32_t n_parts, uint32_t rows,
+             uint32_t head_dim, TO* __restrict__ out, float* __restrict__ out_m,
+             float* __restrict__ out_l) {
+    const uint32_t row = blockIdx.x * 4 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float m = -INFINITY;
+    for (uint32_t p = lane; p < n_parts; p += 32) m = fmaxf(m, part_m[(size_t)p * rows + row]);
+    m = warp_max(m);
+    float l = 0.0f;
+    for (uint32_t p = lane; p < n_parts; p += 32) {
+        const float mp = part_m[(size_t)p * rows + row];
+        if (mp != -INFINITY) l += part_l[(size_t)p * rows + row] * expf(mp - m);
+    }
+    l = warp_sum(l);
+    for (uint32_t d = lane; d < head_dim; d += 32) {
+        float o = 0.0f;
+        for (uint32_t p = 0; p < n_parts; ++p) {
+            const float mp = part_m[(size_t)p * rows + row];
+            if (mp == -INFINITY) continue;
+            o = fmaf(part_o[((size_t)p * rows + row) * head_dim + d], expf(mp - m), o);
+        }
+        if constexpr (NORMALIZE) {
+            out[(size_t)row * head_dim + d] = from_f32<TO>(o / l);
+        } else {
+            out[(size_t)row * head_dim + d] = m == -INFINITY ? 0.0f : o;
+        }
+    }
+    if constexpr (!NORMALIZE) {
+        if (lane == 0) {
+            out_m[row] = m;
+            out_l[row] = l;
+        }
+    }
+}
+
+}  // namespace kvq

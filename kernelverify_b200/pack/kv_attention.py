@@ -1,0 +1,364 @@
+"""CUDA build of kernelverify's quantized-KV attention decode pack.
+
+Mirrors the reference pack module (kernelverify/pack/kv_attention.py) name
+for name, with the Metal kernel replaced by the sm_100a library behind the C
+ABI of include/kvq_b200.h:
+
+* `build(torch)`    -- the framework door (the reference's `build(mx)`,
+  kernelverify/pack/kv_attention.py:369-393): a callable taking the nine
+  tensor inputs in the reference's order plus the LOGICAL cached length.
+* `kernel_spec()`   -- the runner door (kernelverify/pack/kv_attention.py:
+  292-352) for `kernelverify_b200.runners.CudaRunner`.
+* `quantize_cache`  -- packed artefact triplet of an (H, T, DH) cache, computed
+  on the device by the library's bit-exact canonical quantizer
+  (kernelverify/pack/kv_attention.py:270-283).
+* `require_capacity`, `should_dispatch`, `launch_config`, `SUPPORTED_BITS`,
+  `SUPPORTED_DH`, `KERNEL_NAME`, `INPUT_NAMES`, `OUTPUT_NAMES`.
+
+Differences from the Metal kernel, all extensions:
+* no capacity bound: T is split into chunks with a log-sum-exp merge, so the
+  reference's TCAP = 1024 (kernelverify/pack/kv_attention.py:53-65) is gone;
+  `require_capacity` keeps only the physical bound (the logical length must
+  fit the buffer it indexes);
+* bits 6 and groups 32/128 besides the reference's {2,3,4,8} x 64;
+* per-sequence caches ([B, HKV, T_stride, ...]) and ragged lengths besides the
+  reference's cache shared by all batch rows;
+* T-range shards (`decode_partial`) for sequence-split multi-GPU decode.
+"""
+
+from __future__ import annotations
+
+from kernelverify_b200 import _native
+from kernelverify_b200._native import KVQ_F16, KVQ_F32, KVQ_T_END_ALL, KvqArgs
+
+KERNEL_NAME = "kv_attn_decode"
+SUPPORTED_BITS = (2, 3, 4, 6, 8)
+SUPPORTED_DH = (64, 128)
+SUPPORTED_GROUPS = (32, 64, 128)
+INPUT_NAMES = ["q", "k_wq", "k_scales", "k_biases",
+               "v_wq", "v_scales", "v_biases", "new_k", "new_v", "t_cached"]
+OUTPUT_NAMES = ["out"]
+THREADS_PER_CTA = 256
+MAX_T = 0xFFFFFFFE  # positions are uint32 in the ABI
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _dtype_code(dt) -> int:
+    torch = _torch()
+    if dt == torch.float16:
+        return KVQ_F16
+    if dt == torch.float32:
+        return KVQ_F32
+    raise ValueError(f"kv_attention: dtype {dt} is not float16 or float32")
+
+
+def require_capacity(t: int, t_stride: int | None = None) -> None:
+    """Reject a logical length the call cannot serve, loudly.
+
+    There is no compile-time capacity here (the reference's TCAP check,
+    kernelverify/pack/kv_attention.py:242-256, guarded a threadgroup buffer
+    this kernel does not have). What remains is the physical bound: the
+    logical length indexes the cache buffer, so it may not exceed its rows."""
+    if t < 0 or t > MAX_T:
+        raise ValueError(f"t={t} is outside the supported range [0, {MAX_T}]")
+    if t_stride is not None and t > t_stride:
+        raise ValueError(f"t_cached={t} exceeds the cache buffer's {t_stride} rows per head")
+
+
+def should_dispatch(t: int) -> bool:
+    """Every length is served (kernelverify/pack/kv_attention.py:259-267 deferred
+    T > 1024 to MLX; nothing is deferred here)."""
+    return 0 <= t <= MAX_T
+
+
+def launch_config(b: int, h: int, n_kv_heads: int | None = None, t: int = 0):
+    """(grid, block) of the partial kernel for B=b, H=h at length t, as the
+    library plans it: grid (T splits, cache heads x head tiles, b), 256
+    threads. Informational -- the library plans its own launch."""
+    hkv = n_kv_heads or h
+    r = h // hkv
+    ht = 1 if r == 1 else (4 if r <= 4 else 8)
+    tiles = -(-r // ht)
+    units = b * hkv * tiles
+    chunk = -(-t * units // (148 * 4 * 2))          # ceil: fill ~2 waves of 4 CTAs/SM
+    chunk = max(THREADS_PER_CTA, -(-chunk // THREADS_PER_CTA) * THREADS_PER_CTA)
+    splits = max(1, -(-t // chunk)) if t else 1
+    return (splits, hkv * tiles, b), (THREADS_PER_CTA, 1, 1)
+
+
+def _args(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *, bits,
+          t_cached=None, seq_lens=None, t_begin=0, t_end=None, has_new_entry=True) -> KvqArgs:
+    """Validate shapes and build the C argument block."""
+    if q.dim() != 3:
+        raise ValueError(f"q must be [B, H, DH], got {tuple(q.shape)}")
+    b, h, dh = q.shape
+    if k_wq.dim() == 3:
+        per_seq, (hkv, t_stride, words) = False, k_wq.shape
+    elif k_wq.dim() == 4:
+        per_seq = True
+        bk, hkv, t_stride, words = k_wq.shape
+        if bk != b:
+            raise ValueError(f"per-sequence cache has {bk} rows, q has {b}")
+    else:
+        raise ValueError(f"k_wq must be [HKV, T, W] or [B, HKV, T, W], got {tuple(k_wq.shape)}")
+    if dh not in SUPPORTED_DH:
+        raise ValueError(f"head_dim {dh} not in {SUPPORTED_DH}")
+    if bits not in SUPPORTED_BITS:
+        raise ValueError(f"bits {bits} not in {SUPPORTED_BITS}")
+    if words * 32 != dh * bits:
+        raise ValueError(f"k_wq rows hold {words} words; {dh} codes of {bits} bits need {dh * bits // 32}")
+    groups = k_scales.shape[-1]
+    if groups == 0 or dh % groups:
+        raise ValueError(f"scales carry {groups} groups per row, which does not divide {dh}")
+    group = dh // groups
+    if h % hkv:
+        raise ValueError(f"{h} query heads do not divide into {hkv} cache heads")
+    for name, ten, shape in (("k_wq", k_wq, tuple(k_wq.shape)), ("v_wq", v_wq, tuple(k_wq.shape)),
+                             ("k_scales", k_scales, tuple(k_wq.shape[:-1]) + (groups,)),
+                             ("k_biases", k_biases, tuple(k_wq.shape[:-1]) + (groups,)),
+                             ("v_scales", v_scales, tuple(k_wq.shape[:-1]) + (groups,)),
+                             ("v_biases", v_biases, tuple(k_wq.shape[:-1]) + (groups,)),
+                             ("new_k", new_k, (b, hkv, dh)), ("new_v", new_v, (b, hkv, dh))):
+        if tuple(ten.shape) != shape:
+            raise ValueError(f"{name} has shape {tuple(ten.shape)}, expected {shape}")
+        if not ten.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+        if not ten.is_cuda or ten.device != q.device:
+            raise ValueError(f"{name} must be a CUDA tensor on {q.device}")
+    torch = _torch()
+    code = _dtype_code(q.dtype)
+    for name, ten in (("new_k", new_k), ("new_v", new_v), ("k_scales", k_scales),
+                      ("k_biases", k_biases), ("v_scales", v_scales), ("v_biases", v_biases)):
+        if ten.dtype != q.dtype:
+            raise ValueError(f"{name} is {ten.dtype}; every float input must be {q.dtype}")
+    if k_wq.dtype not in (torch.int32, torch.uint32) or v_wq.dtype != k_wq.dtype:
+        raise ValueError("packed words must be int32/uint32 tensors")
+    if not q.is_contiguous():
+        raise ValueError("q must be contiguous")
+    if t_cached is None:
+        t_cached = t_stride
+    require_capacity(int(t_cached), t_stride)
+    if seq_lens is not None:
+        if seq_lens.dtype != torch.int32 or tuple(seq_lens.shape) != (b,) or not seq_lens.is_cuda:
+            raise ValueError("seq_lens must be a CUDA int32 tensor [B]")
+    a = KvqArgs()
+    a.q, a.k_wq, a.k_scales, a.k_biases = (q.data_ptr(), k_wq.data_ptr(), k_scales.data_ptr(),
+                                           k_biases.data_ptr())
+    a.v_wq, a.v_scales, a.v_biases = v_wq.data_ptr(), v_scales.data_ptr(), v_biases.data_ptr()
+    a.new_k, a.new_v = new_k.data_ptr(), new_v.data_ptr()
+    a.seq_lens = seq_lens.data_ptr() if seq_lens is not None else None
+    a.b_rows, a.n_heads, a.n_kv_heads = b, h, hkv
+    a.t_cached, a.t_stride, a.head_dim = int(t_cached), t_stride, dh
+    a.bits, a.group_size, a.dtype = bits, group, code
+    a.has_new_entry = 1 if has_new_entry else 0
+    a.cache_batch_stride = hkv * t_stride if per_seq else 0
+    a.t_begin = int(t_begin)
+    a.t_end = KVQ_T_END_ALL if t_end is None else int(t_end)
+    return a
+
+
+class Workspace:
+    """A reusable, growing scratch buffer on one device (the library never
+    allocates; this is the caller-side allocation it asks for)."""
+
+    def __init__(self):
+        self._buf = None
+
+    def get(self, nbytes: int, device):
+        torch = _torch()
+        if nbytes == 0:
+            return None, 0
+        if self._buf is None or self._buf.numel() < nbytes or self._buf.device != device:
+            self._buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        return self._buf, self._buf.numel()
+
+
+_default_ws: dict = {}
+
+
+def _workspace(device, nbytes, ws: Workspace | None):
+    if ws is None:
+        ws = _default_ws.setdefault((device.type, device.index), Workspace())
+    return ws.get(nbytes, device)
+
+
+def decode(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *, bits,
+           t_cached=None, seq_lens=None, out=None, workspace: Workspace | None = None,
+           stream=None):
+    """One decode step on the current CUDA stream: out [B, H, DH] in q's dtype.
+
+    Caches are [HKV, T_stride, ...] (shared by every batch row, the reference
+    layout) or [B, HKV, T_stride, ...] (one per sequence); `t_cached` is the
+    logical length (default: all rows), `seq_lens` an optional int32 [B]
+    tensor of ragged lengths (then `t_cached` bounds them)."""
+    torch = _torch()
+    a = _args(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, bits=bits,
+              t_cached=t_cached, seq_lens=seq_lens)
+    lib = _native.lib()
+    if out is None:
+        out = torch.empty_like(q)
+    elif tuple(out.shape) != tuple(q.shape) or out.dtype != q.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous tensor shaped and typed like q")
+    need = lib.kvq_workspace_bytes(a)
+    buf, have = _workspace(q.device, need, workspace)
+    s = stream if stream is not None else torch.cuda.current_stream(q.device)
+    _native.check(lib.kvq_decode(a, out.data_ptr(), buf.data_ptr() if buf is not None else None,
+                                 have, s.cuda_stream))
+    return out
+
+
+def decode_partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
+                   bits, t_begin, t_end, has_new_entry, t_cached=None, seq_lens=None,
+                   part_o=None, part_m=None, part_l=None, workspace: Workspace | None = None,
+                   stream=None):
+    """One T-range shard: (O [B,H,DH] fp32 unnormalised, m [B,H], l [B,H])."""
+    torch = _torch()
+    a = _args(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, bits=bits,
+              t_cached=t_cached, seq_lens=seq_lens, t_begin=t_begin, t_end=t_end,
+              has_new_entry=has_new_entry)
+    lib = _native.lib()
+    b, h, dh = q.shape
+    if part_o is None:
+        part_o = torch.empty((b, h, dh), dtype=torch.float32, device=q.device)
+    if part_m is None:
+        part_m = torch.empty((b, h), dtype=torch.float32, device=q.device)
+    if part_l is None:
+        part_l = torch.empty((b, h), dtype=torch.float32, device=q.device)
+    need = lib.kvq_workspace_bytes(a)
+    buf, have = _workspace(q.device, need, workspace)
+    s = stream if stream is not None else torch.cuda.current_stream(q.device)
+    _native.check(lib.kvq_decode_partial(a, part_o.data_ptr(), part_m.data_ptr(),
+                                         part_l.data_ptr(),
+                                         buf.data_ptr() if buf is not None else None, have,
+                                         s.cuda_stream))
+    return part_o, part_m, part_l
+
+
+def lse_merge(part_o, part_m, part_l, out_dtype, out=None, stream=None):
+    """Merge stacked partials part_o [P, B, H, DH], part_m/part_l [P, B, H]
+    into out [B, H, DH] (the sequence-split merge)."""
+    torch = _torch()
+    n, b, h, dh = part_o.shape
+    if out is None:
+        out = torch.empty((b, h, dh), dtype=out_dtype, device=part_o.device)
+    s = stream if stream is not None else torch.cuda.current_stream(part_o.device)
+    lib = _native.lib()
+    _native.check(lib.kvq_lse_merge(part_o.data_ptr(), part_m.data_ptr(), part_l.data_ptr(), n,
+                                    b * h, dh, _dtype_code(out_dtype), out.data_ptr(),
+                                    s.cuda_stream))
+    return out
+
+
+def quantize(w, bits: int, group_size: int = 64, stream=None):
+    """Canonical quantizer on the device: w [..., DH] (fp16/fp32, contiguous)
+    -> (words uint32-as-int32 [..., DH*bits/32], scales [..., DH/g], biases)."""
+    torch = _torch()
+    if not w.is_cuda or not w.is_contiguous():
+        raise ValueError("w must be a contiguous CUDA tensor")
+    dh = w.shape[-1]
+    rows = w.numel() // dh if dh else 0
+    lead = tuple(w.shape[:-1])
+    words = torch.empty(lead + (dh * bits // 32,), dtype=torch.int32, device=w.device)
+    scales = torch.empty(lead + (dh // group_size,), dtype=w.dtype, device=w.device)
+    biases = torch.empty_like(scales)
+    s = stream if stream is not None else torch.cuda.current_stream(w.device)
+    _native.check(_native.lib().kvq_quantize(w.data_ptr(), rows, dh, bits, group_size,
+                                             _dtype_code(w.dtype), words.data_ptr(),
+                                             scales.data_ptr(), biases.data_ptr(),
+                                             s.cuda_stream))
+    return words, scales, biases
+
+
+def quantize_cache(cache, bits: int, group_size: int = 64):
+    """Packed artefact triplet for an (H, T, DH) -- or (B, H, T, DH) -- cache,
+    quantized row by row on the device (kernelverify/pack/kv_attention.py:270-283)."""
+    return quantize(cache.contiguous(), bits, group_size)
+
+
+def dequant(words, scales, biases, bits: int, stream=None):
+    """fp32 dequantized values of a packed artefact, same leading shape."""
+    torch = _torch()
+    groups = scales.shape[-1]
+    dh = words.shape[-1] * 32 // bits
+    rows = words.numel() // words.shape[-1]
+    out = torch.empty(tuple(words.shape[:-1]) + (dh,), dtype=torch.float32, device=words.device)
+    s = stream if stream is not None else torch.cuda.current_stream(words.device)
+    _native.check(_native.lib().kvq_dequant(words.data_ptr(), scales.data_ptr(),
+                                            biases.data_ptr(), rows, dh, bits, dh // groups,
+                                            _dtype_code(scales.dtype), out.data_ptr(),
+                                            s.cuda_stream))
+    return out
+
+
+def build(torch_module=None):
+    """The framework door: a callable in the reference's MLX-door spelling
+    (kernelverify/pack/kv_attention.py:369-393).
+
+        kernel = build(torch)
+        [out] = kernel(inputs=[q, k_wq, k_scales, k_biases, v_wq, v_scales,
+                               v_biases, new_k, new_v],
+                       t_cached=t, template=[("T", torch.float16),
+                                             ("BITS", bits), ("DH", dh)])
+
+    Padded caches are passed whole with the logical length as a scalar;
+    `output_shapes`/`output_dtypes`, when given, are checked against what the
+    step produces; `grid`/`threadgroup` are accepted and ignored (the library
+    plans its own launch)."""
+    def guarded(*, inputs, t_cached, template=(), output_shapes=None, output_dtypes=None,
+                grid=None, threadgroup=None, seq_lens=None):
+        tmpl = dict(template)
+        q = inputs[0]
+        bits = int(tmpl.get("BITS", 0)) or None
+        if bits is None:
+            raise ValueError("template must carry BITS")
+        if "DH" in tmpl and int(tmpl["DH"]) != q.shape[-1]:
+            raise ValueError(f"template DH={tmpl['DH']} but q has head_dim {q.shape[-1]}")
+        if "T" in tmpl and tmpl["T"] != q.dtype:
+            raise ValueError(f"template T={tmpl['T']} but q is {q.dtype}")
+        if output_shapes is not None and [tuple(s) for s in output_shapes] != [tuple(q.shape)]:
+            raise ValueError(f"output_shapes {output_shapes} != [{tuple(q.shape)}]")
+        if output_dtypes is not None and list(output_dtypes) != [q.dtype]:
+            raise ValueError(f"output_dtypes {output_dtypes} != [{q.dtype}]")
+        return [decode(*inputs, bits=bits, t_cached=t_cached, seq_lens=seq_lens)]
+
+    return guarded
+
+
+def kernel_spec():
+    """The runner-door template (kernelverify/pack/kv_attention.py:292-352),
+    for `kernelverify_b200.runners.CudaRunner`. `specialize()` fills `$T`,
+    `$BITS`, `$DH` (and optionally `$GROUP`); the source names the library
+    entry point and the instantiation it selects, the bindings keep the
+    reference's names and order."""
+    from kernelverify_b200.runners import Binding, BindingKind, KernelSpec, LaunchSpec
+
+    source = (
+        "// kvq-b200 library translation unit: libkvq_b200.so, entry kvq_decode\n"
+        "#pragma kvq library kvq_decode\n"
+        "#pragma kvq instantiate T=$T BITS=$BITS DH=$DH\n"
+    )
+    return KernelSpec(
+        source=source,
+        entry_point=KERNEL_NAME,
+        name=f"{KERNEL_NAME}-$BITS bit-DH$DH-$T",
+        bindings=(Binding(BindingKind.INPUT, "q"),
+                  Binding(BindingKind.INPUT, "k_wq"),
+                  Binding(BindingKind.INPUT, "k_scales"),
+                  Binding(BindingKind.INPUT, "k_biases"),
+                  Binding(BindingKind.INPUT, "v_wq"),
+                  Binding(BindingKind.INPUT, "v_scales"),
+                  Binding(BindingKind.INPUT, "v_biases"),
+                  Binding(BindingKind.INPUT, "new_k"),
+                  Binding(BindingKind.INPUT, "new_v"),
+                  Binding(BindingKind.OUTPUT),
+                  Binding(BindingKind.SCALAR, "n_heads", "uint32"),
+                  Binding(BindingKind.SCALAR, "t_cached", "uint32"),
+                  Binding(BindingKind.SCALAR, "n_kv_heads", "uint32"),
+                  Binding(BindingKind.SCALAR, "t_stride", "uint32")),
+        launch=LaunchSpec(grid=(THREADS_PER_CTA, 1, ["b_rows", "n_heads"]),
+                          threadgroup=(THREADS_PER_CTA, 1, 1)),
+    )
