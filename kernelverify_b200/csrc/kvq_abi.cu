@@ -6,6 +6,8 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "kvq_b200.h"
@@ -70,8 +72,17 @@ size_t align_up(size_t n) { return (n + kAlign - 1) / kAlign * kAlign; }
 constexpr uint64_t kTargetCtas = 148 * 4 * 2;
 constexpr uint32_t kMaxSplits = 4096;
 
+enum KernelKind { KERNEL_GENERIC = 0, KERNEL_MMA4 = 1 };
+
+// KVQ_KERNEL=generic forces the CUDA-core kernel (A/B checks of the paths).
+bool generic_forced() {
+    const char* v = getenv("KVQ_KERNEL");
+    return v != nullptr && strcmp(v, "generic") == 0;
+}
+
 struct Plan {
     kvq::Problem P;
+    int kernel;
     int ht;
     uint32_t rows;      // b_rows * n_heads
     size_t part_bytes;  // one fp32 [n_splits, rows, DH] block
@@ -110,7 +121,22 @@ int plan(const kvq_args* a, Plan* pl) {
     P.cache_batch_stride = a->cache_batch_stride;
     P.t_begin = a->t_begin; P.t_end = a->t_end;
     P.r = a->n_heads / a->n_kv_heads;
-    pl->ht = P.r == 1 ? 1 : (P.r <= 4 ? 4 : 8);
+    // The tensor-core kernel streams 16-byte-aligned runs of 8 rows with TMA:
+    // it needs the fp16 / 4-bit / DH 128 format, at most 8 query heads per
+    // cache head, and 8-row-aligned geometry; everything else runs on the
+    // CUDA-core kernel.
+    const bool tma_ok = aligned(a->k_wq, 16) && aligned(a->v_wq, 16) && aligned(a->k_scales, 16) &&
+                        aligned(a->k_biases, 16) && aligned(a->v_scales, 16) &&
+                        aligned(a->v_biases, 16) && a->t_stride % 8 == 0 &&
+                        a->cache_batch_stride % 8 == 0 && a->t_begin % 8 == 0;
+    pl->kernel = (!generic_forced() && a->dtype == KVQ_F16 && a->bits == 4 && a->head_dim == 128 &&
+                  P.r <= 8 && tma_ok)
+                     ? KERNEL_MMA4
+                     : KERNEL_GENERIC;
+    if (pl->kernel == KERNEL_MMA4)
+        pl->ht = P.r <= 4 ? 4 : 8;
+    else
+        pl->ht = P.r == 1 ? 1 : (P.r <= 4 ? 4 : 8);
     P.head_tiles = (P.r + pl->ht - 1) / pl->ht;
     P.scale = 1.0f / sqrtf((float)a->head_dim);
 
@@ -136,6 +162,7 @@ int plan(const kvq_args* a, Plan* pl) {
 
 cudaError_t launch_partial_any(const Plan& pl, uint32_t bits, uint32_t dtype, uint32_t dh,
                                float* o, float* m, float* l, cudaStream_t s) {
+    if (pl.kernel == KERNEL_MMA4) return kvq::launch_mma4(pl.P, pl.ht, pl.P.group_size, o, m, l, s);
     switch (bits) {
         case 2: return kvq::launch_partial<2>(pl.P, dtype, dh, pl.ht, o, m, l, s);
         case 3: return kvq::launch_partial<3>(pl.P, dtype, dh, pl.ht, o, m, l, s);
@@ -161,13 +188,13 @@ namespace kvq {
 cudaError_t launch_merge(const float* part_o, const float* part_m, const float* part_l,
                          uint32_t n_parts, uint32_t rows, uint32_t head_dim, int out_dtype,
                          void* out, cudaStream_t stream) {
-    const unsigned blocks = (rows + 3) / 4;
+    const unsigned blocks = rows;
     if (out_dtype == KVQ_F16)
-        merge_kernel<__half, true><<<blocks, 128, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
+        merge_kernel<__half, true><<<blocks, head_dim, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
                                                                head_dim, static_cast<__half*>(out),
                                                                nullptr, nullptr);
     else
-        merge_kernel<float, true><<<blocks, 128, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
+        merge_kernel<float, true><<<blocks, head_dim, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
                                                               head_dim, static_cast<float*>(out),
                                                               nullptr, nullptr);
     return cudaGetLastError();
@@ -176,8 +203,8 @@ cudaError_t launch_merge(const float* part_o, const float* part_m, const float* 
 cudaError_t launch_merge_partial(const float* part_o, const float* part_m, const float* part_l,
                                  uint32_t n_parts, uint32_t rows, uint32_t head_dim,
                                  float* out_o, float* out_m, float* out_l, cudaStream_t stream) {
-    const unsigned blocks = (rows + 3) / 4;
-    merge_kernel<float, false><<<blocks, 128, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
+    const unsigned blocks = rows;
+    merge_kernel<float, false><<<blocks, head_dim, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
                                                            head_dim, out_o, out_m, out_l);
     return cudaGetLastError();
 }
@@ -287,6 +314,8 @@ int kvq_lse_merge(const float* part_o, const float* part_m, const float* part_l,
     g_error.clear();
     if (!part_o || !part_m || !part_l || !out) return fail(KVQ_ERR_INVALID, "a pointer is NULL");
     if (n_parts == 0 || rows == 0 || head_dim == 0) return fail(KVQ_ERR_INVALID, "empty merge");
+    if (head_dim > 1024 || head_dim % 32) return fail(KVQ_ERR_INVALID, "head_dim %u: a multiple of 32 up to 1024", head_dim);
+    if (rows > 0x7FFFFFFFu) return fail(KVQ_ERR_INVALID, "too many rows");
     if (out_dtype != KVQ_F16 && out_dtype != KVQ_F32) return fail(KVQ_ERR_INVALID, "bad out_dtype");
     int rc = device_ok();
     if (rc) return rc;

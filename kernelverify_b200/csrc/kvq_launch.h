@@ -26,6 +26,10 @@ cudaError_t launch_dequant(const uint32_t* wq, const void* scales, const void* b
                            uint64_t rows, uint32_t head_dim, uint32_t group, int dtype,
                            float* out, cudaStream_t stream);
 
+// Tensor-core partial kernel: fp16, 4-bit, head_dim 128, ht in {4, 8}.
+cudaError_t launch_mma4(const Problem& P, int ht, int group, float* part_o, float* part_m,
+                        float* part_l, cudaStream_t stream);
+
 cudaError_t launch_merge(const float* part_o, const float* part_m, const float* part_l,
                          uint32_t n_parts, uint32_t rows, uint32_t head_dim, int out_dtype,
                          void* out, cudaStream_t stream);

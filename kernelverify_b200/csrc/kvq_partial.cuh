@@ -227,7 +227,9 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
     }
 }
 
-// Log-sum-exp merge of n_parts partials per row; one warp per row.
+// Log-sum-exp merge of n_parts partials: one block per row, one thread per
+// dim (blockDim.x == head_dim), so the partials' O rows are read coalesced
+// and the m / l of each part are one broadcast load per warp.
 // NORMALIZE: out = sum_p O_p e^(m_p - m) / l in TO. Otherwise the merged
 // partial (O unnormalised, m, l) in fp32.
 template <typename TO, bool NORMALIZE>
@@ -236,33 +238,23 @@ merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
              const float* __restrict__ part_l, uint32_t n_parts, uint32_t rows,
              uint32_t head_dim, TO* __restrict__ out, float* __restrict__ out_m,
              float* __restrict__ out_l) {
-    const uint32_t row = blockIdx.x * 4 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
+    const uint32_t row = blockIdx.x;
+    const uint32_t d = threadIdx.x;
     float m = -INFINITY;
-    for (uint32_t p = lane; p < n_parts; p += 32) m = fmaxf(m, part_m[(size_t)p * rows + row]);
-    m = warp_max(m);
-    float l = 0.0f;
-    for (uint32_t p = lane; p < n_parts; p += 32) {
+    for (uint32_t p = 0; p < n_parts; ++p) m = fmaxf(m, part_m[(size_t)p * rows + row]);
+    float l = 0.0f, o = 0.0f;
+    for (uint32_t p = 0; p < n_parts; ++p) {
         const float mp = part_m[(size_t)p * rows + row];
-        if (mp != -INFINITY) l += part_l[(size_t)p * rows + row] * expf(mp - m);
+        if (mp == -INFINITY) continue;
+        const float w = expf(mp - m);
+        l = fmaf(part_l[(size_t)p * rows + row], w, l);
+        o = fmaf(part_o[((size_t)p * rows + row) * head_dim + d], w, o);
     }
-    l = warp_sum(l);
-    for (uint32_t d = lane; d < head_dim; d += 32) {
-        float o = 0.0f;
-        for (uint32_t p = 0; p < n_parts; ++p) {
-            const float mp = part_m[(size_t)p * rows + row];
-            if (mp == -INFINITY) continue;
-            o = fmaf(part_o[((size_t)p * rows + row) * head_dim + d], expf(mp - m), o);
-        }
-        if constexpr (NORMALIZE) {
-            out[(size_t)row * head_dim + d] = from_f32<TO>(o / l);
-        } else {
-            out[(size_t)row * head_dim + d] = m == -INFINITY ? 0.0f : o;
-        }
-    }
-    if constexpr (!NORMALIZE) {
-        if (lane == 0) {
+    if constexpr (NORMALIZE) {
+        out[(size_t)row * head_dim + d] = from_f32<TO>(o / l);
+    } else {
+        out[(size_t)row * head_dim + d] = m == -INFINITY ? 0.0f : o;
+        if (d == 0) {
             out_m[row] = m;
             out_l[row] = l;
         }
