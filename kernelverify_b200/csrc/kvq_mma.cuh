@@ -57,9 +57,14 @@ struct Layout {
     static constexpr int STAGE = VB + TP * G * 2;         // bytes per stage
     static_assert(STAGE % 128 == 0, "stage size");
     static constexpr int RING = STAGE * STAGES;
+    // per consumer warp: fp32 [16][G] k_scale, k_bias, v_scale, v_bias - 128 v_scale
+    // of the warp's 16-position block
+    static constexpr int SCR_WARP = 4 * 16 * G * 4;
+    static constexpr int SCR = RING;                       // scratch base
+    static constexpr int RING_SCR = RING + CWARPS * SCR_WARP;
     // merge area (reuses the ring once it drains): per warp O[8][128], m[8], l[8], bsum[8][G]
     static constexpr int MERGE = CWARPS * (8 * DH + 8 + 8 + 8 * G) * 4 + 8 * 4;
-    static constexpr int BYTES = (RING > MERGE ? RING : MERGE) + 2 * STAGES * 8 + 16;
+    static constexpr int BYTES = (RING_SCR > MERGE ? RING_SCR : MERGE) + 2 * STAGES * 8 + 16;
 };
 
 template <int GROUP>
@@ -131,6 +136,27 @@ __device__ __forceinline__ void named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// ---- integer helpers with a fixed instruction choice ------------------------
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "n"(SEL));
+    return d;
+}
+// (x & mask) | magic in one lop3
+template <uint32_t MASK, uint32_t MAGIC>
+__device__ __forceinline__ uint32_t and_or(uint32_t x) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(x), "n"(MASK), "n"(MAGIC));
+    return d;
+}
+// x >> k as mul.hi by the run-time 2^(32-k): an FMA-pipe integer multiply
+__device__ __forceinline__ uint32_t shr_mul(uint32_t x, uint32_t pow2) {
+    uint32_t d;
+    asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(pow2));
+    return d;
+}
+
 // ---- exact small-integer conversions ----------------------------------------
 __device__ __forceinline__ uint32_t h2_sub1024(uint32_t x) {
     __half2 v = __hsub2(*reinterpret_cast<__half2*>(&x), __half2(__half(1024.0f), __half(1024.0f)));
@@ -147,23 +173,38 @@ __device__ __forceinline__ uint32_t bf2_sub128(uint32_t x) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 // word of 8 nibbles n0..n7 -> four half2 registers (n0,n4) (n1,n5) (n2,n6) (n3,n7)
-__device__ __forceinline__ void nibbles_f16(uint32_t w, uint32_t (&h)[4]) {
-    h[0] = h2_sub1024((w & 0x000F000Fu) | 0x64006400u);
-    h[1] = h2_hi_nibble((w & 0x00F000F0u) | 0x64006400u);
-    const uint32_t w8 = w >> 8;
-    h[2] = h2_sub1024((w8 & 0x000F000Fu) | 0x64006400u);
-    h[3] = h2_hi_nibble((w8 & 0x00F000F0u) | 0x64006400u);
+__device__ __forceinline__ void nibbles_f16(uint32_t w, uint32_t shr8, uint32_t (&h)[4]) {
+    h[0] = h2_sub1024(and_or<0x000F000Fu, 0x64006400u>(w));
+    h[1] = h2_hi_nibble(and_or<0x00F000F0u, 0x64006400u>(w));
+    const uint32_t w8 = shr_mul(w, shr8);
+    h[2] = h2_sub1024(and_or<0x000F000Fu, 0x64006400u>(w8));
+    h[3] = h2_hi_nibble(and_or<0x00F000F0u, 0x64006400u>(w8));
 }
-// byte k of words a and b -> bf16x2 (128 + low nibble of a, 128 + low of b)
-// and (128 + high of a, 128 + high of b): exact bf16 values of the codes plus
-// 128. The combine subtracts 128 * P' through the bias term instead of per
-// code (sum_t P'_t (128 + c_t) + sum_t p_t (b_t - 128 s_t) = sum_t p_t (s_t c_t + b_t)).
+// Bytes K and K+1 of words a and b -> four bf16x2 registers of exact code
+// values plus 128: (lo(a.K), lo(b.K)), (hi(a.K), hi(b.K)), (lo(a.K+1),
+// lo(b.K+1)), (hi(a.K+1), hi(b.K+1)). One byte permute gathers the four
+// bytes as [a.K, a.K+1, b.K, b.K+1]; each nibble pair is then one shift
+// (an FMA-pipe mul.hi) and one and-or. The combine subtracts 128 * P' through
+// the bias term instead of per code:
+//   sum_t P'_t (128 + c_t) + sum_t p_t (b_t - 128 s_t) = sum_t p_t (s_t c_t + b_t).
 template <int K>
-__device__ __forceinline__ void pair_bf16(uint32_t a, uint32_t b, uint32_t& lo, uint32_t& hi) {
+__device__ __forceinline__ void quad_bf16(uint32_t a, uint32_t b, const Problem& P, uint32_t& lo0,
+                                          uint32_t& hi0, uint32_t& lo1, uint32_t& hi1) {
+    constexpr uint32_t sel = K | ((K + 1) << 4) | ((4 + K) << 8) | ((5 + K) << 12);
+    const uint32_t u = prmt<sel>(a, b);
+    lo0 = and_or<0x000F000Fu, 0x43004300u>(u);
+    hi0 = and_or<0x000F000Fu, 0x43004300u>(shr_mul(u, P.shr4));
+    lo1 = and_or<0x000F000Fu, 0x43004300u>(shr_mul(u, P.shr8));
+    hi1 = and_or<0x000F000Fu, 0x43004300u>(shr_mul(u, P.shr12));
+}
+// byte K of words a and b only (lo, hi)
+template <int K>
+__device__ __forceinline__ void pair_bf16(uint32_t a, uint32_t b, const Problem& P, uint32_t& lo,
+                                          uint32_t& hi) {
     constexpr uint32_t sel = K | (K << 4) | ((4 + K) << 8) | ((4 + K) << 12);
-    const uint32_t u = __byte_perm(a, b, sel);
-    lo = (u & 0x000F000Fu) | 0x43004300u;
-    hi = ((u >> 4) & 0x000F000Fu) | 0x43004300u;
+    const uint32_t u = prmt<sel>(a, b);
+    lo = and_or<0x000F000Fu, 0x43004300u>(u);
+    hi = and_or<0x000F000Fu, 0x43004300u>(shr_mul(u, P.shr4));
 }
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -173,19 +214,26 @@ __device__ __forceinline__ void bf16x2_to_f32(uint32_t v, float& lo, float& hi) 
     lo = __uint_as_float(v << 16);
     hi = __uint_as_float(v & 0xFFFF0000u);
 }
-// split two fp32 values into three packed bf16x2 parts whose sums reproduce them
+// Split two fp32 values into three packed bf16x2 parts whose sum reproduces
+// them: bf16 is the upper half of fp32, so each part is a truncation taken by
+// a byte permute, and each residual x - part is exact in fp32. The three parts
+// carry the full 24-bit significand (the last truncation drops less than one
+// fp32 ulp). Integer and fma-pipe work only.
 __device__ __forceinline__ void split3(float x0, float x1, uint32_t& p_hi, uint32_t& p_mid,
                                        uint32_t& p_lo) {
-    const float2 x = make_float2(x0, x1);
     const float2 neg1 = make_float2(-1.0f, -1.0f);
-    float2 t;
-    p_hi = pack_bf16(x.x, x.y);
-    bf16x2_to_f32(p_hi, t.x, t.y);
-    const float2 r = __ffma2_rn(t, neg1, x);          // x - hi, exact
-    p_mid = pack_bf16(r.x, r.y);
-    bf16x2_to_f32(p_mid, t.x, t.y);
-    const float2 r2 = __ffma2_rn(t, neg1, r);         // r - mid, exact
-    p_lo = pack_bf16(r2.x, r2.y);
+    const uint32_t u0 = __float_as_uint(x0), u1 = __float_as_uint(x1);
+    p_hi = prmt<0x7632>(u0, u1);
+    // the parts back as fp32: low half << 16 (an integer multiply), high half masked
+    const float2 r = __ffma2_rn(make_float2(__uint_as_float(p_hi * 65536u),
+                                            __uint_as_float(p_hi & 0xFFFF0000u)),
+                                neg1, make_float2(x0, x1));
+    const uint32_t v0 = __float_as_uint(r.x), v1 = __float_as_uint(r.y);
+    p_mid = prmt<0x7632>(v0, v1);
+    const float2 r2 = __ffma2_rn(make_float2(__uint_as_float(p_mid * 65536u),
+                                             __uint_as_float(p_mid & 0xFFFF0000u)),
+                                 neg1, r);
+    p_lo = prmt<0x7632>(__float_as_uint(r2.x), __float_as_uint(r2.y));
 }
 
 __device__ __forceinline__ float h2f(const __half* p) { return __half2float(*p); }
@@ -196,6 +244,20 @@ __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// G consecutive fp32 values from shared memory (vector loads)
+template <int G>
+__device__ __forceinline__ void load_f(const float* p, float (&out)[G]) {
+    if constexpr (G == 1) {
+        out[0] = *p;
+    } else if constexpr (G == 2) {
+        const float2 f = *reinterpret_cast<const float2*>(p);
+        out[0] = f.x; out[1] = f.y;
+    } else {
+        const float4 f = *reinterpret_cast<const float4*>(p);
+        out[0] = f.x; out[1] = f.y; out[2] = f.z; out[3] = f.w;
+    }
 }
 
 // G consecutive fp16 values -> fp32
@@ -216,7 +278,7 @@ __device__ __forceinline__ void load_g(const __half* p, float (&out)[G]) {
 
 // -----------------------------------------------------------------------------
 template <int HT, int GROUP>
-__global__ void __launch_bounds__(THREADS, KVQ_MMA_MINBLOCKS)
+__global__ void __launch_bounds__(THREADS, GROUP == 32 ? 2 : KVQ_MMA_MINBLOCKS)
 partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m,
                float* __restrict__ part_l) {
     using Lay = Layout<GROUP>;
@@ -231,7 +293,7 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
     const float scale2 = P.scale * L2E;   // scores are kept in log2 units
 
     extern __shared__ __align__(128) unsigned char smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (Lay::RING > Lay::MERGE ? Lay::RING : Lay::MERGE));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (Lay::RING_SCR > Lay::MERGE ? Lay::RING_SCR : Lay::MERGE));
     uint64_t* empty = full + STAGES;
     int* err_flag = reinterpret_cast<int*>(empty + STAGES);
 
@@ -255,8 +317,8 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&full[s], 1);          // the producer's arrive + the stage's bytes
+            mbar_init(&empty[s], CWARPS);    // every consumer warp releases every stage
         }
         *err_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -337,7 +399,11 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
         // 8-position n-tile, pi(n) = (n >> 1) + 4 (n & 1).
         const int krow = (r >> 1) + 4 * (r & 1);
 
-        for (int s = warp; s < n_stages; s += CWARPS) {
+        // Every consumer warp takes every stage: warp w owns the 16-position
+        // block w of each 64-position stage. Waiting on every stage in order
+        // keeps each warp at most one phase ahead of each barrier, which the
+        // parity-based waits require.
+        for (int s = 0; s < n_stages; ++s) {
             const int slot = s % STAGES, round = s / STAGES;
             if (!mbar_wait(&full[slot], round & 1)) {
                 atomicExch(err_flag, 1);
@@ -345,27 +411,49 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
             }
             unsigned char* st = smem + slot * Lay::STAGE;
             const uint32_t t0 = lo + s * TP;
+            const int blk = warp;
             const int nvalid = (int)min((uint32_t)TP, hi - t0);
-            if (nvalid < TP) {
-                // tail stage: rows past the logical end get zero V scales and
-                // biases, so their (zero) weights meet finite values only
-                __half* vsz = reinterpret_cast<__half*>(st + Lay::VS);
-                __half* vbz = reinterpret_cast<__half*>(st + Lay::VB);
-                for (int i = nvalid * G + lane; i < TP * G; i += 32) {
-                    vsz[i] = __float2half(0.0f);
-                    vbz[i] = __float2half(0.0f);
-                }
-                // order these generic-proxy writes before any later TMA write to the slot
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            if (nvalid <= blk * 16) {          // no live position in this warp's block
                 __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+                continue;
             }
 
-            const __half* ksb = reinterpret_cast<const __half*>(st + Lay::KS);
-            const __half* kbb = reinterpret_cast<const __half*>(st + Lay::KB);
-            const __half* vsb = reinterpret_cast<const __half*>(st + Lay::VS);
-            const __half* vbb = reinterpret_cast<const __half*>(st + Lay::VB);
-#pragma unroll 1
-            for (int blk = 0; blk < TP / 16; ++blk) {
+            // fp32 copies of the block's scales and biases, converted once (every
+            // score row and P' part reuses them); positions past the logical end
+            // get zero V scale and bias so their zero weights meet finite values
+            // only. The V bias carries the codes' +128 offset.
+            float* scr = reinterpret_cast<float*>(smem + Lay::SCR + warp * Lay::SCR_WARP);
+            {
+                const __half2* kss = reinterpret_cast<const __half2*>(st + Lay::KS) + blk * 16 * G / 2;
+                const __half2* kbs = reinterpret_cast<const __half2*>(st + Lay::KB) + blk * 16 * G / 2;
+                const __half2* vss = reinterpret_cast<const __half2*>(st + Lay::VS) + blk * 16 * G / 2;
+                const __half2* vbs = reinterpret_cast<const __half2*>(st + Lay::VB) + blk * 16 * G / 2;
+                float2* ks2 = reinterpret_cast<float2*>(scr);
+                float2* kb2 = ks2 + 16 * G / 2;
+                float2* vs2 = kb2 + 16 * G / 2;
+                float2* vb2 = vs2 + 16 * G / 2;
+                const int nv_blk = nvalid - blk * 16;
+#pragma unroll
+                for (int i = lane; i < 16 * G / 2; i += 32) {
+                    ks2[i] = __half22float2(kss[i]);
+                    kb2[i] = __half22float2(kbs[i]);
+                    // element 2i belongs to position 2i / G, element 2i + 1 to (2i + 1) / G
+                    const bool live0 = (2 * i) / G < nv_blk, live1 = (2 * i + 1) / G < nv_blk;
+                    float2 vsv = __half22float2(vss[i]), vbv = __half22float2(vbs[i]);
+                    vsv = make_float2(live0 ? vsv.x : 0.0f, live1 ? vsv.y : 0.0f);
+                    vbv = make_float2(live0 ? vbv.x : 0.0f, live1 ? vbv.y : 0.0f);
+                    vs2[i] = vsv;
+                    vb2[i] = __ffma2_rn(vsv, make_float2(-128.0f, -128.0f), vbv);
+                }
+                __syncwarp();
+            }
+            // indexed by the position within the warp's block
+            const float* ksb = scr;
+            const float* kbb = scr + 16 * G;
+            const float* vsb = scr + 2 * 16 * G;
+            const float* vbb = scr + 3 * 16 * G;
+            {
                 // ---- scores of 16 positions, log2 units: lane (r, j) holds head
                 // r at positions j, j+4 (n-tile 0) and 8+j, 12+j (n-tile 1)
                 float sc[4];
@@ -384,7 +472,7 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
 #pragma unroll
                         for (int wi = 0; wi < WPG; ++wi) {
                             uint32_t hcodes[4];
-                            nibbles_f16(w[wi], hcodes);
+                            nibbles_f16(w[wi], P.shr8, hcodes);
                             mma_f16(x[g], qa[g][2 * wi][0], 0u, qa[g][2 * wi][1], 0u, hcodes[0],
                                     hcodes[1]);
                             mma_f16(x[g], qa[g][2 * wi + 1][0], 0u, qa[g][2 * wi + 1][1], 0u,
@@ -393,10 +481,11 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                     }
 #pragma unroll
                     for (int c = 0; c < 2; ++c) {
-                        const int pos = blk * 16 + nt * 8 + j + 4 * c;
+                        const int lpos = nt * 8 + j + 4 * c;
+                        const int pos = blk * 16 + lpos;
                         float ksf[G], kbf[G];
-                        load_g<G>(ksb + pos * G, ksf);
-                        load_g<G>(kbb + pos * G, kbf);
+                        load_f<G>(ksb + lpos * G, ksf);
+                        load_f<G>(kbb + lpos * G, kbf);
                         float acc = 0.0f;
 #pragma unroll
                         for (int g = 0; g < G; ++g) acc = fmaf(ksf[g], x[g][c], fmaf(kbf[g], qsum[g], acc));
@@ -439,8 +528,8 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                 float vsf[4][G], vbf[4][G];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    load_g<G>(vsb + (p0 + 4 * k) * G, vsf[k]);
-                    load_g<G>(vbb + (p0 + 4 * k) * G, vbf[k]);
+                    load_f<G>(vsb + (j + 4 * k) * G, vsf[k]);
+                    load_f<G>(vbb + (j + 4 * k) * G, vbf[k]);
                 }
                 // B fragments: the three bf16 parts of P' = p * v_scale per group
                 uint32_t bh[G][2], bm[G][2], bl[G][2];
@@ -448,10 +537,10 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                 for (int g = 0; g < G; ++g) {
                     // bias with the codes' +128 offset folded in: b - 128 s
                     float acc = bsum[g];
-                    acc = fmaf(e0, fmaf(vsf[0][g], -128.0f, vbf[0][g]), acc);
-                    acc = fmaf(e1, fmaf(vsf[1][g], -128.0f, vbf[1][g]), acc);
-                    acc = fmaf(e2, fmaf(vsf[2][g], -128.0f, vbf[2][g]), acc);
-                    acc = fmaf(e3, fmaf(vsf[3][g], -128.0f, vbf[3][g]), acc);
+                    acc = fmaf(e0, vbf[0][g], acc);
+                    acc = fmaf(e1, vbf[1][g], acc);
+                    acc = fmaf(e2, vbf[2][g], acc);
+                    acc = fmaf(e3, vbf[3][g], acc);
                     bsum[g] = acc;
                     const float2 v01 = __fmul2_rn(make_float2(e0, e1), make_float2(vsf[0][g], vsf[1][g]));
                     const float2 v23 = __fmul2_rn(make_float2(e2, e3), make_float2(vsf[2][g], vsf[3][g]));
@@ -480,16 +569,25 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                             wD[k] = *reinterpret_cast<const uint16_t*>(vrow + (p0 + 12) * ROWB + boff);
                         }
                     }
+                    // A fragments of M-tile ii: (a0, a1) from rows (j, j+4) and
+                    // (a2, a3) from rows (8+j, 12+j), byte ii of the lane's chunk
+                    uint32_t fa[MTG][4];
+#pragma unroll
+                    for (int ii = 0; ii < MTG; ii += 2) {
+                        const int wi = ii >> 2;
+                        if constexpr (MTG >= 2) {
+                            if ((ii & 3) == 0) {
+                                quad_bf16<0>(wA[wi], wB[wi], P, fa[ii][0], fa[ii][1], fa[ii + 1][0], fa[ii + 1][1]);
+                                quad_bf16<0>(wC[wi], wD[wi], P, fa[ii][2], fa[ii][3], fa[ii + 1][2], fa[ii + 1][3]);
+                            } else {
+                                quad_bf16<2>(wA[wi], wB[wi], P, fa[ii][0], fa[ii][1], fa[ii + 1][0], fa[ii + 1][1]);
+                                quad_bf16<2>(wC[wi], wD[wi], P, fa[ii][2], fa[ii][3], fa[ii + 1][2], fa[ii + 1][3]);
+                            }
+                        }
+                    }
 #pragma unroll
                     for (int ii = 0; ii < MTG; ++ii) {
-                        uint32_t a0, a1, a2, a3;
-                        const int wi = ii >> 2;
-                        switch (ii & 3) {
-                            case 0: pair_bf16<0>(wA[wi], wB[wi], a0, a1); pair_bf16<0>(wC[wi], wD[wi], a2, a3); break;
-                            case 1: pair_bf16<1>(wA[wi], wB[wi], a0, a1); pair_bf16<1>(wC[wi], wD[wi], a2, a3); break;
-                            case 2: pair_bf16<2>(wA[wi], wB[wi], a0, a1); pair_bf16<2>(wC[wi], wD[wi], a2, a3); break;
-                            default: pair_bf16<3>(wA[wi], wB[wi], a0, a1); pair_bf16<3>(wC[wi], wD[wi], a2, a3); break;
-                        }
+                        const uint32_t a0 = fa[ii][0], a1 = fa[ii][1], a2 = fa[ii][2], a3 = fa[ii][3];
                         // a0: (dim row r, pos j, j+4); a1: (row r+8 = high nibble);
                         // a2/a3: the same for positions 8+j, 12+j
                         float (&acc)[4] = oacc[g * MTG + ii];
