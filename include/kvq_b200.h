@@ -161,6 +161,27 @@ int kvq_quantize(const void* w, uint64_t rows, uint32_t head_dim, uint32_t bits,
                  uint32_t group_size, uint32_t dtype, uint32_t* wq, void* scales,
                  void* biases, void* stream);
 
+/*
+ * The full step like kvq_decode, for callers that cannot allocate device
+ * memory: a host that binds this library through a plain C FFI and owns no
+ * CUDA allocator (a cgo / JNI / ctypes worker), or a serving process that
+ * reserves all device memory up front and forbids allocation on its decode
+ * path. No counterpart in the reference.
+ *
+ * Its scratch is a buffer inside the library itself, KVQ_NOALLOC_SCRATCH_BYTES
+ * bytes on every GPU that loads the library, held until the process exits.
+ * Calls whose split partials need more (kvq_workspace_bytes(a) above the
+ * limit) fail with KVQ_ERR_INVALID; use kvq_decode with a workspace instead.
+ * The first call on a device looks up the buffer's device address for that
+ * device; make that first call before any stream capture. Every call on a
+ * device shares the one buffer: calls that overlap on the GPU (two streams,
+ * two host threads) race on it and must be serialized by the caller. Nothing
+ * in the buffer needs to start at zero: each call writes every partial it
+ * reads.
+ */
+#define KVQ_NOALLOC_SCRATCH_BYTES (16u << 20)
+int kvq_decode_noalloc(const kvq_args* a, void* out, void* stream);
+
 /* 1 when this library carries a kernel for the combination, else 0. */
 int kvq_supports(uint32_t head_dim, uint32_t bits, uint32_t group_size, uint32_t dtype);
 

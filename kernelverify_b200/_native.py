@@ -17,10 +17,11 @@ ABI_VERSION = 1
 KVQ_OK, KVQ_ERR_INVALID, KVQ_ERR_LAUNCH, KVQ_ERR_UNSUPPORTED = 0, -1, -2, -3
 KVQ_F16, KVQ_F32 = 0, 1
 KVQ_T_END_ALL = 0xFFFFFFFF
+KVQ_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 # Every symbol include/kvq_b200.h declares.
 EXPORTS = ("kvq_workspace_bytes", "kvq_decode", "kvq_decode_partial", "kvq_split_count",
-           "kvq_decode_splits", "kvq_lse_merge",
+           "kvq_decode_splits", "kvq_lse_merge", "kvq_decode_noalloc",
            "kvq_dequant", "kvq_quantize", "kvq_supports", "kvq_last_error", "kvq_abi_version")
 
 
@@ -66,6 +67,7 @@ def _declare(lib) -> None:
         "kvq_split_count": (U32, [AP]),
         "kvq_decode_splits": (I, [AP, P, P, P, P]),
         "kvq_lse_merge": (I, [P, P, P, U32, U32, U32, U32, P, P]),
+        "kvq_decode_noalloc": (I, [AP, P, P]),
         "kvq_dequant": (I, [P, P, P, U64, U32, U32, U32, U32, P, P]),
         "kvq_quantize": (I, [P, U64, U32, U32, U32, U32, P, P, P, P]),
         "kvq_supports": (I, [U32, U32, U32, U32]),

@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "kvq_b200.h"
@@ -184,6 +185,33 @@ int check_workspace(const void* ws, size_t have, size_t need) {
     return KVQ_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Scratch for kvq_decode_noalloc: a file-scope device buffer, present on every
+// device that loads this library. Host code may not use its name as a device
+// address (on the host it is a stand-in), so the device address is looked up
+// once per device with cudaGetSymbolAddress, with that device current.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[KVQ_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(KVQ_ERR_UNSUPPORTED, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress of the built-in scratch");
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return KVQ_OK;
+}
+
 }  // namespace
 
 namespace kvq {
@@ -246,6 +274,36 @@ int kvq_decode(const kvq_args* a, void* out, void* workspace, size_t workspace_b
     if (rc) return rc;
     auto s = static_cast<cudaStream_t>(stream);
     char* ws = static_cast<char*>(workspace);
+    float* po = reinterpret_cast<float*>(ws);
+    float* pm = reinterpret_cast<float*>(ws + pl.part_bytes);
+    float* pll = reinterpret_cast<float*>(ws + pl.part_bytes + pl.ml_bytes);
+    cudaError_t e = launch_partial_any(pl, a->bits, a->dtype, a->head_dim, po, pm, pll, s);
+    if (e != cudaSuccess) return cuda_fail(e, "partial kernel launch");
+    e = kvq::launch_merge(po, pm, pll, pl.P.n_splits, pl.rows, a->head_dim, (int)a->dtype, out, s);
+    if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
+    return KVQ_OK;
+}
+
+int kvq_decode_noalloc(const kvq_args* a, void* out, void* stream) {
+    g_error.clear();
+    Plan pl;
+    int rc = plan(a, &pl);
+    if (rc) return rc;
+    if (!out) return fail(KVQ_ERR_INVALID, "out is NULL");
+    if (!aligned(out, a->dtype == KVQ_F16 ? 2 : 4)) return fail(KVQ_ERR_INVALID, "out is misaligned");
+    const size_t need = 2 * pl.ml_bytes + pl.part_bytes;
+    if (need > KVQ_NOALLOC_SCRATCH_BYTES)
+        return fail(KVQ_ERR_INVALID,
+                    "this step needs %zu bytes of scratch for its %u T splits, above the %u "
+                    "bytes built into the library; call kvq_decode with a workspace instead",
+                    need, pl.P.n_splits, (unsigned)KVQ_NOALLOC_SCRATCH_BYTES);
+    rc = device_ok();
+    if (rc) return rc;
+    void* scratch = nullptr;
+    rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    auto s = static_cast<cudaStream_t>(stream);
+    char* ws = static_cast<char*>(scratch);
     float* po = reinterpret_cast<float*>(ws);
     float* pm = reinterpret_cast<float*>(ws + pl.part_bytes);
     float* pll = reinterpret_cast<float*>(ws + pl.part_bytes + pl.ml_bytes);
