@@ -254,9 +254,14 @@ __device__ __forceinline__ void load_f(const float* p, float (&out)[G]) {
     } else if constexpr (G == 2) {
         const float2 f = *reinterpret_cast<const float2*>(p);
         out[0] = f.x; out[1] = f.y;
-    } else {
+    } else if constexpr (G == 4) {
         const float4 f = *reinterpret_cast<const float4*>(p);
         out[0] = f.x; out[1] = f.y; out[2] = f.z; out[3] = f.w;
+    } else {
+        const float4 f = *reinterpret_cast<const float4*>(p);
+        const float4 h = *reinterpret_cast<const float4*>(p + 4);
+        out[0] = f.x; out[1] = f.y; out[2] = f.z; out[3] = f.w;
+        out[4] = h.x; out[5] = h.y; out[6] = h.z; out[7] = h.w;
     }
 }
 
@@ -420,39 +425,32 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
             }
 
             // fp32 copies of the block's scales and biases, converted once (every
-            // score row and P' part reuses them); positions past the logical end
-            // get zero V scale and bias so their zero weights meet finite values
-            // only. The V bias carries the codes' +128 offset.
+            // score row and P' part reuses them), per position [k_scale (G) |
+            // k_bias (G)] with the score scale log2(e)/sqrt(DH) folded in, and
+            // [v_scale (G) | v_bias - 128 v_scale (G)]; positions past the
+            // logical end get zero V scale and bias so their zero weights meet
+            // finite values only.
             float* scr = reinterpret_cast<float*>(smem + Lay::SCR + warp * Lay::SCR_WARP);
             {
-                const __half2* kss = reinterpret_cast<const __half2*>(st + Lay::KS) + blk * 16 * G / 2;
-                const __half2* kbs = reinterpret_cast<const __half2*>(st + Lay::KB) + blk * 16 * G / 2;
-                const __half2* vss = reinterpret_cast<const __half2*>(st + Lay::VS) + blk * 16 * G / 2;
-                const __half2* vbs = reinterpret_cast<const __half2*>(st + Lay::VB) + blk * 16 * G / 2;
-                float2* ks2 = reinterpret_cast<float2*>(scr);
-                float2* kb2 = ks2 + 16 * G / 2;
-                float2* vs2 = kb2 + 16 * G / 2;
-                float2* vb2 = vs2 + 16 * G / 2;
+                const __half* kss = reinterpret_cast<const __half*>(st + Lay::KS) + blk * 16 * G;
+                const __half* kbs = reinterpret_cast<const __half*>(st + Lay::KB) + blk * 16 * G;
+                const __half* vss = reinterpret_cast<const __half*>(st + Lay::VS) + blk * 16 * G;
+                const __half* vbs = reinterpret_cast<const __half*>(st + Lay::VB) + blk * 16 * G;
                 const int nv_blk = nvalid - blk * 16;
-#pragma unroll
-                for (int i = lane; i < 16 * G / 2; i += 32) {
-                    ks2[i] = __half22float2(kss[i]);
-                    kb2[i] = __half22float2(kbs[i]);
-                    // element 2i belongs to position 2i / G, element 2i + 1 to (2i + 1) / G
-                    const bool live0 = (2 * i) / G < nv_blk, live1 = (2 * i + 1) / G < nv_blk;
-                    float2 vsv = __half22float2(vss[i]), vbv = __half22float2(vbs[i]);
-                    vsv = make_float2(live0 ? vsv.x : 0.0f, live1 ? vsv.y : 0.0f);
-                    vbv = make_float2(live0 ? vbv.x : 0.0f, live1 ? vbv.y : 0.0f);
-                    vs2[i] = vsv;
-                    vb2[i] = __ffma2_rn(vsv, make_float2(-128.0f, -128.0f), vbv);
+                for (int i = lane; i < 16 * G; i += 32) {
+                    const int pos = i / G, g = i % G;
+                    const bool live = pos < nv_blk;
+                    const float vsv = live ? __half2float(vss[i]) : 0.0f;
+                    const float vbv = live ? __half2float(vbs[i]) : 0.0f;
+                    scr[pos * 2 * G + g] = __half2float(kss[i]) * scale2;
+                    scr[pos * 2 * G + G + g] = __half2float(kbs[i]) * scale2;
+                    scr[16 * 2 * G + pos * 2 * G + g] = vsv;
+                    scr[16 * 2 * G + pos * 2 * G + G + g] = fmaf(vsv, -128.0f, vbv);
                 }
                 __syncwarp();
             }
-            // indexed by the position within the warp's block
-            const float* ksb = scr;
-            const float* kbb = scr + 16 * G;
-            const float* vsb = scr + 2 * 16 * G;
-            const float* vbb = scr + 3 * 16 * G;
+            const float* kscr = scr;                 // [16][2G]
+            const float* vscr = scr + 16 * 2 * G;    // [16][2G]
             {
                 // ---- scores of 16 positions, log2 units: lane (r, j) holds head
                 // r at positions j, j+4 (n-tile 0) and 8+j, 12+j (n-tile 1)
@@ -483,13 +481,12 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                     for (int c = 0; c < 2; ++c) {
                         const int lpos = nt * 8 + j + 4 * c;
                         const int pos = blk * 16 + lpos;
-                        float ksf[G], kbf[G];
-                        load_f<G>(ksb + lpos * G, ksf);
-                        load_f<G>(kbb + lpos * G, kbf);
+                        float kf[2 * G];
+                        load_f<2 * G>(kscr + lpos * 2 * G, kf);
                         float acc = 0.0f;
 #pragma unroll
-                        for (int g = 0; g < G; ++g) acc = fmaf(ksf[g], x[g][c], fmaf(kbf[g], qsum[g], acc));
-                        sc[nt * 2 + c] = pos < nvalid ? acc * scale2 : -INFINITY;
+                        for (int g = 0; g < G; ++g) acc = fmaf(kf[g], x[g][c], fmaf(kf[G + g], qsum[g], acc));
+                        sc[nt * 2 + c] = pos < nvalid ? acc : -INFINITY;
                     }
                 }
 
@@ -497,10 +494,12 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                 // m_run moves only when a head's block max exceeds it by more
                 // than 2^8, so weights stay <= 256 and O rarely needs rescaling
                 float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                const bool grow = mx > m_run + 8.0f;
-                if (__any_sync(0xffffffffu, grow)) {
+                if (__any_sync(0xffffffffu, mx > m_run + 8.0f)) {
+                    // some head's scores outgrew its reference point: take the
+                    // head's block max over its four lanes and move the point
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                    const bool grow = mx > m_run + 8.0f;
                     const float m_new = grow ? mx : m_run;
                     const float alpha = ex2(m_run - m_new);   // 0 on the first block, 1 if unchanged
                     m_run = m_new;
@@ -528,8 +527,10 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                 float vsf[4][G], vbf[4][G];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    load_f<G>(vsb + (j + 4 * k) * G, vsf[k]);
-                    load_f<G>(vbb + (j + 4 * k) * G, vbf[k]);
+                    float vf[2 * G];
+                    load_f<2 * G>(vscr + (j + 4 * k) * 2 * G, vf);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) { vsf[k][g] = vf[g]; vbf[k][g] = vf[G + g]; }
                 }
                 // B fragments: the three bf16 parts of P' = p * v_scale per group
                 uint32_t bh[G][2], bm[G][2], bl[G][2];
