@@ -275,14 +275,9 @@ def run_ours(args) -> dict | None:
     sp = stream.cuda_stream
 
     if args.config == 5:
-        go = torch.empty((world, rows, cfg["DH"]), dtype=torch.float32, device=device)
-        gm = torch.empty((world, rows), dtype=torch.float32, device=device)
-        gl = torch.empty((world, rows), dtype=torch.float32, device=device)
-        lo_ = torch.empty((rows, cfg["DH"]), dtype=torch.float32, device=device)
-        lm_ = torch.empty((rows,), dtype=torch.float32, device=device)
-        ll_ = torch.empty((rows,), dtype=torch.float32, device=device)
-        ws_need = max(lib.kvq_workspace_bytes(a) for a in margs)
-        ws = torch.empty(max(ws_need, 256), dtype=torch.uint8, device=device)
+        from kernelverify_b200.pack.tsplit import SequenceSplitDecoder
+        decoder = SequenceSplitDecoder(cfg["B"], cfg["H"], cfg["DH"], device,
+                                       group=dist.group.WORLD if dist is not None else None)
 
     launches_per_step = 2
 
@@ -297,23 +292,12 @@ def run_ours(args) -> dict | None:
             _native.check(lib.kvq_lse_merge(po.data_ptr(), pm.data_ptr(), pl.data_ptr(), n_splits,
                                             rows, cfg["DH"], 0, out.data_ptr(), sp))
         else:
-            if ev is not None:
-                ev[0].record(stream)
-            _native.check(lib.kvq_decode_partial(a, lo_.data_ptr(), lm_.data_ptr(), ll_.data_ptr(),
-                                                 ws.data_ptr(), ws.numel(), sp))
-            if ev is not None:
-                ev[1].record(stream)
-            if dist is not None:
-                dist.all_gather_into_tensor(go, lo_)
-                dist.all_gather_into_tensor(gm, lm_)
-                dist.all_gather_into_tensor(gl, ll_)
-                src = (go, gm, gl, world)
-            else:
-                src = (lo_.view(1, rows, -1), lm_.view(1, -1), ll_.view(1, -1), 1)
-            _native.check(lib.kvq_lse_merge(src[0].data_ptr(), src[1].data_ptr(), src[2].data_ptr(),
-                                            src[3], rows, cfg["DH"], 0, out.data_ptr(), sp))
+            kw, ks, kb, vw, vs, vb = sets[i % n_sets]
+            decoder.step(q, kw, ks, kb, vw, vs, vb, nk, nv, bits=cfg["bits"], t_local=t_rows,
+                         out=out, partial_events=ev)
 
     if args.config == 5:
+        # partial (+ its local merge when split) and the cross-rank merge
         launches_per_step = (3 if n_splits > 1 else 2)
 
     sampler = ClockSampler(local)

@@ -221,11 +221,11 @@ cudaError_t launch_merge(const float* part_o, const float* part_m, const float* 
                          void* out, cudaStream_t stream) {
     const unsigned blocks = rows;
     if (out_dtype == KVQ_F16)
-        merge_kernel<__half, true><<<blocks, head_dim, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
+        merge_kernel<__half, true><<<blocks, MERGE_THREADS, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
                                                                head_dim, static_cast<__half*>(out),
                                                                nullptr, nullptr);
     else
-        merge_kernel<float, true><<<blocks, head_dim, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
+        merge_kernel<float, true><<<blocks, MERGE_THREADS, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
                                                               head_dim, static_cast<float*>(out),
                                                               nullptr, nullptr);
     return cudaGetLastError();
@@ -235,7 +235,7 @@ cudaError_t launch_merge_partial(const float* part_o, const float* part_m, const
                                  uint32_t n_parts, uint32_t rows, uint32_t head_dim,
                                  float* out_o, float* out_m, float* out_l, cudaStream_t stream) {
     const unsigned blocks = rows;
-    merge_kernel<float, false><<<blocks, head_dim, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
+    merge_kernel<float, false><<<blocks, MERGE_THREADS, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
                                                            head_dim, out_o, out_m, out_l);
     return cudaGetLastError();
 }
@@ -375,7 +375,8 @@ int kvq_lse_merge(const float* part_o, const float* part_m, const float* part_l,
     g_error.clear();
     if (!part_o || !part_m || !part_l || !out) return fail(KVQ_ERR_INVALID, "a pointer is NULL");
     if (n_parts == 0 || rows == 0 || head_dim == 0) return fail(KVQ_ERR_INVALID, "empty merge");
-    if (head_dim > 1024 || head_dim % 32) return fail(KVQ_ERR_INVALID, "head_dim %u: a multiple of 32 up to 1024", head_dim);
+    if (head_dim > kvq::MERGE_MAX_DH || head_dim % 32)
+        return fail(KVQ_ERR_INVALID, "head_dim %u: a multiple of 32 up to %d", head_dim, kvq::MERGE_MAX_DH);
     if (rows > 0x7FFFFFFFu) return fail(KVQ_ERR_INVALID, "too many rows");
     if (out_dtype != KVQ_F16 && out_dtype != KVQ_F32) return fail(KVQ_ERR_INVALID, "bad out_dtype");
     int rc = device_ok();

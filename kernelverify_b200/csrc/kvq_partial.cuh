@@ -227,36 +227,77 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
     }
 }
 
-// Log-sum-exp merge of n_parts partials: one block per row, one thread per
-// dim (blockDim.x == head_dim), so the partials' O rows are read coalesced
-// and the m / l of each part are one broadcast load per warp.
+// Log-sum-exp merge of n_parts partials, one 256-thread block per row: the
+// block's threads first take the max of the parts' m, then warp w sums the
+// parts w, w+8, ... (lane owns dims lane, lane+32, ...; each part's O row is
+// read coalesced) and the eight warp sums meet in shared memory. head_dim is
+// a multiple of 32, at most 256.
 // NORMALIZE: out = sum_p O_p e^(m_p - m) / l in TO. Otherwise the merged
 // partial (O unnormalised, m, l) in fp32.
+constexpr int MERGE_THREADS = 256;
+constexpr int MERGE_WARPS = MERGE_THREADS / 32;
+constexpr int MERGE_MAX_DH = 256;
+
 template <typename TO, bool NORMALIZE>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(MERGE_THREADS)
 merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
              const float* __restrict__ part_l, uint32_t n_parts, uint32_t rows,
              uint32_t head_dim, TO* __restrict__ out, float* __restrict__ out_m,
              float* __restrict__ out_l) {
+    __shared__ float s_max[MERGE_WARPS];
+    __shared__ float s_l[MERGE_WARPS];
+    __shared__ float s_o[MERGE_WARPS][MERGE_MAX_DH];
     const uint32_t row = blockIdx.x;
-    const uint32_t d = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
     float m = -INFINITY;
-    for (uint32_t p = 0; p < n_parts; ++p) m = fmaxf(m, part_m[(size_t)p * rows + row]);
-    float l = 0.0f, o = 0.0f;
-    for (uint32_t p = 0; p < n_parts; ++p) {
-        const float mp = part_m[(size_t)p * rows + row];
-        if (mp == -INFINITY) continue;
-        const float w = expf(mp - m);
-        l = fmaf(part_l[(size_t)p * rows + row], w, l);
-        o = fmaf(part_o[((size_t)p * rows + row) * head_dim + d], w, o);
+    for (uint32_t p = tid; p < n_parts; p += MERGE_THREADS) m = fmaxf(m, part_m[(size_t)p * rows + row]);
+    m = warp_max(m);
+    if (lane == 0) s_max[warp] = m;
+    __syncthreads();
+    m = s_max[0];
+#pragma unroll
+    for (int w = 1; w < MERGE_WARPS; ++w) m = fmaxf(m, s_max[w]);
+
+    const int per_lane = (int)head_dim / 32;
+    float acc[MERGE_MAX_DH / 32];
+#pragma unroll
+    for (int k = 0; k < MERGE_MAX_DH / 32; ++k) acc[k] = 0.0f;
+    float l = 0.0f;
+    if (m != -INFINITY) {
+        for (uint32_t p = warp; p < n_parts; p += MERGE_WARPS) {
+            const float mp = part_m[(size_t)p * rows + row];
+            if (mp == -INFINITY) continue;
+            const float w = expf(mp - m);
+            l = fmaf(part_l[(size_t)p * rows + row], w, l);
+            const float* o = part_o + ((size_t)p * rows + row) * head_dim + lane;
+#pragma unroll
+            for (int k = 0; k < MERGE_MAX_DH / 32; ++k)
+                if (k < per_lane) acc[k] = fmaf(o[32 * k], w, acc[k]);
+        }
     }
-    if constexpr (NORMALIZE) {
-        out[(size_t)row * head_dim + d] = from_f32<TO>(o / l);
-    } else {
-        out[(size_t)row * head_dim + d] = m == -INFINITY ? 0.0f : o;
-        if (d == 0) {
+#pragma unroll
+    for (int k = 0; k < MERGE_MAX_DH / 32; ++k)
+        if (k < per_lane) s_o[warp][lane + 32 * k] = acc[k];
+    if (lane == 0) s_l[warp] = l;
+    __syncthreads();
+    float lt = 0.0f;
+#pragma unroll
+    for (int w = 0; w < MERGE_WARPS; ++w) lt += s_l[w];
+    for (uint32_t d = tid; d < head_dim; d += MERGE_THREADS) {
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < MERGE_WARPS; ++w) o += s_o[w][d];
+        if constexpr (NORMALIZE) {
+            out[(size_t)row * head_dim + d] = from_f32<TO>(o / lt);
+        } else {
+            out[(size_t)row * head_dim + d] = m == -INFINITY ? 0.0f : o;
+        }
+    }
+    if constexpr (!NORMALIZE) {
+        if (tid == 0) {
             out_m[row] = m;
-            out_l[row] = l;
+            out_l[row] = lt;
         }
     }
 }
