@@ -17,10 +17,15 @@ on the data path).
 its shard's partial (O, m, l), the partials are all-gathered over NCCL and
 merged by log-sum-exp on every rank (strong scaling).
 
-Timing: W untimed warm-up steps, then exactly K steps between a barrier +
-cudaDeviceSynchronize on both sides, CUDA events on the launching stream, max
-over ranks. Cache sets rotate so that the bytes a step reads are never
-L2-resident (working set > 2 x 126 MB L2). rank 0 prints one JSON line.
+Timing: W untimed eager warm-up steps, then each cache set's step is captured
+as a CUDA graph (kernels, and for config 5 the all-gather) and exactly K graph
+replays are timed between a barrier + cudaDeviceSynchronize on both sides,
+CUDA events on the launching stream, max over ranks. The dominant kernel (the
+split stage) is then timed alone over K launches the same way (roofline).
+`e2e` repeats the step through the public Python API with pinned host inputs
+copied in and the result copied out every step. Cache sets rotate so that the
+bytes a step reads are never L2-resident (working set > 2 x 126 MB L2). rank 0
+prints one JSON line.
 
 --impl reference times the reference's own CPU implementation of the path
 (the numpy port of kv_attention in oracle/, including its canonical
@@ -271,78 +276,97 @@ def run_ours(args) -> dict | None:
     po = torch.empty((n_splits, rows, cfg["DH"]), dtype=torch.float32, device=device)
     pm = torch.empty((n_splits, rows), dtype=torch.float32, device=device)
     pl = torch.empty((n_splits, rows), dtype=torch.float32, device=device)
-    stream = torch.cuda.current_stream(device)
-    sp = stream.cuda_stream
 
     if args.config == 5:
         from kernelverify_b200.pack.tsplit import SequenceSplitDecoder
         decoder = SequenceSplitDecoder(cfg["B"], cfg["H"], cfg["DH"], device,
                                        group=dist.group.WORLD if dist is not None else None)
 
-    launches_per_step = 2
+    def splits(i):
+        """The dominant kernel alone: the split stage over cache set i."""
+        _native.check(lib.kvq_decode_splits(margs[i % n_sets], po.data_ptr(), pm.data_ptr(),
+                                            pl.data_ptr(), torch.cuda.current_stream().cuda_stream))
 
-    def step(i, ev=None):
-        a = margs[i % n_sets]
+    def eager_step(i):
         if args.config == 2:
-            if ev is not None:
-                ev[0].record(stream)
-            _native.check(lib.kvq_decode_splits(a, po.data_ptr(), pm.data_ptr(), pl.data_ptr(), sp))
-            if ev is not None:
-                ev[1].record(stream)
+            splits(i)
             _native.check(lib.kvq_lse_merge(po.data_ptr(), pm.data_ptr(), pl.data_ptr(), n_splits,
-                                            rows, cfg["DH"], 0, out.data_ptr(), sp))
+                                            rows, cfg["DH"], 0, out.data_ptr(),
+                                            torch.cuda.current_stream().cuda_stream))
         else:
             kw, ks, kb, vw, vs, vb = sets[i % n_sets]
             decoder.step(q, kw, ks, kb, vw, vs, vb, nk, nv, bits=cfg["bits"], t_local=t_rows,
-                         out=out, partial_events=ev)
+                         out=out)
 
-    if args.config == 5:
-        # partial (+ its local merge when split) and the cross-rank merge
-        launches_per_step = (3 if n_splits > 1 else 2)
+    # kernels of ours per step: partial + merge (config 2); partial, its local
+    # merge when split, and the cross-rank merge (config 5)
+    launches_per_step = 2 if args.config == 2 else (3 if n_splits > 1 else 2)
 
     sampler = ClockSampler(local)
     sampler.start()
     for i in range(args.warmup):
-        step(i)
+        eager_step(i)
     barrier(dist)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
+    # one CUDA graph per cache set: a replayed step makes no host calls
+    pool = torch.cuda.graph_pool_handle()
+    graphs = []
+    for i in range(n_sets):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=pool):
+            eager_step(i)
+        graphs.append(g)
+    for i in range(n_sets):
+        graphs[i].replay()
+    barrier(dist)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(dist)
+    stream = torch.cuda.current_stream(device)
     wall0 = time.time()
     e0.record(stream)
     for i in range(args.steps):
-        step(args.warmup + i, evs[i])
+        graphs[(args.warmup + i) % n_sets].replay()
     e1.record(stream)
     torch.cuda.synchronize()
     wall1 = time.time()
     barrier(dist)
+    # the dominant kernel timed alone over the same rotation of cache sets
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(3):
+        splits(i)
+    barrier(dist)
+    k0.record(stream)
+    for i in range(args.steps):
+        splits(args.warmup + i)
+    k1.record(stream)
+    torch.cuda.synchronize()
+    barrier(dist)
     clocks = sampler.stop(wall0, wall1)
     local_ms = e0.elapsed_time(e1) / args.steps
-    kern_ms = statistics.fmean(a.elapsed_time(b) for a, b in evs)
+    kern_ms = k0.elapsed_time(k1) / args.steps
     step_ms = max_over_ranks(local_ms, dist)
     kern_ms_max = max_over_ranks(kern_ms, dist)
+    del graphs     # the graphs hold NCCL work: release them before the group goes
 
     # ---- e2e through the public API: pinned host inputs in, result out -------
     e2e = None
-    if args.config == 2 and not args.no_e2e:
+    if not args.no_e2e:
         hq = q.cpu().pin_memory()
         hnk = nk.cpu().pin_memory()
         hnv = nv.cpu().pin_memory()
         hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
         dq, dnk, dnv = torch.empty_like(q), torch.empty_like(nk), torch.empty_like(nv)
-        e2e_args = []
-        for (kw, ks, kb, vw, vs, vb) in sets:
-            e2e_args.append((kw, ks, kb, vw, vs, vb))
         wsd = kva.Workspace()
 
         def e2e_step(i):
-            kw, ks, kb, vw, vs, vb = e2e_args[i % n_sets]
+            kw, ks, kb, vw, vs, vb = sets[i % n_sets]
             dq.copy_(hq, non_blocking=True)
             dnk.copy_(hnk, non_blocking=True)
             dnv.copy_(hnv, non_blocking=True)
-            res = kva.decode(dq, kw, ks, kb, vw, vs, vb, dnk, dnv, bits=cfg["bits"],
-                             t_cached=t_rows, out=out, workspace=wsd)
+            if args.config == 2:
+                res = kva.decode(dq, kw, ks, kb, vw, vs, vb, dnk, dnv, bits=cfg["bits"],
+                                 t_cached=t_rows, out=out, workspace=wsd)
+            else:
+                res = decoder.step(dq, kw, ks, kb, vw, vs, vb, dnk, dnv, bits=cfg["bits"],
+                                   t_local=t_rows, out=out)
             hout.copy_(res, non_blocking=True)
 
         for i in range(max(3, args.warmup)):
@@ -356,10 +380,14 @@ def run_ours(args) -> dict | None:
         torch.cuda.synchronize()
         e2e_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps, dist)
         h2d = hq.numel() * 2 + hnk.numel() * 2 + hnv.numel() * 2
-        e2e = {"value": round(world * step_kv / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+        total = world * step_kv if args.config == 2 else step_kv
+        e2e = {"value": round(total / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                "us_per_step": round(e2e_ms * 1e3, 2),
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": hout.numel() * 2,
-               "path": "kernelverify_b200.pack.kv_attention.decode -> kvq_decode (C ABI)"}
+               "path": ("kernelverify_b200.pack.kv_attention.decode -> kvq_decode (C ABI)"
+                        if args.config == 2 else
+                        "kernelverify_b200.pack.tsplit.SequenceSplitDecoder.step -> "
+                        "kvq_decode_partial, NCCL all-gather, kvq_lse_merge_records (C ABI)")}
 
     if rank != 0:
         if dist is not None:
@@ -400,7 +428,7 @@ def run_ours(args) -> dict | None:
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "peak_kind": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
-                     "kernel": "partial_kernel (kvq_decode_splits)",
+                     "kernel": "partial_kernel (kvq_decode_splits), timed alone",
                      "kernel_us": round(kern_ms_max * 1e3, 2),
                      "alg_bytes_per_launch": alg_kernel,
                      "traffic": profiled_traffic(traffic_key)},

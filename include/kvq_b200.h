@@ -140,6 +140,19 @@ int kvq_lse_merge(const float* part_o, const float* part_m, const float* part_l,
                   void* out, void* stream);
 
 /*
+ * A partial record: one shard's kvq_decode_partial output in one buffer of
+ * KVQ_RECORD_FLOATS(rows, head_dim) floats, O [rows, head_dim] first, then
+ * m [rows], then l [rows] (pass part_o = rec, part_m = rec + rows*head_dim,
+ * part_l = part_m + rows). An all-gather of every rank's record lays them end
+ * to end, and kvq_lse_merge_records merges them there: one collective per
+ * step instead of three. No reference counterpart (the reference has no
+ * multi-GPU path).
+ */
+#define KVQ_RECORD_FLOATS(rows, head_dim) ((size_t)(rows) * ((size_t)(head_dim) + 2))
+int kvq_lse_merge_records(const float* records, uint32_t n_parts, uint32_t rows,
+                          uint32_t head_dim, uint32_t out_dtype, void* out, void* stream);
+
+/*
  * fp32 dequantized values [rows, head_dim] of a packed artefact: scale * code
  * + bias per group, a rounded multiply then a rounded add -- bit-exact to the
  * reference's _cache_dequant (kernelverify/reference/native_kernels.py:153-165,

@@ -21,7 +21,7 @@ KVQ_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 # Every symbol include/kvq_b200.h declares.
 EXPORTS = ("kvq_workspace_bytes", "kvq_decode", "kvq_decode_partial", "kvq_split_count",
-           "kvq_decode_splits", "kvq_lse_merge", "kvq_decode_noalloc",
+           "kvq_decode_splits", "kvq_lse_merge", "kvq_lse_merge_records", "kvq_decode_noalloc",
            "kvq_dequant", "kvq_quantize", "kvq_supports", "kvq_last_error", "kvq_abi_version")
 
 
@@ -67,6 +67,7 @@ def _declare(lib) -> None:
         "kvq_split_count": (U32, [AP]),
         "kvq_decode_splits": (I, [AP, P, P, P, P]),
         "kvq_lse_merge": (I, [P, P, P, U32, U32, U32, U32, P, P]),
+        "kvq_lse_merge_records": (I, [P, U32, U32, U32, U32, P, P]),
         "kvq_decode_noalloc": (I, [AP, P, P]),
         "kvq_dequant": (I, [P, P, P, U64, U32, U32, U32, U32, P, P]),
         "kvq_quantize": (I, [P, U64, U32, U32, U32, U32, P, P, P, P]),

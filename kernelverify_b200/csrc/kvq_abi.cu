@@ -81,6 +81,45 @@ bool generic_forced() {
     return v != nullptr && strcmp(v, "generic") == 0;
 }
 
+// Split plan of the tensor-core kernel. Its CTAs run in waves of the resident
+// CTAs (per SM x SMs); a CTA costs its chunk of positions plus a fixed ramp
+// (barrier setup, the first copies' latency, the epilogue) worth about two
+// 64-position stages. Of the split counts that fill 1..8 whole waves, take the
+// one whose waves x (chunk + ramp) is least. Chunks are whole 64-row stages.
+constexpr uint64_t kMmaStage = 64;
+constexpr uint64_t kMmaRamp = 128;
+
+void mma4_splits(uint64_t span, uint64_t units, int ctas_per_sm, uint32_t* chunk_out,
+                 uint32_t* splits_out) {
+    const uint64_t resident = (uint64_t)ctas_per_sm * kvq::sm_count();
+    const auto round_stage = [](uint64_t n) {
+        n = (n + kMmaStage - 1) / kMmaStage * kMmaStage;
+        return n < kMmaStage ? kMmaStage : n;
+    };
+    uint64_t best_chunk = round_stage(span), best_splits = 1;
+    uint64_t best_cost = ((units + resident - 1) / resident) * (best_chunk + kMmaRamp);
+    for (uint64_t waves = 1; span && waves <= 8; ++waves) {
+        const uint64_t fit = waves * resident / units;
+        if (fit <= 1) continue;
+        const uint64_t chunk = round_stage((span + fit - 1) / fit);
+        const uint64_t splits = (span + chunk - 1) / chunk;
+        if (splits > kMaxSplits) break;
+        const uint64_t cost = ((units * splits + resident - 1) / resident) * (chunk + kMmaRamp);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best_chunk = chunk;
+            best_splits = splits;
+        }
+    }
+    constexpr uint64_t kMaxChunk = 0xFFFFFFFFull / kMmaStage * kMmaStage;
+    if (best_chunk > kMaxChunk) {
+        best_chunk = kMaxChunk;
+        best_splits = (span + best_chunk - 1) / best_chunk;
+    }
+    *chunk_out = (uint32_t)best_chunk;
+    *splits_out = (uint32_t)best_splits;
+}
+
 struct Plan {
     kvq::Problem P;
     int kernel;
@@ -147,6 +186,13 @@ int plan(const kvq_args* a, Plan* pl) {
     const uint32_t end = a->t_end < a->t_cached ? a->t_end : a->t_cached;
     const uint64_t span = end > a->t_begin ? end - a->t_begin : 0;
     const uint64_t units = (uint64_t)a->b_rows * a->n_kv_heads * P.head_tiles;
+    pl->rows = a->b_rows * a->n_heads;
+    if (pl->kernel == KERNEL_MMA4) {
+        mma4_splits(span, units, kvq::mma4_ctas_per_sm(pl->ht, a->group_size), &P.chunk, &P.n_splits);
+        pl->part_bytes = align_up((size_t)P.n_splits * pl->rows * a->head_dim * sizeof(float));
+        pl->ml_bytes = align_up((size_t)P.n_splits * pl->rows * sizeof(float));
+        return KVQ_OK;
+    }
     uint64_t chunk = (span * units + kTargetCtas - 1) / kTargetCtas;
     const uint64_t tile = kvq::P_TILE;
     chunk = (chunk + tile - 1) / tile * tile;
@@ -158,7 +204,6 @@ int plan(const kvq_args* a, Plan* pl) {
     }
     P.chunk = (uint32_t)chunk;
     P.n_splits = (uint32_t)splits;
-    pl->rows = a->b_rows * a->n_heads;
     pl->part_bytes = align_up((size_t)P.n_splits * pl->rows * a->head_dim * sizeof(float));
     pl->ml_bytes = align_up((size_t)P.n_splits * pl->rows * sizeof(float));
     return KVQ_OK;
@@ -182,6 +227,17 @@ int check_workspace(const void* ws, size_t have, size_t need) {
     if (ws == nullptr || have < need)
         return fail(KVQ_ERR_INVALID, "workspace of %zu bytes is smaller than the %zu this call needs", have, need);
     if (!aligned(ws, kAlign)) return fail(KVQ_ERR_INVALID, "workspace is not 256-byte aligned");
+    return KVQ_OK;
+}
+
+int check_merge(uint32_t n_parts, uint32_t rows, uint32_t head_dim, uint32_t out_dtype) {
+    if (n_parts == 0 || rows == 0 || head_dim == 0) return fail(KVQ_ERR_INVALID, "empty merge");
+    if (n_parts > (uint32_t)kvq::MERGE_MAX_PARTS)
+        return fail(KVQ_ERR_INVALID, "%u parts: at most %d", n_parts, kvq::MERGE_MAX_PARTS);
+    if (head_dim > kvq::MERGE_MAX_DH || head_dim % 32)
+        return fail(KVQ_ERR_INVALID, "head_dim %u: a multiple of 32 up to %d", head_dim, kvq::MERGE_MAX_DH);
+    if (rows > 0x7FFFFFFFu) return fail(KVQ_ERR_INVALID, "too many rows");
+    if (out_dtype != KVQ_F16 && out_dtype != KVQ_F32) return fail(KVQ_ERR_INVALID, "bad out_dtype");
     return KVQ_OK;
 }
 
@@ -217,17 +273,17 @@ int noalloc_scratch(void** out) {
 namespace kvq {
 
 cudaError_t launch_merge(const float* part_o, const float* part_m, const float* part_l,
-                         uint32_t n_parts, uint32_t rows, uint32_t head_dim, int out_dtype,
-                         void* out, cudaStream_t stream) {
+                         uint32_t n_parts, uint32_t rows, uint32_t head_dim, uint64_t o_stride,
+                         uint64_t ml_stride, int out_dtype, void* out, cudaStream_t stream) {
     const unsigned blocks = rows;
     if (out_dtype == KVQ_F16)
-        merge_kernel<__half, true><<<blocks, MERGE_THREADS, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
-                                                               head_dim, static_cast<__half*>(out),
-                                                               nullptr, nullptr);
+        merge_kernel<__half, true><<<blocks, MERGE_THREADS, 0, stream>>>(
+            part_o, part_m, part_l, n_parts, rows, head_dim, o_stride, ml_stride,
+            static_cast<__half*>(out), nullptr, nullptr);
     else
-        merge_kernel<float, true><<<blocks, MERGE_THREADS, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
-                                                              head_dim, static_cast<float*>(out),
-                                                              nullptr, nullptr);
+        merge_kernel<float, true><<<blocks, MERGE_THREADS, 0, stream>>>(
+            part_o, part_m, part_l, n_parts, rows, head_dim, o_stride, ml_stride,
+            static_cast<float*>(out), nullptr, nullptr);
     return cudaGetLastError();
 }
 
@@ -235,8 +291,9 @@ cudaError_t launch_merge_partial(const float* part_o, const float* part_m, const
                                  uint32_t n_parts, uint32_t rows, uint32_t head_dim,
                                  float* out_o, float* out_m, float* out_l, cudaStream_t stream) {
     const unsigned blocks = rows;
-    merge_kernel<float, false><<<blocks, MERGE_THREADS, 0, stream>>>(part_o, part_m, part_l, n_parts, rows,
-                                                           head_dim, out_o, out_m, out_l);
+    merge_kernel<float, false><<<blocks, MERGE_THREADS, 0, stream>>>(
+        part_o, part_m, part_l, n_parts, rows, head_dim, (uint64_t)rows * head_dim, rows, out_o,
+        out_m, out_l);
     return cudaGetLastError();
 }
 
@@ -279,7 +336,8 @@ int kvq_decode(const kvq_args* a, void* out, void* workspace, size_t workspace_b
     float* pll = reinterpret_cast<float*>(ws + pl.part_bytes + pl.ml_bytes);
     cudaError_t e = launch_partial_any(pl, a->bits, a->dtype, a->head_dim, po, pm, pll, s);
     if (e != cudaSuccess) return cuda_fail(e, "partial kernel launch");
-    e = kvq::launch_merge(po, pm, pll, pl.P.n_splits, pl.rows, a->head_dim, (int)a->dtype, out, s);
+    e = kvq::launch_merge(po, pm, pll, pl.P.n_splits, pl.rows, a->head_dim,
+                          (uint64_t)pl.rows * a->head_dim, pl.rows, (int)a->dtype, out, s);
     if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
     return KVQ_OK;
 }
@@ -309,7 +367,8 @@ int kvq_decode_noalloc(const kvq_args* a, void* out, void* stream) {
     float* pll = reinterpret_cast<float*>(ws + pl.part_bytes + pl.ml_bytes);
     cudaError_t e = launch_partial_any(pl, a->bits, a->dtype, a->head_dim, po, pm, pll, s);
     if (e != cudaSuccess) return cuda_fail(e, "partial kernel launch");
-    e = kvq::launch_merge(po, pm, pll, pl.P.n_splits, pl.rows, a->head_dim, (int)a->dtype, out, s);
+    e = kvq::launch_merge(po, pm, pll, pl.P.n_splits, pl.rows, a->head_dim,
+                          (uint64_t)pl.rows * a->head_dim, pl.rows, (int)a->dtype, out, s);
     if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
     return KVQ_OK;
 }
@@ -374,15 +433,30 @@ int kvq_lse_merge(const float* part_o, const float* part_m, const float* part_l,
                   uint32_t rows, uint32_t head_dim, uint32_t out_dtype, void* out, void* stream) {
     g_error.clear();
     if (!part_o || !part_m || !part_l || !out) return fail(KVQ_ERR_INVALID, "a pointer is NULL");
-    if (n_parts == 0 || rows == 0 || head_dim == 0) return fail(KVQ_ERR_INVALID, "empty merge");
-    if (head_dim > kvq::MERGE_MAX_DH || head_dim % 32)
-        return fail(KVQ_ERR_INVALID, "head_dim %u: a multiple of 32 up to %d", head_dim, kvq::MERGE_MAX_DH);
-    if (rows > 0x7FFFFFFFu) return fail(KVQ_ERR_INVALID, "too many rows");
-    if (out_dtype != KVQ_F16 && out_dtype != KVQ_F32) return fail(KVQ_ERR_INVALID, "bad out_dtype");
-    int rc = device_ok();
+    int rc = check_merge(n_parts, rows, head_dim, out_dtype);
     if (rc) return rc;
-    cudaError_t e = kvq::launch_merge(part_o, part_m, part_l, n_parts, rows, head_dim, (int)out_dtype,
-                                      out, static_cast<cudaStream_t>(stream));
+    rc = device_ok();
+    if (rc) return rc;
+    cudaError_t e = kvq::launch_merge(part_o, part_m, part_l, n_parts, rows, head_dim,
+                                      (uint64_t)rows * head_dim, rows, (int)out_dtype, out,
+                                      static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
+    return KVQ_OK;
+}
+
+int kvq_lse_merge_records(const float* records, uint32_t n_parts, uint32_t rows, uint32_t head_dim,
+                          uint32_t out_dtype, void* out, void* stream) {
+    g_error.clear();
+    if (!records || !out) return fail(KVQ_ERR_INVALID, "a pointer is NULL");
+    if (!aligned(records, 4)) return fail(KVQ_ERR_INVALID, "records must be 4-byte aligned");
+    int rc = check_merge(n_parts, rows, head_dim, out_dtype);
+    if (rc) return rc;
+    rc = device_ok();
+    if (rc) return rc;
+    const uint64_t rec = (uint64_t)rows * (head_dim + 2);
+    const float* m = records + (size_t)rows * head_dim;
+    cudaError_t e = kvq::launch_merge(records, m, m + rows, n_parts, rows, head_dim, rec, rec,
+                                      (int)out_dtype, out, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
     return KVQ_OK;
 }

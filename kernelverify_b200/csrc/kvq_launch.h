@@ -30,12 +30,21 @@ cudaError_t launch_dequant(const uint32_t* wq, const void* scales, const void* b
 cudaError_t launch_mma4(const Problem& P, int ht, int group, float* part_o, float* part_m,
                         float* part_l, cudaStream_t stream);
 
+// Merges of n_parts partials; part p's O block starts o_stride floats after
+// part p-1's, its m and l ml_stride floats after (stacked partials:
+// o_stride = rows * head_dim, ml_stride = rows).
 cudaError_t launch_merge(const float* part_o, const float* part_m, const float* part_l,
-                         uint32_t n_parts, uint32_t rows, uint32_t head_dim, int out_dtype,
-                         void* out, cudaStream_t stream);
+                         uint32_t n_parts, uint32_t rows, uint32_t head_dim, uint64_t o_stride,
+                         uint64_t ml_stride, int out_dtype, void* out, cudaStream_t stream);
 
 cudaError_t launch_merge_partial(const float* part_o, const float* part_m, const float* part_l,
                                  uint32_t n_parts, uint32_t rows, uint32_t head_dim,
                                  float* out_o, float* out_m, float* out_l, cudaStream_t stream);
+
+// Resident tensor-core CTAs per SM for (ht, group) on the current device,
+// and the device's SM count (both cached per device; fixed fallbacks when the
+// device cannot be queried).
+int mma4_ctas_per_sm(int ht, int group);
+int sm_count();
 
 }  // namespace kvq

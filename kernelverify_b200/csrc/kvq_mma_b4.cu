@@ -1,22 +1,88 @@
 // Tensor-core partial kernels (fp16 steps, 4-bit caches, head_dim 128).
+#include <atomic>
+
 #include "kvq_launch.h"
 #include "kvq_mma.cuh"
 
 namespace kvq {
 
+constexpr int kMaxDevices = 64;
+
+// The kernel's attributes (dynamic shared memory above 48 KB; a carveout that
+// prefers shared memory, so three CTAs fit on an SM), set once per device so
+// that later launches, captured ones included, make no attribute calls.
 template <int HT, int GROUP>
-static cudaError_t mma4_one(const Problem& P, float* o, float* m, float* l, cudaStream_t stream) {
-    constexpr size_t smem = mma4::smem_bytes<GROUP>();
-    auto kernel = mma4::partial_kernel<HT, GROUP>;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+static cudaError_t mma4_prepare() {
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    // prefer shared memory over L1 so three CTAs fit on an SM
+    const uint64_t bit = dev >= 0 && dev < kMaxDevices ? 1ull << dev : 0;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    auto kernel = mma4::partial_kernel<HT, GROUP>;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)mma4::smem_bytes<GROUP>());
+    if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+    return cudaSuccess;
+}
+
+template <int HT, int GROUP>
+static cudaError_t mma4_one(const Problem& P, float* o, float* m, float* l, cudaStream_t stream) {
+    cudaError_t e = mma4_prepare<HT, GROUP>();
+    if (e != cudaSuccess) return e;
     dim3 grid(P.n_splits, P.n_kv_heads * P.head_tiles, P.b_rows);
-    kernel<<<grid, mma4::THREADS, smem, stream>>>(P, o, m, l);
+    mma4::partial_kernel<HT, GROUP><<<grid, mma4::THREADS, mma4::smem_bytes<GROUP>(), stream>>>(P, o, m, l);
     return cudaGetLastError();
+}
+
+template <int HT, int GROUP>
+static int mma4_occupancy() {
+    static std::atomic<int> cached[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (n > 0) return n;
+    if (mma4_prepare<HT, GROUP>() != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, mma4::partial_kernel<HT, GROUP>,
+                                                      mma4::THREADS,
+                                                      mma4::smem_bytes<GROUP>()) != cudaSuccess)
+        return 0;
+    cached[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
+
+int mma4_ctas_per_sm(int ht, int group) {
+    int n = 0;
+    if (ht == 4)
+        n = group == 32 ? mma4_occupancy<4, 32>() : group == 64 ? mma4_occupancy<4, 64>() : mma4_occupancy<4, 128>();
+    else
+        n = group == 32 ? mma4_occupancy<8, 32>() : group == 64 ? mma4_occupancy<8, 64>() : mma4_occupancy<8, 128>();
+    if (n <= 0) {
+        cudaGetLastError();  // a failed query leaves no error behind
+        n = group == 32 ? 2 : 3;
+    }
+    return n;
+}
+
+int sm_count() {
+    static std::atomic<int> cached[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return 148;
+    }
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (n > 0) return n;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return 148;
+    }
+    cached[dev].store(n, std::memory_order_relaxed);
+    return n;
 }
 
 cudaError_t launch_mma4(const Problem& P, int ht, int group, float* o, float* m, float* l,

@@ -227,63 +227,92 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
     }
 }
 
-// Log-sum-exp merge of n_parts partials, one 256-thread block per row: the
-// block's threads first take the max of the parts' m, then warp w sums the
-// parts w, w+8, ... (lane owns dims lane, lane+32, ...; each part's O row is
-// read coalesced) and the eight warp sums meet in shared memory. head_dim is
-// a multiple of 32, at most 256.
+// Log-sum-exp merge of n_parts partials, one 256-thread block per row.
+// Part p's O row starts at part_o + p * o_stride + row * head_dim and its m, l
+// at part_m / part_l + p * ml_stride + row, so stacked partials ([P, rows, DH]
+// and [P, rows]) and partial records laid end to end are both served.
+// Phase 1 stages the parts' m in shared memory and takes their max; phase 2
+// turns them into weights e^(m_p - m) there and sums l; phase 3 has warp w sum
+// the parts w, w+8, ... (lane owns dims lane, lane+32, ...), four parts' loads
+// in flight at a time with no load waiting on another, and the eight warp sums
+// meet in shared memory. head_dim is a multiple of 32, at most 256; n_parts at
+// most MERGE_MAX_PARTS.
 // NORMALIZE: out = sum_p O_p e^(m_p - m) / l in TO. Otherwise the merged
-// partial (O unnormalised, m, l) in fp32.
+// partial (O unnormalised, m, l) in fp32. A part with m = -inf (an empty
+// range) adds nothing; a NaN m (a poisoned partial) makes the row NaN.
 constexpr int MERGE_THREADS = 256;
 constexpr int MERGE_WARPS = MERGE_THREADS / 32;
 constexpr int MERGE_MAX_DH = 256;
+constexpr int MERGE_MAX_PARTS = 4096;
+constexpr int MERGE_UNROLL = 4;
 
 template <typename TO, bool NORMALIZE>
 __global__ void __launch_bounds__(MERGE_THREADS)
 merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
              const float* __restrict__ part_l, uint32_t n_parts, uint32_t rows,
-             uint32_t head_dim, TO* __restrict__ out, float* __restrict__ out_m,
-             float* __restrict__ out_l) {
-    __shared__ float s_max[MERGE_WARPS];
-    __shared__ float s_l[MERGE_WARPS];
+             uint32_t head_dim, uint64_t o_stride, uint64_t ml_stride, TO* __restrict__ out,
+             float* __restrict__ out_m, float* __restrict__ out_l) {
+    __shared__ float s_w[MERGE_MAX_PARTS];
+    __shared__ float s_red[2][MERGE_WARPS];
     __shared__ float s_o[MERGE_WARPS][MERGE_MAX_DH];
     const uint32_t row = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     float m = -INFINITY;
-    for (uint32_t p = tid; p < n_parts; p += MERGE_THREADS) m = fmaxf(m, part_m[(size_t)p * rows + row]);
+    for (uint32_t p = tid; p < n_parts; p += MERGE_THREADS) {
+        const float v = part_m[p * ml_stride + row];
+        s_w[p] = v;
+        m = fmaxf(m, v);
+    }
     m = warp_max(m);
-    if (lane == 0) s_max[warp] = m;
+    if (lane == 0) s_red[0][warp] = m;
     __syncthreads();
-    m = s_max[0];
+    m = s_red[0][0];
 #pragma unroll
-    for (int w = 1; w < MERGE_WARPS; ++w) m = fmaxf(m, s_max[w]);
+    for (int w = 1; w < MERGE_WARPS; ++w) m = fmaxf(m, s_red[0][w]);
+
+    // each thread rewrites only the entries it staged, so no barrier between
+    float l = 0.0f;
+    for (uint32_t p = tid; p < n_parts; p += MERGE_THREADS) {
+        const float v = s_w[p];
+        const float w = v == -INFINITY ? 0.0f : expf(v - m);
+        s_w[p] = w;
+        if (w != 0.0f) l = fmaf(part_l[p * ml_stride + row], w, l);
+    }
+    l = warp_sum(l);
+    if (lane == 0) s_red[1][warp] = l;
+    __syncthreads();
+    float lt = 0.0f;
+#pragma unroll
+    for (int w = 0; w < MERGE_WARPS; ++w) lt += s_red[1][w];
 
     const int per_lane = (int)head_dim / 32;
+    const float* orow = part_o + (size_t)row * head_dim + lane;
     float acc[MERGE_MAX_DH / 32];
 #pragma unroll
     for (int k = 0; k < MERGE_MAX_DH / 32; ++k) acc[k] = 0.0f;
-    float l = 0.0f;
-    if (m != -INFINITY) {
-        for (uint32_t p = warp; p < n_parts; p += MERGE_WARPS) {
-            const float mp = part_m[(size_t)p * rows + row];
-            if (mp == -INFINITY) continue;
-            const float w = expf(mp - m);
-            l = fmaf(part_l[(size_t)p * rows + row], w, l);
-            const float* o = part_o + ((size_t)p * rows + row) * head_dim + lane;
+    for (uint32_t p0 = warp; p0 < n_parts; p0 += MERGE_WARPS * MERGE_UNROLL) {
+        float wv[MERGE_UNROLL];
+        float ov[MERGE_UNROLL][MERGE_MAX_DH / 32];
+#pragma unroll
+        for (int j = 0; j < MERGE_UNROLL; ++j) {
+            const uint32_t p = p0 + j * MERGE_WARPS;
+            wv[j] = p < n_parts ? s_w[p] : 0.0f;
+            const float* o = orow + p * o_stride;
 #pragma unroll
             for (int k = 0; k < MERGE_MAX_DH / 32; ++k)
-                if (k < per_lane) acc[k] = fmaf(o[32 * k], w, acc[k]);
+                ov[j][k] = (k < per_lane && wv[j] != 0.0f) ? o[32 * k] : 0.0f;
         }
+#pragma unroll
+        for (int j = 0; j < MERGE_UNROLL; ++j)
+#pragma unroll
+            for (int k = 0; k < MERGE_MAX_DH / 32; ++k)
+                if (wv[j] != 0.0f) acc[k] = fmaf(ov[j][k], wv[j], acc[k]);
     }
 #pragma unroll
     for (int k = 0; k < MERGE_MAX_DH / 32; ++k)
         if (k < per_lane) s_o[warp][lane + 32 * k] = acc[k];
-    if (lane == 0) s_l[warp] = l;
     __syncthreads();
-    float lt = 0.0f;
-#pragma unroll
-    for (int w = 0; w < MERGE_WARPS; ++w) lt += s_l[w];
     for (uint32_t d = tid; d < head_dim; d += MERGE_THREADS) {
         float o = 0.0f;
 #pragma unroll

@@ -253,6 +253,42 @@ def lse_merge(part_o, part_m, part_l, out_dtype, out=None, stream=None):
     return out
 
 
+def record_floats(rows: int, head_dim: int) -> int:
+    """Floats in one partial record: O [rows, DH], then m [rows], then l [rows]."""
+    return rows * (head_dim + 2)
+
+
+def record_views(record, b_rows: int, n_heads: int, head_dim: int):
+    """(part_o [B, H, DH], part_m [B, H], part_l [B, H]) views into one fp32
+    partial record, for `decode_partial` to write in place."""
+    rows = b_rows * n_heads
+    if record.dtype != _torch().float32 or record.numel() != record_floats(rows, head_dim):
+        raise ValueError(f"a record of {rows} rows x DH {head_dim} is "
+                         f"{record_floats(rows, head_dim)} fp32 values")
+    o = record[:rows * head_dim].view(b_rows, n_heads, head_dim)
+    m = record[rows * head_dim:rows * (head_dim + 1)].view(b_rows, n_heads)
+    l = record[rows * (head_dim + 1):].view(b_rows, n_heads)
+    return o, m, l
+
+
+def lse_merge_records(records, b_rows: int, n_heads: int, head_dim: int, out_dtype, out=None,
+                      stream=None):
+    """Merge partial records laid end to end (records [P, record_floats]) --
+    what an all-gather of every rank's record produces -- into out [B, H, DH]."""
+    torch = _torch()
+    rows = b_rows * n_heads
+    if (records.dim() != 2 or records.shape[1] != record_floats(rows, head_dim)
+            or records.dtype != torch.float32 or not records.is_contiguous()):
+        raise ValueError(f"records must be contiguous fp32 [P, {record_floats(rows, head_dim)}]")
+    if out is None:
+        out = torch.empty((b_rows, n_heads, head_dim), dtype=out_dtype, device=records.device)
+    s = stream if stream is not None else torch.cuda.current_stream(records.device)
+    _native.check(_native.lib().kvq_lse_merge_records(records.data_ptr(), records.shape[0], rows,
+                                                      head_dim, _dtype_code(out_dtype),
+                                                      out.data_ptr(), s.cuda_stream))
+    return out
+
+
 def quantize(w, bits: int, group_size: int = 64, stream=None):
     """Canonical quantizer on the device: w [..., DH] (fp16/fp32, contiguous)
     -> (words uint32-as-int32 [..., DH*bits/32], scales [..., DH/g], biases)."""

@@ -45,7 +45,9 @@ class SequenceSplitDecoder:
 
     `group` is a torch.distributed process group (None: a single rank). The
     local cache tensors hold only this rank's rows ([HKV, T_local, ...] or
-    [B, HKV, T_local, ...]); positions are local to them.
+    [B, HKV, T_local, ...]); positions are local to them. Each rank's partial
+    lands in one fp32 record (O, then m, then l), so a step makes one
+    all-gather; `capture` records a whole step as a CUDA graph.
     """
 
     b_rows: int
@@ -56,48 +58,50 @@ class SequenceSplitDecoder:
 
     def __post_init__(self):
         import torch
+        from kernelverify_b200.pack.kv_attention import Workspace, record_floats, record_views
         self.world = 1 if self.group is None else torch.distributed.get_world_size(self.group)
         self.rank = 0 if self.group is None else torch.distributed.get_rank(self.group)
-        rows = self.b_rows * self.n_heads
-        f32 = dict(dtype=torch.float32, device=self.device)
-        self.part_o = torch.empty((rows, self.head_dim), **f32)
-        self.part_m = torch.empty((rows,), **f32)
-        self.part_l = torch.empty((rows,), **f32)
-        self.all_o = torch.empty((self.world, rows, self.head_dim), **f32)
-        self.all_m = torch.empty((self.world, rows), **f32)
-        self.all_l = torch.empty((self.world, rows), **f32)
-        from kernelverify_b200.pack.kv_attention import Workspace
+        n = record_floats(self.b_rows * self.n_heads, self.head_dim)
+        self.records = torch.empty((self.world, n), dtype=torch.float32, device=self.device)
+        self.record = torch.empty((n,), dtype=torch.float32, device=self.device)
+        self.part_o, self.part_m, self.part_l = record_views(self.record, self.b_rows,
+                                                             self.n_heads, self.head_dim)
         self.workspace = Workspace()
 
-    def step(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
-             bits: int, t_local: int, out=None, partial_events=None):
-        """out [B, H, DH] in q's dtype, identical on every rank.
-        `partial_events`, a (start, stop) pair of CUDA events, brackets the
-        local partial on the current stream (for timing it alone)."""
-        import torch
+    def partial(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
+                bits: int, t_local: int):
+        """This rank's partial into its record (the local step alone)."""
         from kernelverify_b200.pack import kv_attention as kva
-
-        if partial_events is not None:
-            partial_events[0].record()
         kva.decode_partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
                            bits=bits, t_begin=0, t_end=t_local, t_cached=t_local,
                            has_new_entry=owns_new_entry(self.world, self.rank),
-                           part_o=self.part_o.view(self.b_rows, self.n_heads, self.head_dim),
-                           part_m=self.part_m.view(self.b_rows, self.n_heads),
-                           part_l=self.part_l.view(self.b_rows, self.n_heads),
+                           part_o=self.part_o, part_m=self.part_m, part_l=self.part_l,
                            workspace=self.workspace)
-        if partial_events is not None:
-            partial_events[1].record()
+
+    def step(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
+             bits: int, t_local: int, out=None):
+        """out [B, H, DH] in q's dtype, identical on every rank."""
+        import torch
+        from kernelverify_b200.pack import kv_attention as kva
+
+        self.partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
+                     bits=bits, t_local=t_local)
         if self.group is None:
-            self.all_o[0].copy_(self.part_o)
-            self.all_m[0].copy_(self.part_m)
-            self.all_l[0].copy_(self.part_l)
+            self.records[0].copy_(self.record)
         else:
-            dist = torch.distributed
-            dist.all_gather_into_tensor(self.all_o, self.part_o, group=self.group)
-            dist.all_gather_into_tensor(self.all_m, self.part_m, group=self.group)
-            dist.all_gather_into_tensor(self.all_l, self.part_l, group=self.group)
-        return kva.lse_merge(self.all_o.view(self.world, self.b_rows, self.n_heads, self.head_dim),
-                             self.all_m.view(self.world, self.b_rows, self.n_heads),
-                             self.all_l.view(self.world, self.b_rows, self.n_heads),
-                             q.dtype, out=out)
+            torch.distributed.all_gather_into_tensor(self.records, self.record, group=self.group)
+        return kva.lse_merge_records(self.records, self.b_rows, self.n_heads, self.head_dim,
+                                     q.dtype, out=out)
+
+    def capture(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
+                bits: int, t_local: int, out, pool=None):
+        """A CUDA graph of one `step` on these tensors (partial, all-gather,
+        merge); `graph.replay()` reruns it on whatever they then hold. Run one
+        eager `step` first (it creates the communicator and sets the kernels'
+        attributes). Drop the graph before destroying the process group."""
+        import torch
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, pool=pool):
+            self.step(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
+                      bits=bits, t_local=t_local, out=out)
+        return graph

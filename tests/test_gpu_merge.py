@@ -1,0 +1,112 @@
+"""The log-sum-exp merges on a B200: stacked partials and partial records give
+the same bits, the merge against an fp64 restatement of its formula, empty
+(m = -inf) and poisoned (NaN) parts, the part-count bound, and the
+sequence-split decoder on one rank -- eager, and replayed from a CUDA graph."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import cases, kv
+
+pytestmark = pytest.mark.gpu
+
+
+def _partials(n_parts, rows, dh, seed, empty=()):
+    rng = np.random.default_rng(seed)
+    o = rng.standard_normal((n_parts, rows, dh)).astype(np.float32)
+    m = (rng.standard_normal((n_parts, rows)) * 4).astype(np.float32)
+    l = rng.uniform(0.5, 40.0, (n_parts, rows)).astype(np.float32)
+    for p in empty:
+        o[p] = 0.0
+        m[p] = -np.inf
+        l[p] = 0.0
+    return o, m, l
+
+
+def _merge64(o, m, l):
+    mm = m.max(axis=0)
+    w = np.where(np.isneginf(m), 0.0, np.exp(m.astype(np.float64) - mm))
+    return (o * w[..., None]).sum(axis=0) / (l * w).sum(axis=0)[..., None]
+
+
+def _records(torch, o, m, l):
+    n, rows, dh = o.shape
+    rec = np.concatenate([o.reshape(n, -1), m, l], axis=1)
+    assert rec.shape[1] == rows * (dh + 2)
+    return torch.from_numpy(np.ascontiguousarray(rec)).cuda()
+
+
+@pytest.mark.parametrize("n_parts,rows,dh", [(1, 3, 64), (2, 64, 128), (8, 64, 128),
+                                             (54, 64, 128), (129, 17, 128), (4096, 2, 64)])
+def test_records_and_stacked_merge_agree_bitwise(native, n_parts, rows, dh):
+    import torch
+    from kernelverify_b200.pack import kv_attention as kva
+    o, m, l = _partials(n_parts, rows, dh, seed=n_parts + rows)
+    stacked = kva.lse_merge(torch.from_numpy(o).cuda().view(n_parts, 1, rows, dh),
+                            torch.from_numpy(m).cuda().view(n_parts, 1, rows),
+                            torch.from_numpy(l).cuda().view(n_parts, 1, rows), torch.float32)
+    recs = kva.lse_merge_records(_records(torch, o, m, l), 1, rows, dh, torch.float32)
+    assert torch.equal(stacked, recs)
+    ref = _merge64(o, m, l)
+    got = recs.cpu().numpy().reshape(rows, dh)
+    assert np.max(np.abs(got - ref)) <= 1e-4 * max(1.0, np.max(np.abs(ref)))
+
+
+def test_empty_parts_add_nothing_and_nan_parts_poison(native):
+    import torch
+    from kernelverify_b200.pack import kv_attention as kva
+    o, m, l = _partials(6, 4, 128, seed=3, empty=(0, 4))
+    got = kva.lse_merge_records(_records(torch, o, m, l), 1, 4, 128, torch.float32).cpu().numpy()
+    keep = [1, 2, 3, 5]
+    ref = _merge64(o[keep], m[keep], l[keep])
+    assert np.max(np.abs(got.reshape(4, 128) - ref)) <= 1e-5 * max(1.0, np.max(np.abs(ref)))
+    m[2, 1] = np.nan
+    bad = kva.lse_merge_records(_records(torch, o, m, l), 1, 4, 128, torch.float32).cpu().numpy()
+    bad = bad.reshape(4, 128)
+    assert np.isnan(bad[1]).all()
+    assert np.isfinite(bad[[0, 2, 3]]).all()
+
+
+def test_merge_rejects_more_parts_than_it_holds(native):
+    import torch
+    from kernelverify_b200._native import KvqError
+    from kernelverify_b200.pack import kv_attention as kva
+    recs = torch.zeros((4097, 2 * 66), dtype=torch.float32, device="cuda")
+    with pytest.raises(KvqError, match="parts"):
+        kva.lse_merge_records(recs, 1, 2, 64, torch.float32)
+    with pytest.raises(ValueError):
+        kva.lse_merge_records(recs[:, :-1].contiguous(), 1, 2, 64, torch.float32)
+
+
+def test_single_rank_sequence_split_eager_and_graph(native):
+    """group=None: the decoder's step equals the fp64 oracle's verdict; its
+    captured graph, replayed after new inputs are copied into the captured
+    tensors, gives exactly what an eager step gives on those inputs."""
+    import torch
+    from kernelverify_b200.pack import kv_attention as kva
+    from kernelverify_b200.pack.tsplit import SequenceSplitDecoder
+    from tests.kvq_cases import pack, to_dev
+    t = 9000
+    q, kc, vc, nk, nv = cases.make_case(1, 64, t, 128, seed=21)
+    kc, vc, nk, nv = kc[:8], vc[:8], nk[:, :8], nv[:, :8]
+    dev = [to_dev(x) for x in (q, *pack(kc, 4), *pack(vc, 4), nk, nv)]
+    dec = SequenceSplitDecoder(1, 64, 128, torch.device("cuda"))
+    out = torch.empty_like(dev[0])
+    dec.step(*dev, bits=4, t_local=t, out=out)
+    torch.cuda.synchronize()
+    v = kv.verify_output(kv.gqa_tiled_inputs(q, kc, vc, nk, nv, 4), out.cpu().numpy())
+    assert v.ok, v
+    graph = dec.capture(*dev, bits=4, t_local=t, out=out)
+    q2 = np.random.default_rng(5).standard_normal(q.shape).astype(np.float16)
+    dev[0].copy_(to_dev(q2))
+    graph.replay()
+    torch.cuda.synchronize()
+    replayed = out.clone()
+    eager = dec.step(*dev, bits=4, t_local=t, out=torch.empty_like(out))
+    torch.cuda.synchronize()
+    assert torch.equal(replayed, eager)
+    v2 = kv.verify_output(kv.gqa_tiled_inputs(q2, kc, vc, nk, nv, 4), replayed.cpu().numpy())
+    assert v2.ok, v2
+    del graph
