@@ -18,8 +18,9 @@ its shard's partial (O, m, l), the partials are all-gathered over NCCL and
 merged by log-sum-exp on every rank (strong scaling).
 
 Timing: W untimed eager warm-up steps, then each cache set's step is captured
-as a CUDA graph (kernels, and for config 5 the all-gather) and exactly K graph
-replays are timed between a barrier + cudaDeviceSynchronize on both sides,
+as a CUDA graph (config 5 on N > 1 ranks: the local partial only, the NCCL
+all-gather and the merge run eagerly after each replay) and exactly K steps
+are timed between a barrier + cudaDeviceSynchronize on both sides,
 CUDA events on the launching stream, max over ranks. The dominant kernel (the
 split stage) is then timed alone over K launches the same way (roofline).
 `e2e` repeats the step through the public Python API with pinned host inputs
@@ -308,22 +309,35 @@ def run_ours(args) -> dict | None:
         eager_step(i)
     barrier(dist)
     # one CUDA graph per cache set: a replayed step makes no host calls
+    # (config 5 on N ranks: the graph holds the local partial; the all-gather
+    # and the merge stay eager, so the process group's timeout watches them)
     pool = torch.cuda.graph_pool_handle()
     graphs = []
     for i in range(n_sets):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, pool=pool):
-            eager_step(i)
+        if args.config == 2:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                eager_step(i)
+        else:
+            kw, ks, kb, vw, vs, vb = sets[i]
+            g = decoder.capture(q, kw, ks, kb, vw, vs, vb, nk, nv, bits=cfg["bits"],
+                                t_local=t_rows, out=out, pool=pool)
         graphs.append(g)
+
+    def graph_step(i):
+        graphs[i % n_sets].replay()
+        if args.config == 5 and world > 1:
+            decoder.finish(q.dtype, out=out)
+
     for i in range(n_sets):
-        graphs[i].replay()
+        graph_step(i)
     barrier(dist)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stream = torch.cuda.current_stream(device)
     wall0 = time.time()
     e0.record(stream)
     for i in range(args.steps):
-        graphs[(args.warmup + i) % n_sets].replay()
+        graph_step(args.warmup + i)
     e1.record(stream)
     torch.cuda.synchronize()
     wall1 = time.time()
@@ -344,7 +358,7 @@ def run_ours(args) -> dict | None:
     kern_ms = k0.elapsed_time(k1) / args.steps
     step_ms = max_over_ranks(local_ms, dist)
     kern_ms_max = max_over_ranks(kern_ms, dist)
-    del graphs     # the graphs hold NCCL work: release them before the group goes
+    del graphs
 
     # ---- e2e through the public API: pinned host inputs in, result out -------
     e2e = None

@@ -78,30 +78,40 @@ class SequenceSplitDecoder:
                            part_o=self.part_o, part_m=self.part_m, part_l=self.part_l,
                            workspace=self.workspace)
 
-    def step(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
-             bits: int, t_local: int, out=None):
-        """out [B, H, DH] in q's dtype, identical on every rank."""
+    def finish(self, out_dtype, out=None):
+        """Gather every rank's record and merge them: out [B, H, DH]."""
         import torch
         from kernelverify_b200.pack import kv_attention as kva
-
-        self.partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
-                     bits=bits, t_local=t_local)
         if self.group is None:
             self.records[0].copy_(self.record)
         else:
             torch.distributed.all_gather_into_tensor(self.records, self.record, group=self.group)
         return kva.lse_merge_records(self.records, self.b_rows, self.n_heads, self.head_dim,
-                                     q.dtype, out=out)
+                                     out_dtype, out=out)
+
+    def step(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
+             bits: int, t_local: int, out=None):
+        """out [B, H, DH] in q's dtype, identical on every rank."""
+        self.partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
+                     bits=bits, t_local=t_local)
+        return self.finish(q.dtype, out=out)
 
     def capture(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
-                bits: int, t_local: int, out, pool=None):
-        """A CUDA graph of one `step` on these tensors (partial, all-gather,
-        merge); `graph.replay()` reruns it on whatever they then hold. Run one
-        eager `step` first (it creates the communicator and sets the kernels'
-        attributes). Drop the graph before destroying the process group."""
+                bits: int, t_local: int, out=None, pool=None):
+        """A CUDA graph of this rank's local work on these tensors; replay it
+        and then call `finish` for the step. With one rank (group None) the
+        graph holds the whole step, writing `out`. With more, it holds the
+        partial only: the all-gather stays an eager NCCL call, watched by the
+        process group's timeout (a collective inside a graph is not). Run one
+        eager `step` first (it sets the kernels' attributes and sizes the
+        workspace)."""
         import torch
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, pool=pool):
-            self.step(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
-                      bits=bits, t_local=t_local, out=out)
+            if self.group is None:
+                self.step(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
+                          bits=bits, t_local=t_local, out=out)
+            else:
+                self.partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k,
+                             new_v, bits=bits, t_local=t_local)
         return graph
