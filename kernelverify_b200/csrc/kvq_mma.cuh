@@ -16,9 +16,10 @@
 //           the dot product is a reassociation of the reference's
 //           sum_d q_d (s c_d + b) (contract clause C2).
 //   combine O[h,d] = sum_t P'[h,t,g] * code[t,d] + sum_t p[h,t] * v_bias[t,g],
-//           P' = p * v_scale, carried as three bf16 parts hi + mid + lo that
-//           reproduce P' to ~24 bits, so the tensor-core product with the
-//           exact bf16 codes is an fp32-accurate P'*code (mma m16n8k16 bf16,
+//           P' = p * v_scale, carried as two bf16 parts hi + lo that
+//           reproduce P' to 2^-16 relative (the kernel serves fp16 outputs,
+//           whose tolerance is 4 fp16 ulps of max|ref|), times the exact bf16
+//           codes on the tensor cores (mma m16n8k16 bf16, exact products,
 //           fp32 accumulation).
 // The MMA shapes are chosen so the score accumulator fragment IS the
 // combine's B fragment: S^T = Q * Codes_K^T puts head h = lane/4 and
@@ -214,26 +215,18 @@ __device__ __forceinline__ void bf16x2_to_f32(uint32_t v, float& lo, float& hi) 
     lo = __uint_as_float(v << 16);
     hi = __uint_as_float(v & 0xFFFF0000u);
 }
-// Split two fp32 values into three packed bf16x2 parts whose sum reproduces
-// them: bf16 is the upper half of fp32, so each part is a truncation taken by
-// a byte permute, and each residual x - part is exact in fp32. The three parts
-// carry the full 24-bit significand (the last truncation drops less than one
-// fp32 ulp). Integer and fma-pipe work only.
-__device__ __forceinline__ void split3(float x0, float x1, uint32_t& p_hi, uint32_t& p_mid,
-                                       uint32_t& p_lo) {
-    const float2 neg1 = make_float2(-1.0f, -1.0f);
+// Split two fp32 values into two packed bf16x2 parts whose sum reproduces
+// them to 16+ significant bits: hi is the truncation (the upper half of the
+// fp32 word, taken by a byte permute), the residual x - hi is exact in fp32,
+// and lo is that residual rounded to nearest bf16. |x - hi - lo| <= 2^-16 |x|.
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& p_hi, uint32_t& p_lo) {
     const uint32_t u0 = __float_as_uint(x0), u1 = __float_as_uint(x1);
     p_hi = prmt<0x7632>(u0, u1);
-    // the parts back as fp32: low half << 16 (an integer multiply), high half masked
+    // hi back as fp32: low half << 16 (an integer multiply), high half masked
     const float2 r = __ffma2_rn(make_float2(__uint_as_float(p_hi * 65536u),
                                             __uint_as_float(p_hi & 0xFFFF0000u)),
-                                neg1, make_float2(x0, x1));
-    const uint32_t v0 = __float_as_uint(r.x), v1 = __float_as_uint(r.y);
-    p_mid = prmt<0x7632>(v0, v1);
-    const float2 r2 = __ffma2_rn(make_float2(__uint_as_float(p_mid * 65536u),
-                                             __uint_as_float(p_mid & 0xFFFF0000u)),
-                                 neg1, r);
-    p_lo = prmt<0x7632>(__float_as_uint(r2.x), __float_as_uint(r2.y));
+                                make_float2(-1.0f, -1.0f), make_float2(x0, x1));
+    p_lo = pack_bf16(r.x, r.y);
 }
 
 __device__ __forceinline__ float h2f(const __half* p) { return __half2float(*p); }
@@ -364,6 +357,8 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
         // ---------------- consumers --------------------------------------------
         const int r = lane >> 2, j = lane & 3;
         const int qh = HT == 4 ? (r & 3) : r;          // head of this lane's score row
+        const int half = r >> 2;                       // HT = 4: which n-tile the lane keeps
+        constexpr int NS = HT == 4 ? 2 : 4;            // scores a lane keeps per block
         const __half* q = static_cast<const __half*>(P.q) + ((size_t)b * H + h0 + qh) * DH;
         const bool qvalid = qh < nh;
         // Q as the K-side A fragment: virtual k (2j,2j+1 | 2j+8,2j+9) of k-step
@@ -452,9 +447,13 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
             const float* kscr = scr;                 // [16][2G]
             const float* vscr = scr + 16 * 2 * G;    // [16][2G]
             {
-                // ---- scores of 16 positions, log2 units: lane (r, j) holds head
-                // r at positions j, j+4 (n-tile 0) and 8+j, 12+j (n-tile 1)
-                float sc[4];
+                // ---- scores of 16 positions, log2 units. The K-side MMAs give
+                // lane (r, j) head qh at positions j, j+4 (n-tile 0) and 8+j,
+                // 12+j (n-tile 1). HT = 8: the lane keeps all four. HT = 4: rows
+                // r and r+4 carry the same head, so the lane keeps n-tile `half`
+                // only and the two halves share the block's scalar work.
+                float sc[NS];
+                float xs[G][2];
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt) {
                     const unsigned char* rowp = st + Lay::KC + (blk * 16 + nt * 8 + krow) * ROWB;
@@ -477,28 +476,50 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                                     hcodes[2], hcodes[3]);
                         }
                     }
+                    if constexpr (HT == 4) {
+#pragma unroll
+                        for (int g = 0; g < G; ++g)
+#pragma unroll
+                            for (int c = 0; c < 2; ++c)
+                                xs[g][c] = (nt == 0 || half) ? x[g][c] : xs[g][c];
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 2; ++c) {
+                            const int lpos = nt * 8 + j + 4 * c;
+                            float kf[2 * G];
+                            load_f<2 * G>(kscr + lpos * 2 * G, kf);
+                            float acc = 0.0f;
+#pragma unroll
+                            for (int g = 0; g < G; ++g) acc = fmaf(kf[g], x[g][c], fmaf(kf[G + g], qsum[g], acc));
+                            sc[nt * 2 + c] = blk * 16 + lpos < nvalid ? acc : -INFINITY;
+                        }
+                    }
+                }
+                if constexpr (HT == 4) {
 #pragma unroll
                     for (int c = 0; c < 2; ++c) {
-                        const int lpos = nt * 8 + j + 4 * c;
-                        const int pos = blk * 16 + lpos;
+                        const int lpos = half * 8 + j + 4 * c;
                         float kf[2 * G];
                         load_f<2 * G>(kscr + lpos * 2 * G, kf);
                         float acc = 0.0f;
 #pragma unroll
-                        for (int g = 0; g < G; ++g) acc = fmaf(kf[g], x[g][c], fmaf(kf[G + g], qsum[g], acc));
-                        sc[nt * 2 + c] = pos < nvalid ? acc : -INFINITY;
+                        for (int g = 0; g < G; ++g) acc = fmaf(kf[g], xs[g][c], fmaf(kf[G + g], qsum[g], acc));
+                        sc[c] = blk * 16 + lpos < nvalid ? acc : -INFINITY;
                     }
                 }
 
                 // ---- online softmax with lazy rescaling: the reference point
                 // m_run moves only when a head's block max exceeds it by more
                 // than 2^8, so weights stay <= 256 and O rarely needs rescaling
-                float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+                float mx = sc[0];
+#pragma unroll
+                for (int i = 1; i < NS; ++i) mx = fmaxf(mx, sc[i]);
                 if (__any_sync(0xffffffffu, mx > m_run + 8.0f)) {
                     // some head's scores outgrew its reference point: take the
-                    // head's block max over its four lanes and move the point
+                    // head's block max over its lanes and move the point
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
                     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                    if constexpr (HT == 4) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
                     const bool grow = mx > m_run + 8.0f;
                     const float m_new = grow ? mx : m_run;
                     const float alpha = ex2(m_run - m_new);   // 0 on the first block, 1 if unchanged
@@ -518,38 +539,59 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                         oacc[i][0] = u.x; oacc[i][1] = u.y; oacc[i][2] = v.x; oacc[i][3] = v.y;
                     }
                 }
-                const float e0 = ex2(sc[0] - m_run), e1 = ex2(sc[1] - m_run);
-                const float e2 = ex2(sc[2] - m_run), e3 = ex2(sc[3] - m_run);
-                l_part += (e0 + e1) + (e2 + e3);
+                float e[NS];
+#pragma unroll
+                for (int i = 0; i < NS; ++i) e[i] = ex2(sc[i] - m_run);
+                if constexpr (HT == 4) {
+                    l_part += e[0] + e[1];
+                } else {
+                    l_part += (e[0] + e[1]) + (e[2] + e[3]);
+                }
 
                 // ---- combine --------------------------------------------------
-                const int p0 = blk * 16 + j;
-                float vsf[4][G], vbf[4][G];
+                // V scale and folded bias of the lane's own positions
+                float vsf[NS][G], vbf[NS][G];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int i = 0; i < NS; ++i) {
+                    const int lpos = HT == 4 ? half * 8 + j + 4 * i : (i >> 1) * 8 + j + 4 * (i & 1);
                     float vf[2 * G];
-                    load_f<2 * G>(vscr + (j + 4 * k) * 2 * G, vf);
+                    load_f<2 * G>(vscr + lpos * 2 * G, vf);
 #pragma unroll
-                    for (int g = 0; g < G; ++g) { vsf[k][g] = vf[g]; vbf[k][g] = vf[G + g]; }
+                    for (int g = 0; g < G; ++g) { vsf[i][g] = vf[g]; vbf[i][g] = vf[G + g]; }
                 }
-                // B fragments: the three bf16 parts of P' = p * v_scale per group
-                uint32_t bh[G][2], bm[G][2], bl[G][2];
+                // B fragments (k rows 2j, 2j+1 <-> positions j, j+4; 2j+8, 2j+9
+                // <-> 8+j, 12+j; column r): bf0/bf1 for the first MMA of a tile,
+                // bs0/bs1 for the second (HT = 8 only).
+                uint32_t bf0[G], bf1[G], bs0[G], bs1[G];
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
                     // bias with the codes' +128 offset folded in: b - 128 s
                     float acc = bsum[g];
-                    acc = fmaf(e0, vbf[0][g], acc);
-                    acc = fmaf(e1, vbf[1][g], acc);
-                    acc = fmaf(e2, vbf[2][g], acc);
-                    acc = fmaf(e3, vbf[3][g], acc);
+#pragma unroll
+                    for (int i = 0; i < NS; ++i) acc = fmaf(e[i], vbf[i][g], acc);
                     bsum[g] = acc;
-                    const float2 v01 = __fmul2_rn(make_float2(e0, e1), make_float2(vsf[0][g], vsf[1][g]));
-                    const float2 v23 = __fmul2_rn(make_float2(e2, e3), make_float2(vsf[2][g], vsf[3][g]));
-                    split3(v01.x, v01.y, bh[g][0], bm[g][0], bl[g][0]);
-                    split3(v23.x, v23.y, bh[g][1], bm[g][1], bl[g][1]);
+                    if constexpr (HT == 4) {
+                        // column r < 4: hi of head r; column r >= 4: lo of head r-4.
+                        // The lane has its half's two positions; the other two come
+                        // from the partner lane r^4 (lane ^ 16), which holds the
+                        // same head: one exchange carries what each side lacks.
+                        const float2 v = __fmul2_rn(make_float2(e[0], e[1]), make_float2(vsf[0][g], vsf[1][g]));
+                        uint32_t hi, lo;
+                        split2(v.x, v.y, hi, lo);
+                        const uint32_t recv = __shfl_xor_sync(0xffffffffu, half ? hi : lo, 16);
+                        bf0[g] = half ? recv : hi;
+                        bf1[g] = half ? lo : recv;
+                        bs0[g] = bs1[g] = 0u;
+                    } else {
+                        const float2 v01 = __fmul2_rn(make_float2(e[0], e[1]), make_float2(vsf[0][g], vsf[1][g]));
+                        const float2 v23 = __fmul2_rn(make_float2(e[2], e[3]), make_float2(vsf[2][g], vsf[3][g]));
+                        split2(v01.x, v01.y, bf0[g], bs0[g]);
+                        split2(v23.x, v23.y, bf1[g], bs1[g]);
+                    }
                 }
                 // A fragments: V codes^T, rows = dims, cols = positions
                 // (k 2j, 2j+1 <-> pos j, j+4; 2j+8, 2j+9 <-> 8+j, 12+j).
+                const int p0 = blk * 16 + j;
                 const unsigned char* vrow = st + Lay::VC;
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
@@ -588,20 +630,12 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                     }
 #pragma unroll
                     for (int ii = 0; ii < MTG; ++ii) {
-                        const uint32_t a0 = fa[ii][0], a1 = fa[ii][1], a2 = fa[ii][2], a3 = fa[ii][3];
                         // a0: (dim row r, pos j, j+4); a1: (row r+8 = high nibble);
                         // a2/a3: the same for positions 8+j, 12+j
                         float (&acc)[4] = oacc[g * MTG + ii];
-                        if constexpr (HT == 4) {
-                            const uint32_t b0 = r < 4 ? bh[g][0] : bm[g][0];
-                            const uint32_t b1 = r < 4 ? bh[g][1] : bm[g][1];
-                            mma_bf16(acc, a0, a1, a2, a3, b0, b1);
-                            mma_bf16(acc, a0, a1, a2, a3, r < 4 ? bl[g][0] : 0u, r < 4 ? bl[g][1] : 0u);
-                        } else {
-                            mma_bf16(acc, a0, a1, a2, a3, bh[g][0], bh[g][1]);
-                            mma_bf16(acc, a0, a1, a2, a3, bm[g][0], bm[g][1]);
-                            mma_bf16(acc, a0, a1, a2, a3, bl[g][0], bl[g][1]);
-                        }
+                        mma_bf16(acc, fa[ii][0], fa[ii][1], fa[ii][2], fa[ii][3], bf0[g], bf1[g]);
+                        if constexpr (HT == 8)
+                            mma_bf16(acc, fa[ii][0], fa[ii][1], fa[ii][2], fa[ii][3], bs0[g], bs1[g]);
                     }
                 }
             }
@@ -612,13 +646,15 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
         // ---- warp partial: reduce l and bias sums over the 4 lanes of a head --
         l_part += __shfl_xor_sync(0xffffffffu, l_part, 1);
         l_part += __shfl_xor_sync(0xffffffffu, l_part, 2);
+        if constexpr (HT == 4) l_part += __shfl_xor_sync(0xffffffffu, l_part, 16);
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             bsum[g] += __shfl_xor_sync(0xffffffffu, bsum[g], 1);
             bsum[g] += __shfl_xor_sync(0xffffffffu, bsum[g], 2);
+            if constexpr (HT == 4) bsum[g] += __shfl_xor_sync(0xffffffffu, bsum[g], 16);
         }
         if constexpr (HT == 4) {
-            // columns 4..7 carry the mid parts of heads 0..3: fold them in
+            // columns 4..7 carry the lo parts of heads 0..3: fold them in
 #pragma unroll
             for (int i = 0; i < MT; ++i)
 #pragma unroll
