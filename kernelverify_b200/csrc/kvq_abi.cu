@@ -179,9 +179,6 @@ int plan(const kvq_args* a, Plan* pl) {
         pl->ht = P.r == 1 ? 1 : (P.r <= 4 ? 4 : 8);
     P.head_tiles = (P.r + pl->ht - 1) / pl->ht;
     P.scale = 1.0f / sqrtf((float)a->head_dim);
-    P.shr4 = 1u << 28;
-    P.shr8 = 1u << 24;
-    P.shr12 = 1u << 20;
 
     const uint32_t end = a->t_end < a->t_cached ? a->t_end : a->t_cached;
     const uint64_t span = end > a->t_begin ? end - a->t_begin : 0;

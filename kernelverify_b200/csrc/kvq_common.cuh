@@ -117,10 +117,6 @@ struct Problem {
     uint32_t r;          // query heads per cache head
     uint32_t head_tiles; // ceil(r / HT)
     float scale;         // 1/sqrt(head_dim)
-    // Powers of two the tensor-core kernel multiplies by to shift right
-    // (mul.hi by 2^(32-k) == >> k) on the FMA pipe instead of the ALU pipe;
-    // passed at run time so the compiler cannot turn them back into shifts.
-    uint32_t shr4, shr8, shr12;
 };
 
 }  // namespace kvq

@@ -38,7 +38,10 @@ namespace mma4 {
 constexpr int CWARPS = 4;                    // consumer warps
 constexpr int THREADS = 32 * (CWARPS + 1);   // + one producer warp
 constexpr int TP = 64;                       // positions per stage
-constexpr int STAGES = 6;
+#ifndef KVQ_MMA_STAGES
+#define KVQ_MMA_STAGES 6                     // depth of the shared-memory stage ring
+#endif
+constexpr int STAGES = KVQ_MMA_STAGES;
 constexpr int DH = 128;
 constexpr int ROWB = DH / 2;                 // code bytes per row (4-bit)
 constexpr uint32_t WAIT_LIMIT = 1u << 22;    // bounded mbarrier waits
@@ -151,13 +154,6 @@ __device__ __forceinline__ uint32_t and_or(uint32_t x) {
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(x), "n"(MASK), "n"(MAGIC));
     return d;
 }
-// x >> k as mul.hi by the run-time 2^(32-k): an FMA-pipe integer multiply
-__device__ __forceinline__ uint32_t shr_mul(uint32_t x, uint32_t pow2) {
-    uint32_t d;
-    asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(pow2));
-    return d;
-}
-
 // ---- exact small-integer conversions ----------------------------------------
 __device__ __forceinline__ uint32_t h2_sub1024(uint32_t x) {
     __half2 v = __hsub2(*reinterpret_cast<__half2*>(&x), __half2(__half(1024.0f), __half(1024.0f)));
@@ -174,38 +170,29 @@ __device__ __forceinline__ uint32_t bf2_sub128(uint32_t x) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 // word of 8 nibbles n0..n7 -> four half2 registers (n0,n4) (n1,n5) (n2,n6) (n3,n7)
-__device__ __forceinline__ void nibbles_f16(uint32_t w, uint32_t shr8, uint32_t (&h)[4]) {
+__device__ __forceinline__ void nibbles_f16(uint32_t w, uint32_t (&h)[4]) {
     h[0] = h2_sub1024(and_or<0x000F000Fu, 0x64006400u>(w));
     h[1] = h2_hi_nibble(and_or<0x00F000F0u, 0x64006400u>(w));
-    const uint32_t w8 = shr_mul(w, shr8);
+    const uint32_t w8 = w >> 8;
     h[2] = h2_sub1024(and_or<0x000F000Fu, 0x64006400u>(w8));
     h[3] = h2_hi_nibble(and_or<0x00F000F0u, 0x64006400u>(w8));
 }
 // Bytes K and K+1 of words a and b -> four bf16x2 registers of exact code
 // values plus 128: (lo(a.K), lo(b.K)), (hi(a.K), hi(b.K)), (lo(a.K+1),
 // lo(b.K+1)), (hi(a.K+1), hi(b.K+1)). One byte permute gathers the four
-// bytes as [a.K, a.K+1, b.K, b.K+1]; each nibble pair is then one shift
-// (an FMA-pipe mul.hi) and one and-or. The combine subtracts 128 * P' through
+// bytes as [a.K, a.K+1, b.K, b.K+1]; each nibble pair is then one shift and
+// one and-or. The combine subtracts 128 * P' through
 // the bias term instead of per code:
 //   sum_t P'_t (128 + c_t) + sum_t p_t (b_t - 128 s_t) = sum_t p_t (s_t c_t + b_t).
 template <int K>
-__device__ __forceinline__ void quad_bf16(uint32_t a, uint32_t b, const Problem& P, uint32_t& lo0,
+__device__ __forceinline__ void quad_bf16(uint32_t a, uint32_t b, uint32_t& lo0,
                                           uint32_t& hi0, uint32_t& lo1, uint32_t& hi1) {
     constexpr uint32_t sel = K | ((K + 1) << 4) | ((4 + K) << 8) | ((5 + K) << 12);
     const uint32_t u = prmt<sel>(a, b);
     lo0 = and_or<0x000F000Fu, 0x43004300u>(u);
-    hi0 = and_or<0x000F000Fu, 0x43004300u>(shr_mul(u, P.shr4));
-    lo1 = and_or<0x000F000Fu, 0x43004300u>(shr_mul(u, P.shr8));
-    hi1 = and_or<0x000F000Fu, 0x43004300u>(shr_mul(u, P.shr12));
-}
-// byte K of words a and b only (lo, hi)
-template <int K>
-__device__ __forceinline__ void pair_bf16(uint32_t a, uint32_t b, const Problem& P, uint32_t& lo,
-                                          uint32_t& hi) {
-    constexpr uint32_t sel = K | (K << 4) | ((4 + K) << 8) | ((4 + K) << 12);
-    const uint32_t u = prmt<sel>(a, b);
-    lo = and_or<0x000F000Fu, 0x43004300u>(u);
-    hi = and_or<0x000F000Fu, 0x43004300u>(shr_mul(u, P.shr4));
+    hi0 = and_or<0x000F000Fu, 0x43004300u>(u >> 4);
+    lo1 = and_or<0x000F000Fu, 0x43004300u>(u >> 8);
+    hi1 = and_or<0x000F000Fu, 0x43004300u>(u >> 12);
 }
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -469,7 +456,7 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
 #pragma unroll
                         for (int wi = 0; wi < WPG; ++wi) {
                             uint32_t hcodes[4];
-                            nibbles_f16(w[wi], P.shr8, hcodes);
+                            nibbles_f16(w[wi], hcodes);
                             mma_f16(x[g], qa[g][2 * wi][0], 0u, qa[g][2 * wi][1], 0u, hcodes[0],
                                     hcodes[1]);
                             mma_f16(x[g], qa[g][2 * wi + 1][0], 0u, qa[g][2 * wi + 1][1], 0u,
@@ -620,11 +607,11 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                         const int wi = ii >> 2;
                         if constexpr (MTG >= 2) {
                             if ((ii & 3) == 0) {
-                                quad_bf16<0>(wA[wi], wB[wi], P, fa[ii][0], fa[ii][1], fa[ii + 1][0], fa[ii + 1][1]);
-                                quad_bf16<0>(wC[wi], wD[wi], P, fa[ii][2], fa[ii][3], fa[ii + 1][2], fa[ii + 1][3]);
+                                quad_bf16<0>(wA[wi], wB[wi], fa[ii][0], fa[ii][1], fa[ii + 1][0], fa[ii + 1][1]);
+                                quad_bf16<0>(wC[wi], wD[wi], fa[ii][2], fa[ii][3], fa[ii + 1][2], fa[ii + 1][3]);
                             } else {
-                                quad_bf16<2>(wA[wi], wB[wi], P, fa[ii][0], fa[ii][1], fa[ii + 1][0], fa[ii + 1][1]);
-                                quad_bf16<2>(wC[wi], wD[wi], P, fa[ii][2], fa[ii][3], fa[ii + 1][2], fa[ii + 1][3]);
+                                quad_bf16<2>(wA[wi], wB[wi], fa[ii][0], fa[ii][1], fa[ii + 1][0], fa[ii + 1][1]);
+                                quad_bf16<2>(wC[wi], wD[wi], fa[ii][2], fa[ii][3], fa[ii + 1][2], fa[ii + 1][3]);
                             }
                         }
                     }
