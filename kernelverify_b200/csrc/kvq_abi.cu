@@ -73,12 +73,18 @@ size_t align_up(size_t n) { return (n + kAlign - 1) / kAlign * kAlign; }
 constexpr uint64_t kTargetCtas = 148 * 4 * 2;
 constexpr uint32_t kMaxSplits = 4096;
 
-enum KernelKind { KERNEL_GENERIC = 0, KERNEL_MMA4 = 1 };
+enum KernelKind { KERNEL_GENERIC = 0, KERNEL_MMA4 = 1, KERNEL_UMMA4 = 2 };
 
-// KVQ_KERNEL=generic forces the CUDA-core kernel (A/B checks of the paths).
-bool generic_forced() {
+// KVQ_KERNEL=generic forces the CUDA-core kernel, KVQ_KERNEL=umma the tcgen05
+// kernel where it applies (fp16, 4-bit, head_dim 128, group 64); unset, each
+// call takes the fastest eligible kernel, the register-fragment tensor-core
+// kernel for the tensor-core formats (A/B checks of the paths use the switch).
+int kernel_override() {
     const char* v = getenv("KVQ_KERNEL");
-    return v != nullptr && strcmp(v, "generic") == 0;
+    if (v == nullptr) return -1;
+    if (strcmp(v, "generic") == 0) return KERNEL_GENERIC;
+    if (strcmp(v, "umma") == 0) return KERNEL_UMMA4;
+    return -1;
 }
 
 // Split plan of the tensor-core kernel. Its CTAs run in waves of the resident
@@ -90,28 +96,28 @@ constexpr uint64_t kMmaStage = 64;
 constexpr uint64_t kMmaRamp = 128;
 
 void mma4_splits(uint64_t span, uint64_t units, int ctas_per_sm, uint32_t* chunk_out,
-                 uint32_t* splits_out) {
+                 uint32_t* splits_out, uint64_t stage = kMmaStage, uint64_t ramp = kMmaRamp) {
     const uint64_t resident = (uint64_t)ctas_per_sm * kvq::sm_count();
-    const auto round_stage = [](uint64_t n) {
-        n = (n + kMmaStage - 1) / kMmaStage * kMmaStage;
-        return n < kMmaStage ? kMmaStage : n;
+    const auto round_stage = [stage](uint64_t n) {
+        n = (n + stage - 1) / stage * stage;
+        return n < stage ? stage : n;
     };
     uint64_t best_chunk = round_stage(span), best_splits = 1;
-    uint64_t best_cost = ((units + resident - 1) / resident) * (best_chunk + kMmaRamp);
+    uint64_t best_cost = ((units + resident - 1) / resident) * (best_chunk + ramp);
     for (uint64_t waves = 1; span && waves <= 8; ++waves) {
         const uint64_t fit = waves * resident / units;
         if (fit <= 1) continue;
         const uint64_t chunk = round_stage((span + fit - 1) / fit);
         const uint64_t splits = (span + chunk - 1) / chunk;
         if (splits > kMaxSplits) break;
-        const uint64_t cost = ((units * splits + resident - 1) / resident) * (chunk + kMmaRamp);
+        const uint64_t cost = ((units * splits + resident - 1) / resident) * (chunk + ramp);
         if (cost < best_cost) {
             best_cost = cost;
             best_chunk = chunk;
             best_splits = splits;
         }
     }
-    constexpr uint64_t kMaxChunk = 0xFFFFFFFFull / kMmaStage * kMmaStage;
+    const uint64_t kMaxChunk = 0xFFFFFFFFull / stage * stage;
     if (best_chunk > kMaxChunk) {
         best_chunk = kMaxChunk;
         best_splits = (span + best_chunk - 1) / best_chunk;
@@ -161,19 +167,23 @@ int plan(const kvq_args* a, Plan* pl) {
     P.cache_batch_stride = a->cache_batch_stride;
     P.t_begin = a->t_begin; P.t_end = a->t_end;
     P.r = a->n_heads / a->n_kv_heads;
-    // The tensor-core kernel streams 16-byte-aligned runs of 8 rows with TMA:
-    // it needs the fp16 / 4-bit / DH 128 format, at most 8 query heads per
-    // cache head, and 8-row-aligned geometry; everything else runs on the
-    // CUDA-core kernel.
+    // The tensor-core kernels stream 16-byte-aligned runs of 8 rows with TMA:
+    // they need the fp16 / 4-bit / DH 128 format, at most 8 query heads per
+    // cache head, and 8-row-aligned geometry (the tcgen05 kernel, when asked
+    // for, group 64 as well); everything else runs on the CUDA-core kernel.
     const bool tma_ok = aligned(a->k_wq, 16) && aligned(a->v_wq, 16) && aligned(a->k_scales, 16) &&
                         aligned(a->k_biases, 16) && aligned(a->v_scales, 16) &&
                         aligned(a->v_biases, 16) && a->t_stride % 8 == 0 &&
                         a->cache_batch_stride % 8 == 0 && a->t_begin % 8 == 0;
-    pl->kernel = (!generic_forced() && a->dtype == KVQ_F16 && a->bits == 4 && a->head_dim == 128 &&
-                  P.r <= 8 && tma_ok)
-                     ? KERNEL_MMA4
-                     : KERNEL_GENERIC;
-    if (pl->kernel == KERNEL_MMA4)
+    const bool tc = a->dtype == KVQ_F16 && a->bits == 4 && a->head_dim == 128 && P.r <= 8 && tma_ok;
+    const int forced = kernel_override();
+    if (!tc || forced == KERNEL_GENERIC)
+        pl->kernel = KERNEL_GENERIC;
+    else if (a->group_size == 64 && forced == KERNEL_UMMA4)
+        pl->kernel = KERNEL_UMMA4;
+    else
+        pl->kernel = KERNEL_MMA4;
+    if (pl->kernel != KERNEL_GENERIC)
         pl->ht = P.r <= 4 ? 4 : 8;
     else
         pl->ht = P.r == 1 ? 1 : (P.r <= 4 ? 4 : 8);
@@ -184,8 +194,13 @@ int plan(const kvq_args* a, Plan* pl) {
     const uint64_t span = end > a->t_begin ? end - a->t_begin : 0;
     const uint64_t units = (uint64_t)a->b_rows * a->n_kv_heads * P.head_tiles;
     pl->rows = a->b_rows * a->n_heads;
-    if (pl->kernel == KERNEL_MMA4) {
-        mma4_splits(span, units, kvq::mma4_ctas_per_sm(pl->ht, a->group_size), &P.chunk, &P.n_splits);
+    if (pl->kernel != KERNEL_GENERIC) {
+        if (pl->kernel == KERNEL_UMMA4)
+            // 128-position tiles; the CTA's fixed work (TMEM, the q operand, the
+            // final reduction) is worth about two tiles
+            mma4_splits(span, units, kvq::umma4_ctas_per_sm(pl->ht), &P.chunk, &P.n_splits, 128, 256);
+        else
+            mma4_splits(span, units, kvq::mma4_ctas_per_sm(pl->ht, a->group_size), &P.chunk, &P.n_splits);
         pl->part_bytes = align_up((size_t)P.n_splits * pl->rows * a->head_dim * sizeof(float));
         pl->ml_bytes = align_up((size_t)P.n_splits * pl->rows * sizeof(float));
         return KVQ_OK;
@@ -208,6 +223,7 @@ int plan(const kvq_args* a, Plan* pl) {
 
 cudaError_t launch_partial_any(const Plan& pl, uint32_t bits, uint32_t dtype, uint32_t dh,
                                float* o, float* m, float* l, cudaStream_t s) {
+    if (pl.kernel == KERNEL_UMMA4) return kvq::launch_umma4(pl.P, pl.ht, o, m, l, s);
     if (pl.kernel == KERNEL_MMA4) return kvq::launch_mma4(pl.P, pl.ht, pl.P.group_size, o, m, l, s);
     switch (bits) {
         case 2: return kvq::launch_partial<2>(pl.P, dtype, dh, pl.ht, o, m, l, s);

@@ -41,6 +41,12 @@ cudaError_t launch_merge_partial(const float* part_o, const float* part_m, const
                                  uint32_t n_parts, uint32_t rows, uint32_t head_dim,
                                  float* out_o, float* out_m, float* out_l, cudaStream_t stream);
 
+// 5th-generation tensor-core (tcgen05) partial kernel: fp16, 4-bit, head_dim
+// 128, group 64, ht in {4, 8}; and its resident CTAs per SM.
+cudaError_t launch_umma4(const Problem& P, int ht, float* part_o, float* part_m, float* part_l,
+                         cudaStream_t stream);
+int umma4_ctas_per_sm(int ht);
+
 // Resident tensor-core CTAs per SM for (ht, group) on the current device,
 // and the device's SM count (both cached per device; fixed fallbacks when the
 // device cannot be queried).

@@ -1,8 +1,9 @@
-"""The tensor-core kernel (fp16, 4-bit, head_dim 128, 8-row-aligned geometry)
-and the CUDA-core kernel on the same inputs: both pass the oracle, and they
+"""The tensor-core kernels (fp16, 4-bit, head_dim 128, 8-row-aligned geometry)
+and the CUDA-core kernel on the same inputs: each passes the oracle, and they
 agree with each other to 2e-3 of the output's max magnitude (the tensor-core
-kernel carries the V-side weights to 2^-16 relative). KVQ_KERNEL=generic
-forces the CUDA-core kernel for a call."""
+kernels carry the V-side weights to 2^-16 relative). KVQ_KERNEL=generic
+forces the CUDA-core kernel for a call, KVQ_KERNEL=umma the tcgen05 kernel
+(group 64; other groups keep the register-fragment kernel)."""
 
 from __future__ import annotations
 
@@ -17,13 +18,18 @@ from tests.kvq_cases import judge_gqa, judge_per_sequence, pack, run_decode, to_
 pytestmark = pytest.mark.gpu
 
 
-def both(fn):
-    os.environ["KVQ_KERNEL"] = "generic"
+def run_with(kernel, fn):
+    if kernel is not None:
+        os.environ["KVQ_KERNEL"] = kernel
     try:
-        generic = fn()
+        return fn()
     finally:
         os.environ.pop("KVQ_KERNEL", None)
-    return fn(), generic
+
+
+def kernels(fn):
+    """(default tensor-core, tcgen05, CUDA-core) outputs of the same call."""
+    return run_with(None, fn), run_with("umma", fn), run_with("generic", fn)
 
 
 def close(a, b, rel=2e-3):
@@ -37,11 +43,11 @@ def test_tensor_core_path_gqa_and_groups(native, h, hkv, group):
     t = 1000   # not a multiple of the 64-position stage: the tail is masked
     q, kc, vc, nk, nv = cases.make_case(2, h, t, 128, seed=h * 7 + hkv + group)
     kc, vc, nk, nv = kc[:hkv], vc[:hkv], nk[:, :hkv], nv[:, :hkv]
-    mma, gen = both(lambda: run_decode(q, kc, vc, nk, nv, 4, group))
-    for out in (mma, gen):
+    mma, umma, gen = kernels(lambda: run_decode(q, kc, vc, nk, nv, 4, group))
+    for out in (mma, umma, gen):
         v = judge_gqa(q, kc, vc, nk, nv, 4, out, group)
         assert v.ok, v
-    assert close(mma, gen)
+    assert close(mma, gen) and close(umma, gen)
 
 
 @pytest.mark.parametrize("t", [1, 7, 8, 63, 64, 65, 129, 4096, 9000])
@@ -54,11 +60,12 @@ def test_tensor_core_path_lengths(native, t):
     junk = rng.standard_normal((2, t_pad - t, 128)).astype(np.float16) * 30
     k_art = pack(np.concatenate([kc, junk], axis=1), 4)
     v_art = pack(np.concatenate([vc, junk], axis=1), 4)
-    mma, gen = both(lambda: run_decode(q, None, None, nk, nv, 4, t_cached=t, k_art=k_art, v_art=v_art))
-    for out in (mma, gen):
+    mma, umma, gen = kernels(lambda: run_decode(q, None, None, nk, nv, 4, t_cached=t, k_art=k_art,
+                                                 v_art=v_art))
+    for out in (mma, umma, gen):
         v = judge_gqa(q, kc, vc, nk, nv, 4, out)
         assert v.ok, (t, v)
-    assert close(mma, gen)
+    assert close(mma, gen) and close(umma, gen)
 
 
 def test_tensor_core_path_per_sequence_ragged(native):
@@ -70,23 +77,26 @@ def test_tensor_core_path_per_sequence_ragged(native):
     vc = rng.standard_normal((b, hkv, t_pad, 128)).astype(np.float16)
     nk = rng.standard_normal((b, hkv, 128)).astype(np.float16)
     nv = rng.standard_normal((b, hkv, 128)).astype(np.float16)
-    mma, gen = both(lambda: run_decode(q, kc, vc, nk, nv, 4, t_cached=int(lens.max()), seq_lens=lens))
-    for out in (mma, gen):
+    mma, umma, gen = kernels(lambda: run_decode(q, kc, vc, nk, nv, 4, t_cached=int(lens.max()),
+                                                 seq_lens=lens))
+    for out in (mma, umma, gen):
         for v in judge_per_sequence(q, kc, vc, nk, nv, 4, out, lens):
             assert v.ok, v
-    assert close(mma, gen)
+    assert close(mma, gen) and close(umma, gen)
 
 
-def test_tensor_core_path_t_split_shards(native):
-    """Shards starting at multiples of 8 run on the tensor-core kernel."""
+@pytest.mark.parametrize("kernel", [None, "umma"])
+def test_tensor_core_path_t_split_shards(native, kernel):
+    """Shards starting at multiples of 8 run on the tensor-core kernels."""
     import torch
     from kernelverify_b200.pack import kv_attention as kva
     q, kc, vc, nk, nv = cases.make_case(1, 64, 4096, 128, seed=3)
     kc, vc, nk, nv = kc[:8], vc[:8], nk[:, :8], nv[:, :8]
     args = [to_dev(x) for x in (q, *pack(kc, 4), *pack(vc, 4), nk, nv)]
     bounds = [(0, 1024), (1024, 2048), (2048, 3072), (3072, 4096)]
-    parts = [kva.decode_partial(*args, bits=4, t_begin=a, t_end=z, has_new_entry=(i == 3))
-             for i, (a, z) in enumerate(bounds)]
+    parts = run_with(kernel, lambda: [
+        kva.decode_partial(*args, bits=4, t_begin=a, t_end=z, has_new_entry=(i == 3))
+        for i, (a, z) in enumerate(bounds)])
     merged = kva.lse_merge(torch.stack([p[0] for p in parts]), torch.stack([p[1] for p in parts]),
                            torch.stack([p[2] for p in parts]), torch.float16).cpu().numpy()
     v = judge_gqa(q, kc, vc, nk, nv, 4, merged)
@@ -101,7 +111,7 @@ def test_outlier_caches(native):
     raw[rng.random(raw.shape) < 0.01] *= 20
     raw = raw.astype(np.float16)
     kc, vc = raw[0], raw[1]
-    mma, gen = both(lambda: run_decode(q, kc, vc, nk, nv, 4))
-    for out in (mma, gen):
+    mma, umma, gen = kernels(lambda: run_decode(q, kc, vc, nk, nv, 4))
+    for out in (mma, umma, gen):
         for v in judge_per_sequence(q, kc, vc, nk, nv, 4, out):
             assert v.ok, v
