@@ -261,6 +261,108 @@ __device__ __forceinline__ void load_g(const __half* p, float (&out)[G]) {
     }
 }
 
+// The producer: one thread streams the split's stages into the ring, each a
+// set of six contiguous runs (K codes, V codes, K/V scales and biases) of the
+// stage's rows, rounded up to whole 8-row runs; it waits (bounded) for every
+// consumer warp to release a slot before refilling it.
+template <int GROUP>
+__device__ __forceinline__ void produce(const Problem& P, unsigned char* smem, uint64_t* full,
+                                        uint64_t* empty, int* err_flag, uint32_t lo, uint32_t hi,
+                                        int n_stages, uint64_t rowbase) {
+    using Lay = Layout<GROUP>;
+    constexpr int G = Lay::G;
+    const uint64_t pol = evict_first_policy();
+    const unsigned char* kw = reinterpret_cast<const unsigned char*>(P.k_wq);
+    const unsigned char* vw = reinterpret_cast<const unsigned char*>(P.v_wq);
+    const unsigned char* ks = static_cast<const unsigned char*>(P.k_scales);
+    const unsigned char* kb = static_cast<const unsigned char*>(P.k_biases);
+    const unsigned char* vs = static_cast<const unsigned char*>(P.v_scales);
+    const unsigned char* vb = static_cast<const unsigned char*>(P.v_biases);
+    for (int s = 0; s < n_stages; ++s) {
+        const int slot = s % STAGES, round = s / STAGES;
+        if (s >= STAGES && !mbar_wait(&empty[slot], (round - 1) & 1)) {
+            atomicExch(err_flag, 1);
+            break;
+        }
+        const uint32_t t0 = lo + s * TP;
+        const uint32_t n = min((uint32_t)TP, hi - t0);
+        const uint32_t nr = (n + 7) & ~7u;
+        const uint64_t row = rowbase + t0;
+        unsigned char* st = smem + slot * Lay::STAGE;
+        mbar_expect_tx(&full[slot], nr * (2 * ROWB + 4 * G * 2));
+        bulk_g2s(st + Lay::KC, kw + row * ROWB, nr * ROWB, &full[slot], pol);
+        bulk_g2s(st + Lay::VC, vw + row * ROWB, nr * ROWB, &full[slot], pol);
+        bulk_g2s(st + Lay::KS, ks + row * G * 2, nr * G * 2, &full[slot], pol);
+        bulk_g2s(st + Lay::KB, kb + row * G * 2, nr * G * 2, &full[slot], pol);
+        bulk_g2s(st + Lay::VS, vs + row * G * 2, nr * G * 2, &full[slot], pol);
+        bulk_g2s(st + Lay::VB, vb + row * G * 2, nr * G * 2, &full[slot], pol);
+    }
+}
+
+// The CTA partial from the consumer warps' partials the caller left in the
+// merge area -- mo [CWARPS][8][DH] (O without the bias term), mm / ml
+// [CWARPS][8] (reference point in log2 units, l), mb [CWARPS][8][G] (bias
+// sums) -- plus the step's own entry when `with_new`; written as (O, m in
+// natural-log units, l) rows of split `split`, NaN when `bad`. Every consumer
+// thread calls it after the merge area is complete.
+template <int HT, int GROUP>
+__device__ __forceinline__ void finish_partial(const Problem& P, unsigned char* smem, int tid, int warp,
+                                               int lane, uint32_t split, uint32_t b, uint32_t hk,
+                                               uint32_t h0, int nh, bool with_new, float scale2,
+                                               const int* err_flag, float* __restrict__ part_o,
+                                               float* __restrict__ part_m, float* __restrict__ part_l) {
+    constexpr int G = DH / GROUP;
+    constexpr float LN2 = 0.6931471805599453f;
+    const uint32_t H = P.n_heads;
+    float* mo = reinterpret_cast<float*>(smem);                 // [CWARPS][8][DH]
+    float* mm = mo + CWARPS * 8 * DH;                           // [CWARPS][8]
+    float* ml = mm + CWARPS * 8;                                // [CWARPS][8]
+    float* mb = ml + CWARPS * 8;                                // [CWARPS][8][G]
+    float* snew = mb + CWARPS * 8 * G;                          // [8]
+    // the step's own entry: s_new[h] = q[h] . new_k / sqrt(DH), at fp32
+    if (with_new && warp == 0) {
+        const __half* nk = static_cast<const __half*>(P.new_k) + ((size_t)b * P.n_kv_heads + hk) * DH;
+        const __half* qb = static_cast<const __half*>(P.q) + ((size_t)b * H + h0) * DH;
+        for (int h = 0; h < nh; ++h) {
+            float part = 0.0f;
+            for (int d = lane; d < DH; d += 32) part = fmaf(__half2float(qb[h * DH + d]), __half2float(nk[d]), part);
+            part = warp_sum(part);
+            if (lane == 0) snew[h] = part * scale2;
+        }
+    }
+    named_sync(1, CWARPS * 32);
+    // ---- merge the warps (and the new entry) into the CTA partial -----------
+    const int bad = *(volatile const int*)err_flag;
+    const size_t rows = (size_t)P.b_rows * H;
+    const __half* nv = static_cast<const __half*>(P.new_v) + ((size_t)b * P.n_kv_heads + hk) * DH;
+    for (int idx = tid; idx < nh * DH; idx += CWARPS * 32) {
+        const int h = idx / DH, d = idx % DH, g = d / GROUP;
+        float M = with_new ? snew[h] : -INFINITY;
+#pragma unroll
+        for (int w = 0; w < CWARPS; ++w) M = fmaxf(M, mm[w * 8 + h]);
+        float o = 0.0f, l = 0.0f;
+#pragma unroll
+        for (int w = 0; w < CWARPS; ++w) {
+            const float mw = mm[w * 8 + h];
+            if (mw == -INFINITY) continue;
+            const float e = ex2(mw - M);
+            o = fmaf(mo[(w * 8 + h) * DH + d] + mb[(w * 8 + h) * G + g], e, o);
+            l = fmaf(ml[w * 8 + h], e, l);
+        }
+        if (with_new) {
+            const float e = ex2(snew[h] - M);
+            o = fmaf(__half2float(nv[d]), e, o);
+            l += e;
+        }
+        const size_t row = split * rows + (size_t)b * H + h0 + h;
+        part_o[row * DH + d] = bad ? __int_as_float(0x7fc00000) : o;
+        if (d == 0) {
+            part_m[row] = bad ? __int_as_float(0x7fc00000) : M * LN2;  // natural-log units
+            part_l[row] = bad ? __int_as_float(0x7fc00000) : l;
+        }
+    }
+}
+
 // -----------------------------------------------------------------------------
 template <int HT, int GROUP>
 __global__ void __launch_bounds__(THREADS, GROUP == 32 ? 2 : KVQ_MMA_MINBLOCKS)
@@ -274,7 +376,6 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
     constexpr int MT = DH / 16;         // V-side M-tiles
     constexpr int VBYTES = GROUP / 16;  // V-side bytes per lane, row and group
     constexpr float L2E = 1.4426950408889634f;
-    constexpr float LN2 = 0.6931471805599453f;
     const float scale2 = P.scale * L2E;   // scores are kept in log2 units
 
     extern __shared__ __align__(128) unsigned char smem[];
@@ -312,34 +413,7 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
 
     if (warp == CWARPS) {
         // ---------------- producer: stream stages into the ring ----------------
-        if (lane == 0) {
-            const uint64_t pol = evict_first_policy();
-            const unsigned char* kw = reinterpret_cast<const unsigned char*>(P.k_wq);
-            const unsigned char* vw = reinterpret_cast<const unsigned char*>(P.v_wq);
-            const unsigned char* ks = static_cast<const unsigned char*>(P.k_scales);
-            const unsigned char* kb = static_cast<const unsigned char*>(P.k_biases);
-            const unsigned char* vs = static_cast<const unsigned char*>(P.v_scales);
-            const unsigned char* vb = static_cast<const unsigned char*>(P.v_biases);
-            for (int s = 0; s < n_stages; ++s) {
-                const int slot = s % STAGES, round = s / STAGES;
-                if (s >= STAGES && !mbar_wait(&empty[slot], (round - 1) & 1)) {
-                    atomicExch(err_flag, 1);
-                    break;
-                }
-                const uint32_t t0 = lo + s * TP;
-                const uint32_t n = min((uint32_t)TP, hi - t0);
-                const uint32_t nr = (n + 7) & ~7u;
-                const uint64_t row = rowbase + t0;
-                unsigned char* st = smem + slot * Lay::STAGE;
-                mbar_expect_tx(&full[slot], nr * (2 * ROWB + 4 * G * 2));
-                bulk_g2s(st + Lay::KC, kw + row * ROWB, nr * ROWB, &full[slot], pol);
-                bulk_g2s(st + Lay::VC, vw + row * ROWB, nr * ROWB, &full[slot], pol);
-                bulk_g2s(st + Lay::KS, ks + row * G * 2, nr * G * 2, &full[slot], pol);
-                bulk_g2s(st + Lay::KB, kb + row * G * 2, nr * G * 2, &full[slot], pol);
-                bulk_g2s(st + Lay::VS, vs + row * G * 2, nr * G * 2, &full[slot], pol);
-                bulk_g2s(st + Lay::VB, vb + row * G * 2, nr * G * 2, &full[slot], pol);
-            }
-        }
+        if (lane == 0) produce<GROUP>(P, smem, full, empty, err_flag, lo, hi, n_stages, rowbase);
     } else {
         // ---------------- consumers --------------------------------------------
         const int r = lane >> 2, j = lane & 3;
@@ -652,7 +726,6 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
         float* mm = mo + CWARPS * 8 * DH;                           // [CWARPS][8]
         float* ml = mm + CWARPS * 8;                                // [CWARPS][8]
         float* mb = ml + CWARPS * 8;                                // [CWARPS][8][G]
-        float* snew = mb + CWARPS * 8 * G;                          // [8]
         if (j == 0 && r < HT) {
             mm[warp * 8 + r] = m_run;
             ml[warp * 8 + r] = l_part;
@@ -672,48 +745,8 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                 mo[(warp * 8 + c1) * DH + dlo + 1] = oacc[i][3];
             }
         }
-        // the step's own entry: s_new[h] = q[h] . new_k / sqrt(DH), at fp32
-        if (with_new && warp == 0) {
-            const __half* nk = static_cast<const __half*>(P.new_k) + ((size_t)b * P.n_kv_heads + hk) * DH;
-            const __half* qb = static_cast<const __half*>(P.q) + ((size_t)b * H + h0) * DH;
-            for (int h = 0; h < nh; ++h) {
-                float part = 0.0f;
-                for (int d = lane; d < DH; d += 32) part = fmaf(__half2float(qb[h * DH + d]), __half2float(nk[d]), part);
-                part = warp_sum(part);
-                if (lane == 0) snew[h] = part * scale2;
-            }
-        }
-        named_sync(1, CWARPS * 32);
-        // ---- merge the warps (and the new entry) into the CTA partial -----------
-        const int bad = *(volatile int*)err_flag;
-        const size_t rows = (size_t)P.b_rows * H;
-        const __half* nv = static_cast<const __half*>(P.new_v) + ((size_t)b * P.n_kv_heads + hk) * DH;
-        for (int idx = tid; idx < nh * DH; idx += CWARPS * 32) {
-            const int h = idx / DH, d = idx % DH, g = d / GROUP;
-            float M = with_new ? snew[h] : -INFINITY;
-#pragma unroll
-            for (int w = 0; w < CWARPS; ++w) M = fmaxf(M, mm[w * 8 + h]);
-            float o = 0.0f, l = 0.0f;
-#pragma unroll
-            for (int w = 0; w < CWARPS; ++w) {
-                const float mw = mm[w * 8 + h];
-                if (mw == -INFINITY) continue;
-                const float e = ex2(mw - M);
-                o = fmaf(mo[(w * 8 + h) * DH + d] + mb[(w * 8 + h) * G + g], e, o);
-                l = fmaf(ml[w * 8 + h], e, l);
-            }
-            if (with_new) {
-                const float e = ex2(snew[h] - M);
-                o = fmaf(__half2float(nv[d]), e, o);
-                l += e;
-            }
-            const size_t row = split * rows + (size_t)b * H + h0 + h;
-            part_o[row * DH + d] = bad ? __int_as_float(0x7fc00000) : o;
-            if (d == 0) {
-                part_m[row] = bad ? __int_as_float(0x7fc00000) : M * LN2;  // natural-log units
-                part_l[row] = bad ? __int_as_float(0x7fc00000) : l;
-            }
-        }
+        finish_partial<HT, GROUP>(P, smem, tid, warp, lane, split, b, hk, h0, nh, with_new, scale2,
+                                  err_flag, part_o, part_m, part_l);
     }
     // a failed wait may leave copies in flight into this CTA's shared memory:
     // let the producer wait for them (bounded) before the CTA retires

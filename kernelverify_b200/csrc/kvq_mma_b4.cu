@@ -1,12 +1,23 @@
-// Tensor-core partial kernels (fp16 steps, 4-bit caches, head_dim 128).
+// Register-fragment tensor-core partial kernels (fp16 steps, 4-bit caches,
+// head_dim 128): the transposed-score kernel for group 64, the original one
+// for groups 32 and 128.
 #include <atomic>
 
 #include "kvq_launch.h"
 #include "kvq_mma.cuh"
+#include "kvq_mmat.cuh"
 
 namespace kvq {
 
 constexpr int kMaxDevices = 64;
+
+template <int HT, int GROUP>
+constexpr auto mma4_kernel() {
+    if constexpr (GROUP == 64)
+        return mma4::partial_kernel_t<HT>;
+    else
+        return mma4::partial_kernel<HT, GROUP>;
+}
 
 // The kernel's attributes (dynamic shared memory above 48 KB; a carveout that
 // prefers shared memory, so three CTAs fit on an SM), set once per device so
@@ -19,7 +30,7 @@ static cudaError_t mma4_prepare() {
     if (e != cudaSuccess) return e;
     const uint64_t bit = dev >= 0 && dev < kMaxDevices ? 1ull << dev : 0;
     if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
-    auto kernel = mma4::partial_kernel<HT, GROUP>;
+    auto kernel = mma4_kernel<HT, GROUP>();
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)mma4::smem_bytes<GROUP>());
     if (e != cudaSuccess) return e;
@@ -35,7 +46,7 @@ static cudaError_t mma4_one(const Problem& P, float* o, float* m, float* l, cuda
     cudaError_t e = mma4_prepare<HT, GROUP>();
     if (e != cudaSuccess) return e;
     dim3 grid(P.n_splits, P.n_kv_heads * P.head_tiles, P.b_rows);
-    mma4::partial_kernel<HT, GROUP><<<grid, mma4::THREADS, mma4::smem_bytes<GROUP>(), stream>>>(P, o, m, l);
+    mma4_kernel<HT, GROUP>()<<<grid, mma4::THREADS, mma4::smem_bytes<GROUP>(), stream>>>(P, o, m, l);
     return cudaGetLastError();
 }
 
@@ -47,7 +58,7 @@ static int mma4_occupancy() {
     int n = cached[dev].load(std::memory_order_relaxed);
     if (n > 0) return n;
     if (mma4_prepare<HT, GROUP>() != cudaSuccess) return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, mma4::partial_kernel<HT, GROUP>,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, mma4_kernel<HT, GROUP>(),
                                                       mma4::THREADS,
                                                       mma4::smem_bytes<GROUP>()) != cudaSuccess)
         return 0;
