@@ -231,11 +231,11 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
 // Part p's O row starts at part_o + p * o_stride + row * head_dim and its m, l
 // at part_m / part_l + p * ml_stride + row, so stacked partials ([P, rows, DH]
 // and [P, rows]) and partial records laid end to end are both served.
-// Phase 1 stages the parts' m in shared memory and takes their max; phase 2
-// turns them into weights e^(m_p - m) there and sums l; phase 3 has warp w sum
-// the parts w, w+8, ... (lane owns dims lane, lane+32, ...), four parts' loads
-// in flight at a time with no load waiting on another, and the eight warp sums
-// meet in shared memory. head_dim is a multiple of 32, at most 256; n_parts at
+// The first 32 parts' O rows are loaded up front (warp w: parts w, w+8, w+16,
+// w+24; lane owns dims lane, lane+32, ...); meanwhile the parts' m and l are
+// staged in shared memory and reduced to the max and to weights e^(m_p - m)
+// with l = sum l_p e^(m_p - m); further parts follow four per warp at a time,
+// no load waiting on another, and the eight warp sums meet in shared memory. head_dim is a multiple of 32, at most 256; n_parts at
 // most MERGE_MAX_PARTS.
 // NORMALIZE: out = sum_p O_p e^(m_p - m) / l in TO. Otherwise the merged
 // partial (O unnormalised, m, l) in fp32. A part with m = -inf (an empty
@@ -253,15 +253,30 @@ merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
              uint32_t head_dim, uint64_t o_stride, uint64_t ml_stride, TO* __restrict__ out,
              float* __restrict__ out_m, float* __restrict__ out_l) {
     __shared__ float s_w[MERGE_MAX_PARTS];
+    __shared__ float s_l[MERGE_MAX_PARTS];
     __shared__ float s_red[2][MERGE_WARPS];
     __shared__ float s_o[MERGE_WARPS][MERGE_MAX_DH];
     const uint32_t row = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per_lane = (int)head_dim / 32;
+    const float* orow = part_o + (size_t)row * head_dim + lane;
 
+    // the first MERGE_WARPS * MERGE_UNROLL parts' O rows are requested before
+    // anything else, so their latency overlaps the m and l phases
+    float ov0[MERGE_UNROLL][MERGE_MAX_DH / 32];
+#pragma unroll
+    for (int u = 0; u < MERGE_UNROLL; ++u) {
+        const uint32_t p = warp + u * MERGE_WARPS;
+        const float* o = orow + p * o_stride;
+#pragma unroll
+        for (int k = 0; k < MERGE_MAX_DH / 32; ++k)
+            ov0[u][k] = (p < n_parts && k < per_lane) ? o[32 * k] : 0.0f;
+    }
     float m = -INFINITY;
     for (uint32_t p = tid; p < n_parts; p += MERGE_THREADS) {
         const float v = part_m[p * ml_stride + row];
         s_w[p] = v;
+        s_l[p] = part_l[p * ml_stride + row];
         m = fmaxf(m, v);
     }
     m = warp_max(m);
@@ -277,7 +292,7 @@ merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
         const float v = s_w[p];
         const float w = v == -INFINITY ? 0.0f : expf(v - m);
         s_w[p] = w;
-        if (w != 0.0f) l = fmaf(part_l[p * ml_stride + row], w, l);
+        if (w != 0.0f) l = fmaf(s_l[p], w, l);
     }
     l = warp_sum(l);
     if (lane == 0) s_red[1][warp] = l;
@@ -286,12 +301,18 @@ merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
 #pragma unroll
     for (int w = 0; w < MERGE_WARPS; ++w) lt += s_red[1][w];
 
-    const int per_lane = (int)head_dim / 32;
-    const float* orow = part_o + (size_t)row * head_dim + lane;
     float acc[MERGE_MAX_DH / 32];
 #pragma unroll
     for (int k = 0; k < MERGE_MAX_DH / 32; ++k) acc[k] = 0.0f;
-    for (uint32_t p0 = warp; p0 < n_parts; p0 += MERGE_WARPS * MERGE_UNROLL) {
+#pragma unroll
+    for (int u = 0; u < MERGE_UNROLL; ++u) {
+        const uint32_t p = warp + u * MERGE_WARPS;
+        const float w = p < n_parts ? s_w[p] : 0.0f;
+#pragma unroll
+        for (int k = 0; k < MERGE_MAX_DH / 32; ++k)
+            if (w != 0.0f) acc[k] = fmaf(ov0[u][k], w, acc[k]);
+    }
+    for (uint32_t p0 = warp + MERGE_WARPS * MERGE_UNROLL; p0 < n_parts; p0 += MERGE_WARPS * MERGE_UNROLL) {
         float wv[MERGE_UNROLL];
         float ov[MERGE_UNROLL][MERGE_MAX_DH / 32];
 #pragma unroll
