@@ -69,6 +69,10 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the bounded CPU-baseline sample of the ours arm")
+    ap.add_argument("--transport", default="auto", choices=("auto", "peer", "nccl"),
+                    help="config 5: partials merged over peer memory in one kernel (the "
+                         "default on more than one GPU), or all-gathered with NCCL (on one "
+                         "GPU: the local merge of the one record)")
     return ap.parse_args(argv)
 
 
@@ -280,8 +284,11 @@ def run_ours(args) -> dict | None:
 
     if args.config == 5:
         from kernelverify_b200.pack.tsplit import SequenceSplitDecoder
+        if args.transport == "auto":
+            args.transport = "peer" if world > 1 else "nccl"
         decoder = SequenceSplitDecoder(cfg["B"], cfg["H"], cfg["DH"], device,
-                                       group=dist.group.WORLD if dist is not None else None)
+                                       group=dist.group.WORLD if dist is not None else None,
+                                       transport=args.transport)
 
     def splits(i):
         """The dominant kernel alone: the split stage over cache set i."""
@@ -309,8 +316,8 @@ def run_ours(args) -> dict | None:
         eager_step(i)
     barrier(dist)
     # one CUDA graph per cache set: a replayed step makes no host calls
-    # (config 5 on N ranks: the graph holds the local partial; the all-gather
-    # and the merge stay eager, so the process group's timeout watches them)
+    # (config 5 over NCCL on N ranks: the graph holds the local partial; the
+    # all-gather and the merge stay eager, under the process group's timeout)
     pool = torch.cuda.graph_pool_handle()
     graphs = []
     for i in range(n_sets):
@@ -325,9 +332,10 @@ def run_ours(args) -> dict | None:
         graphs.append(g)
 
     def graph_step(i):
-        graphs[i % n_sets].replay()
-        if args.config == 5 and world > 1:
-            decoder.finish(q.dtype, out=out)
+        if args.config == 2:
+            graphs[i % n_sets].replay()
+        else:
+            graphs[i % n_sets].replay(out=out)
 
     for i in range(n_sets):
         graph_step(i)
@@ -401,8 +409,11 @@ def run_ours(args) -> dict | None:
                "path": ("kernelverify_b200.pack.kv_attention.decode -> kvq_decode (C ABI)"
                         if args.config == 2 else
                         "kernelverify_b200.pack.tsplit.SequenceSplitDecoder.step -> "
-                        "kvq_decode_partial, NCCL all-gather, kvq_lse_merge_records (C ABI)")}
+                        + ("kvq_decode_partial, kvq_peer_merge (C ABI)" if args.transport == "peer"
+                           else "kvq_decode_partial, NCCL all-gather, kvq_lse_merge_records (C ABI)"))}
 
+    if args.config == 5:
+        decoder.close()
     if rank != 0:
         if dist is not None:
             dist.destroy_process_group()
@@ -437,7 +448,8 @@ def run_ours(args) -> dict | None:
                    "t_cached": cfg["T"], "bits": cfg["bits"], "group": cfg["group"],
                    "per_rank_t": t_rows, "n_splits": n_splits,
                    "l2": f"inputs larger than L2: {n_sets} cache sets of {local_kv / 1e6:.1f} MB rotated",
-                   "kv_bytes_per_step": step_kv, "parallelism": f"dp{world}" if args.config == 2 else f"tsplit{world}"},
+                   "kv_bytes_per_step": step_kv,
+                   "parallelism": f"dp{world}" if args.config == 2 else f"tsplit{world}-{args.transport}"},
         "hbm_frac_step": round(value / world / peak, 4) if args.config == 2 else round(value / world / peak, 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),

@@ -153,6 +153,43 @@ int kvq_lse_merge_records(const float* records, uint32_t n_parts, uint32_t rows,
                           uint32_t head_dim, uint32_t out_dtype, void* out, void* stream);
 
 /*
+ * Sequence split over peer memory (no reference counterpart; the reference
+ * has no multi-GPU path). Each rank allocates one exchange region in its own
+ * GPU memory (kvq_peer_alloc, zeroed, exported as a 64-byte CUDA IPC handle),
+ * every rank maps every peer's region (kvq_peer_open, from its own device),
+ * and each step:
+ *   1. the local partial (kvq_decode_partial) writes this rank's record into
+ *      its own region at kvq_peer_record_offset(rows, head_dim, parity) --
+ *      O [rows, head_dim], then m [rows], then l [rows], fp32 -- where parity
+ *      is (step number + 1) & 1, steps counted from 0 on every rank alike;
+ *   2. kvq_peer_merge publishes the record to the peers (a flag store into each
+ *      peer's region after a system-scope fence), waits for every peer's flag
+ *      of this step in its own region (bounded by timeout_us, 0 = 2 s), and
+ *      merges all ranks' records by log-sum-exp reading them over NVLink:
+ *      out [rows, head_dim] in out_dtype, identical on every rank.
+ * regions[p] is rank p's region as mapped in this process (this rank's own at
+ * regions[rank]). A wait that times out sets the region's status word (read
+ * it with kvq_peer_status) and writes NaN rows; the kernel always returns.
+ * Regions must be freed (kvq_peer_free) only after every peer has closed its
+ * mapping (kvq_peer_close).
+ */
+#define KVQ_PEER_MAX_RANKS 8
+#define KVQ_PEER_HANDLE_BYTES 64
+size_t kvq_peer_region_bytes(uint32_t rows, uint32_t head_dim);
+size_t kvq_peer_record_offset(uint32_t rows, uint32_t head_dim, uint32_t parity);
+int kvq_peer_alloc(size_t bytes, void** region, void* ipc_handle);
+int kvq_peer_open(const void* ipc_handle, void** region);
+int kvq_peer_close(void* region);
+int kvq_peer_free(void* region);
+int kvq_peer_merge(void* const* regions, uint32_t world, uint32_t rank, uint32_t parity,
+                   uint32_t rows, uint32_t head_dim, uint32_t out_dtype, void* out,
+                   uint64_t timeout_us, void* stream);
+/* status word of a region: 0 ok, 1 a peer's flag did not arrive in time */
+int kvq_peer_status(const void* region, uint32_t* status, void* stream);
+/* the calling thread's last error from a kvq_peer_* call ("" when none) */
+const char* kvq_peer_last_error(void);
+
+/*
  * fp32 dequantized values [rows, head_dim] of a packed artefact: scale * code
  * + bias per group, a rounded multiply then a rounded add -- bit-exact to the
  * reference's _cache_dequant (kernelverify/reference/native_kernels.py:153-165,

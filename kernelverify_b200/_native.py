@@ -18,11 +18,16 @@ KVQ_OK, KVQ_ERR_INVALID, KVQ_ERR_LAUNCH, KVQ_ERR_UNSUPPORTED = 0, -1, -2, -3
 KVQ_F16, KVQ_F32 = 0, 1
 KVQ_T_END_ALL = 0xFFFFFFFF
 KVQ_NOALLOC_SCRATCH_BYTES = 16 << 20
+KVQ_PEER_MAX_RANKS = 8
+KVQ_PEER_HANDLE_BYTES = 64
 
 # Every symbol include/kvq_b200.h declares.
 EXPORTS = ("kvq_workspace_bytes", "kvq_decode", "kvq_decode_partial", "kvq_split_count",
            "kvq_decode_splits", "kvq_lse_merge", "kvq_lse_merge_records", "kvq_decode_noalloc",
-           "kvq_dequant", "kvq_quantize", "kvq_supports", "kvq_last_error", "kvq_abi_version")
+           "kvq_dequant", "kvq_quantize", "kvq_supports", "kvq_last_error", "kvq_abi_version",
+           "kvq_peer_region_bytes", "kvq_peer_record_offset", "kvq_peer_alloc", "kvq_peer_open",
+           "kvq_peer_close", "kvq_peer_free", "kvq_peer_merge", "kvq_peer_status",
+           "kvq_peer_last_error")
 
 
 class NativeUnavailable(RuntimeError):
@@ -74,6 +79,15 @@ def _declare(lib) -> None:
         "kvq_supports": (I, [U32, U32, U32, U32]),
         "kvq_last_error": (ctypes.c_char_p, []),
         "kvq_abi_version": (I, []),
+        "kvq_peer_region_bytes": (SZ, [U32, U32]),
+        "kvq_peer_record_offset": (SZ, [U32, U32, U32]),
+        "kvq_peer_alloc": (I, [SZ, ctypes.POINTER(ctypes.c_void_p), P]),
+        "kvq_peer_open": (I, [P, ctypes.POINTER(ctypes.c_void_p)]),
+        "kvq_peer_close": (I, [P]),
+        "kvq_peer_free": (I, [P]),
+        "kvq_peer_merge": (I, [P, U32, U32, U32, U32, U32, U32, P, U64, P]),
+        "kvq_peer_status": (I, [P, ctypes.POINTER(ctypes.c_uint32), P]),
+        "kvq_peer_last_error": (ctypes.c_char_p, []),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -105,3 +119,9 @@ def lib():
 def check(status: int) -> None:
     if status != KVQ_OK:
         raise KvqError(status, lib().kvq_last_error().decode(errors="replace"))
+
+
+def check_peer(status: int) -> None:
+    """check() for the kvq_peer_* entries, which keep their own last error."""
+    if status != KVQ_OK:
+        raise KvqError(status, lib().kvq_peer_last_error().decode(errors="replace"))

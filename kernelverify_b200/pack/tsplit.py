@@ -11,11 +11,19 @@ and every rank merges them with `kvq_lse_merge`:
     m = max_r m_r,  l = sum_r l_r e^(m_r - m),  out = sum_r O_r e^(m_r - m) / l.
 
 Batch x KV-head work is never split across ranks; only T is.
+
+Two transports move the partials. "nccl": one all_gather_into_tensor of the
+ranks' fp32 records (O, m, l) and kvq_lse_merge_records. "peer": every rank's
+record stays in an exchange region in its own GPU memory, mapped into the
+peers over CUDA IPC, and kvq_peer_merge publishes, waits (bounded) and merges
+in one kernel reading the peers' records over NVLink -- no collective, so a
+whole step can be captured in a CUDA graph.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+import ctypes
+from dataclasses import dataclass, field
 
 # Shard starts are multiples of this many positions, so every rank's rows
 # stay on the tensor-core kernel's 8-row TMA alignment.
@@ -39,15 +47,116 @@ def owns_new_entry(world: int, rank: int) -> bool:
     return rank == world - 1
 
 
+class PeerExchange:
+    """The ranks' exchange regions: this rank's own (allocated, zeroed) and
+    every peer's, mapped over CUDA IPC. Create it on every rank of `group`
+    together; close() it on every rank together."""
+
+    def __init__(self, rows: int, head_dim: int, device, group=None, timeout_us: int = 2_000_000):
+        import torch
+        from kernelverify_b200 import _native
+        lib = _native.lib()
+        self.rows, self.head_dim, self.timeout_us = rows, head_dim, timeout_us
+        self.group = group
+        self.world = 1 if group is None else torch.distributed.get_world_size(group)
+        self.rank = 0 if group is None else torch.distributed.get_rank(group)
+        if self.world > _native.KVQ_PEER_MAX_RANKS:
+            raise ValueError(f"the peer transport serves at most {_native.KVQ_PEER_MAX_RANKS} ranks")
+        self.device = torch.device(device)
+        self.nbytes = lib.kvq_peer_region_bytes(rows, head_dim)
+        handle = (ctypes.c_char * _native.KVQ_PEER_HANDLE_BYTES)()
+        own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _native.check_peer(lib.kvq_peer_alloc(self.nbytes, ctypes.byref(own), handle))
+        self.own = own.value
+        handles = [bytes(handle)]
+        if self.world > 1:
+            handles = [None] * self.world
+            torch.distributed.all_gather_object(handles, bytes(handle), group=group)
+        self.regions = []
+        with torch.cuda.device(self.device):
+            for p, h in enumerate(handles):
+                if p == self.rank:
+                    self.regions.append(self.own)
+                    continue
+                ptr = ctypes.c_void_p()
+                buf = (ctypes.c_char * _native.KVQ_PEER_HANDLE_BYTES).from_buffer_copy(h)
+                _native.check_peer(lib.kvq_peer_open(buf, ctypes.byref(ptr)))
+                self.regions.append(ptr.value)
+        self._array = (ctypes.c_void_p * self.world)(*self.regions)
+        if self.world > 1:
+            torch.distributed.barrier(group=group)   # every mapping exists before first use
+
+    def record(self, parity: int) -> tuple[int, int, int]:
+        """Device addresses (O, m, l) of this rank's record of `parity`."""
+        from kernelverify_b200 import _native
+        base = self.own + _native.lib().kvq_peer_record_offset(self.rows, self.head_dim, parity)
+        o_bytes = self.rows * self.head_dim * 4
+        return base, base + o_bytes, base + o_bytes + self.rows * 4
+
+    def merge(self, parity: int, out, stream=None) -> None:
+        """All ranks' records of `parity` merged into out [rows, head_dim]."""
+        import torch
+        from kernelverify_b200 import _native
+        from kernelverify_b200.pack.kv_attention import _dtype_code
+        s = stream if stream is not None else torch.cuda.current_stream(out.device)
+        _native.check_peer(_native.lib().kvq_peer_merge(
+            self._array, self.world, self.rank, parity, self.rows, self.head_dim,
+            _dtype_code(out.dtype), out.data_ptr(), self.timeout_us, s.cuda_stream))
+
+    def status(self) -> int:
+        """0, or 1 when a peer's flag did not arrive in time."""
+        import torch
+        from kernelverify_b200 import _native
+        v = ctypes.c_uint32()
+        with torch.cuda.device(self.device):
+            _native.check_peer(_native.lib().kvq_peer_status(
+                self.own, ctypes.byref(v), torch.cuda.current_stream(self.device).cuda_stream))
+        return v.value
+
+    def close(self) -> None:
+        import torch
+        from kernelverify_b200 import _native
+        if not self.regions:
+            return
+        lib = _native.lib()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p, ptr in enumerate(self.regions):
+                if p != self.rank:
+                    _native.check_peer(lib.kvq_peer_close(ptr))
+            if self.world > 1:
+                torch.distributed.barrier(group=self.group)   # no peer maps us any more
+            _native.check_peer(lib.kvq_peer_free(self.own))
+        self.regions = []
+
+
+@dataclass
+class CapturedStep:
+    """A step captured as CUDA graphs; replay() runs the next one."""
+
+    decoder: "SequenceSplitDecoder"
+    graphs: tuple
+    finish: bool = False        # the all-gather and merge follow the replay eagerly
+
+    def replay(self, out=None):
+        dec = self.decoder
+        g = self.graphs[dec._parity()] if len(self.graphs) == 2 else self.graphs[0]
+        g.replay()
+        if self.finish:
+            dec.finish(dec._dtype, out=out)
+        dec.steps += 1
+
+
 @dataclass
 class SequenceSplitDecoder:
     """One decode step over a T-sharded cache, reusing its buffers.
 
     `group` is a torch.distributed process group (None: a single rank). The
     local cache tensors hold only this rank's rows ([HKV, T_local, ...] or
-    [B, HKV, T_local, ...]); positions are local to them. Each rank's partial
-    lands in one fp32 record (O, then m, then l), so a step makes one
-    all-gather; `capture` records a whole step as a CUDA graph.
+    [B, HKV, T_local, ...]); positions are local to them. `transport` is
+    "nccl" (one all-gather of fp32 records, then kvq_lse_merge_records) or
+    "peer" (kvq_peer_merge over the ranks' exchange regions).
     """
 
     b_rows: int
@@ -55,33 +164,64 @@ class SequenceSplitDecoder:
     head_dim: int
     device: object
     group: object = None
+    transport: str = "nccl"
+    steps: int = field(default=0, init=False)
 
     def __post_init__(self):
         import torch
         from kernelverify_b200.pack.kv_attention import Workspace, record_floats, record_views
+        if self.transport not in ("nccl", "peer"):
+            raise ValueError(f"transport {self.transport!r} is not 'nccl' or 'peer'")
         self.world = 1 if self.group is None else torch.distributed.get_world_size(self.group)
         self.rank = 0 if self.group is None else torch.distributed.get_rank(self.group)
-        n = record_floats(self.b_rows * self.n_heads, self.head_dim)
+        rows = self.b_rows * self.n_heads
+        self.workspace = Workspace()
+        self._dtype = None
+        if self.transport == "peer":
+            self.exchange = PeerExchange(rows, self.head_dim, self.device, self.group)
+            return
+        n = record_floats(rows, self.head_dim)
         self.records = torch.empty((self.world, n), dtype=torch.float32, device=self.device)
         self.record = torch.empty((n,), dtype=torch.float32, device=self.device)
         self.part_o, self.part_m, self.part_l = record_views(self.record, self.b_rows,
                                                              self.n_heads, self.head_dim)
-        self.workspace = Workspace()
+
+    def _parity(self) -> int:
+        return (self.steps + 1) & 1
 
     def partial(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
-                bits: int, t_local: int):
+                bits: int, t_local: int, parity: int | None = None):
         """This rank's partial into its record (the local step alone)."""
+        import torch
+        from kernelverify_b200 import _native
         from kernelverify_b200.pack import kv_attention as kva
-        kva.decode_partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
-                           bits=bits, t_begin=0, t_end=t_local, t_cached=t_local,
-                           has_new_entry=owns_new_entry(self.world, self.rank),
-                           part_o=self.part_o, part_m=self.part_m, part_l=self.part_l,
-                           workspace=self.workspace)
+        has_new = owns_new_entry(self.world, self.rank)
+        if self.transport == "nccl":
+            kva.decode_partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
+                               bits=bits, t_begin=0, t_end=t_local, t_cached=t_local,
+                               has_new_entry=has_new, part_o=self.part_o, part_m=self.part_m,
+                               part_l=self.part_l, workspace=self.workspace)
+            return
+        a = kva._args(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
+                      bits=bits, t_cached=t_local, t_begin=0, t_end=t_local, has_new_entry=has_new)
+        lib = _native.lib()
+        o, m, l = self.exchange.record(self._parity() if parity is None else parity)
+        need = lib.kvq_workspace_bytes(a)
+        buf, have = self.workspace.get(need, q.device)
+        _native.check(lib.kvq_decode_partial(a, o, m, l, buf.data_ptr() if buf is not None else None,
+                                             have, torch.cuda.current_stream(q.device).cuda_stream))
 
-    def finish(self, out_dtype, out=None):
+    def finish(self, out_dtype, out=None, parity: int | None = None):
         """Gather every rank's record and merge them: out [B, H, DH]."""
         import torch
         from kernelverify_b200.pack import kv_attention as kva
+        if out is None:
+            out = torch.empty((self.b_rows, self.n_heads, self.head_dim), dtype=out_dtype,
+                              device=self.device)
+        if self.transport == "peer":
+            self.exchange.merge(self._parity() if parity is None else parity,
+                                out.view(self.b_rows * self.n_heads, self.head_dim))
+            return out
         if self.group is None:
             self.records[0].copy_(self.record)
         else:
@@ -94,24 +234,41 @@ class SequenceSplitDecoder:
         """out [B, H, DH] in q's dtype, identical on every rank."""
         self.partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
                      bits=bits, t_local=t_local)
-        return self.finish(q.dtype, out=out)
+        res = self.finish(q.dtype, out=out)
+        self.steps += 1
+        return res
 
     def capture(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
-                bits: int, t_local: int, out=None, pool=None):
-        """A CUDA graph of this rank's local work on these tensors; replay it
-        and then call `finish` for the step. With one rank (group None) the
-        graph holds the whole step, writing `out`. With more, it holds the
-        partial only: the all-gather stays an eager NCCL call, watched by the
-        process group's timeout (a collective inside a graph is not). Run one
-        eager `step` first (it sets the kernels' attributes and sizes the
-        workspace)."""
+                bits: int, t_local: int, out, pool=None) -> CapturedStep:
+        """This step on these tensors as CUDA graphs; `.replay()` reruns it on
+        whatever they then hold. With the peer transport, or with one rank,
+        the graphs hold the whole step (one graph per record parity for the
+        peer transport). With NCCL on more ranks they hold the partial only and
+        the all-gather and merge run eagerly after each replay: a collective
+        inside a graph is outside the process group's timeout. Run one eager
+        `step` first (it sets the kernels' attributes and sizes the workspace)."""
         import torch
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, pool=pool):
+        self._dtype = q.dtype
+        args = (q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v)
+        if self.transport == "peer":
+            graphs = []
+            for parity in (0, 1):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, pool=pool):
+                    self.partial(*args, bits=bits, t_local=t_local, parity=parity)
+                    self.finish(q.dtype, out=out, parity=parity)
+                graphs.append(g)
+            return CapturedStep(self, tuple(graphs))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=pool):
             if self.group is None:
-                self.step(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
-                          bits=bits, t_local=t_local, out=out)
+                self.partial(*args, bits=bits, t_local=t_local)
+                self.finish(q.dtype, out=out)
             else:
-                self.partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k,
-                             new_v, bits=bits, t_local=t_local)
-        return graph
+                self.partial(*args, bits=bits, t_local=t_local)
+        return CapturedStep(self, (g,), finish=self.group is not None)
+
+    def close(self) -> None:
+        """Release the peer transport's regions (on every rank together)."""
+        if self.transport == "peer":
+            self.exchange.close()

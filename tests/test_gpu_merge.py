@@ -110,3 +110,70 @@ def test_single_rank_sequence_split_eager_and_graph(native):
     v2 = kv.verify_output(kv.gqa_tiled_inputs(q2, kc, vc, nk, nv, 4), replayed.cpu().numpy())
     assert v2.ok, v2
     del graph
+
+
+def test_single_rank_peer_transport_eager_and_graph(native):
+    """The peer transport on one rank: its record and kvq_peer_merge give the
+    oracle's verdict, and the graphs (one per record parity) replay it."""
+    import torch
+    from kernelverify_b200.pack.tsplit import SequenceSplitDecoder
+    from tests.kvq_cases import pack, to_dev
+    t = 5000
+    q, kc, vc, nk, nv = cases.make_case(1, 64, t, 128, seed=23)
+    kc, vc, nk, nv = kc[:8], vc[:8], nk[:, :8], nv[:, :8]
+    dev = [to_dev(x) for x in (q, *pack(kc, 4), *pack(vc, 4), nk, nv)]
+    dec = SequenceSplitDecoder(1, 64, 128, torch.device("cuda"), transport="peer")
+    try:
+        out = torch.empty_like(dev[0])
+        for _ in range(3):   # both record parities, eagerly
+            dec.step(*dev, bits=4, t_local=t, out=out)
+            torch.cuda.synchronize()
+            v = kv.verify_output(kv.gqa_tiled_inputs(q, kc, vc, nk, nv, 4), out.cpu().numpy())
+            assert v.ok, v
+        step = dec.capture(*dev, bits=4, t_local=t, out=out)
+        for _ in range(3):
+            out.zero_()
+            step.replay(out=out)
+            torch.cuda.synchronize()
+            v = kv.verify_output(kv.gqa_tiled_inputs(q, kc, vc, nk, nv, 4), out.cpu().numpy())
+            assert v.ok, v
+        assert dec.exchange.status() == 0
+        del step
+    finally:
+        dec.close()
+
+
+def test_peer_merge_wait_runs_out_and_reports(native):
+    """A rank whose peer never publishes: the merge's wait on a flag that
+    nothing sets expires (bounded), the region's status says so, the rows are
+    NaN, and the device stays usable. Both regions are on this GPU and only
+    one merge kernel runs, so nothing waits on another kernel."""
+    import ctypes
+    import torch
+    from kernelverify_b200 import _native
+    lib = _native.lib()
+    rows, dh = 4, 128
+    nbytes = lib.kvq_peer_region_bytes(rows, dh)
+    regions = []
+    for _ in range(2):
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_char * _native.KVQ_PEER_HANDLE_BYTES)()
+        _native.check_peer(lib.kvq_peer_alloc(nbytes, ctypes.byref(ptr), handle))
+        regions.append(ptr.value)
+    try:
+        arr = (ctypes.c_void_p * 2)(*regions)
+        out = torch.zeros((rows, dh), dtype=torch.float32, device="cuda")
+        _native.check_peer(lib.kvq_peer_merge(arr, 2, 0, 1, rows, dh, _native.KVQ_F32, out.data_ptr(),
+                                              200_000, torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        st = ctypes.c_uint32()
+        _native.check_peer(lib.kvq_peer_status(regions[0], ctypes.byref(st),
+                                               torch.cuda.current_stream().cuda_stream))
+        assert st.value == 1
+        assert torch.isnan(out).all()
+        # the context is intact: an ordinary kernel still runs
+        assert float((torch.ones(1000, device="cuda") * 2).sum()) == 2000.0
+    finally:
+        torch.cuda.synchronize()
+        for r in regions:
+            _native.check_peer(lib.kvq_peer_free(r))
