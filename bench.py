@@ -295,12 +295,16 @@ def run_ours(args) -> dict | None:
         _native.check(lib.kvq_decode_splits(margs[i % n_sets], po.data_ptr(), pm.data_ptr(),
                                             pl.data_ptr(), torch.cuda.current_stream().cuda_stream))
 
+    ws_need = lib.kvq_workspace_bytes(margs[0])
+    ws = torch.empty(ws_need + 256, dtype=torch.uint8, device=device)
+    ws_base = (ws.data_ptr() + 255) // 256 * 256
+
     def eager_step(i):
         if args.config == 2:
-            splits(i)
-            _native.check(lib.kvq_lse_merge(po.data_ptr(), pm.data_ptr(), pl.data_ptr(), n_splits,
-                                            rows, cfg["DH"], 0, out.data_ptr(),
-                                            torch.cuda.current_stream().cuda_stream))
+            # the full step through the C ABI: the split stage, then the merge
+            # of its splits
+            _native.check(lib.kvq_decode(margs[i % n_sets], out.data_ptr(), ws_base, ws_need,
+                                         torch.cuda.current_stream().cuda_stream))
         else:
             kw, ks, kb, vw, vs, vb = sets[i % n_sets]
             decoder.step(q, kw, ks, kb, vw, vs, vb, nk, nv, bits=cfg["bits"], t_local=t_rows,
@@ -308,7 +312,9 @@ def run_ours(args) -> dict | None:
 
     # kernels of ours per step: partial + merge (config 2); partial, its local
     # merge when split, and the cross-rank merge (config 5)
-    launches_per_step = 2 if args.config == 2 else (3 if n_splits > 1 else 2)
+    # our kernels per step: the split stage and the merge of its splits;
+    # config 5 adds the merge of the ranks' records
+    launches_per_step = 2 + (1 if args.config == 5 else 0)
 
     sampler = ClockSampler(local)
     sampler.start()
