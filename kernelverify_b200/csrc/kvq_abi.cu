@@ -87,6 +87,14 @@ int kernel_override() {
     return -1;
 }
 
+// KVQ_PRECISION=fast lets the register-fragment tensor-core kernels carry the
+// combine's weights p * v_scale as two bf16 parts (2^-16 relative) instead of
+// three (2^-23, binary32-class: the contract's working-precision clause C1).
+bool fast_precision() {
+    const char* v = getenv("KVQ_PRECISION");
+    return v != nullptr && strcmp(v, "fast") == 0;
+}
+
 // Split plan of the tensor-core kernel. Its CTAs run in waves of the resident
 // CTAs (per SM x SMs); a CTA costs its chunk of positions plus a fixed ramp
 // (barrier setup, the first copies' latency, the epilogue) worth about two
@@ -224,7 +232,8 @@ int plan(const kvq_args* a, Plan* pl) {
 cudaError_t launch_partial_any(const Plan& pl, uint32_t bits, uint32_t dtype, uint32_t dh,
                                float* o, float* m, float* l, cudaStream_t s) {
     if (pl.kernel == KERNEL_UMMA4) return kvq::launch_umma4(pl.P, pl.ht, o, m, l, s);
-    if (pl.kernel == KERNEL_MMA4) return kvq::launch_mma4(pl.P, pl.ht, pl.P.group_size, o, m, l, s);
+    if (pl.kernel == KERNEL_MMA4)
+        return kvq::launch_mma4(pl.P, pl.ht, pl.P.group_size, fast_precision() ? 2 : 3, o, m, l, s);
     switch (bits) {
         case 2: return kvq::launch_partial<2>(pl.P, dtype, dh, pl.ht, o, m, l, s);
         case 3: return kvq::launch_partial<3>(pl.P, dtype, dh, pl.ht, o, m, l, s);

@@ -27,7 +27,9 @@ cudaError_t launch_dequant(const uint32_t* wq, const void* scales, const void* b
                            float* out, cudaStream_t stream);
 
 // Tensor-core partial kernel: fp16, 4-bit, head_dim 128, ht in {4, 8}.
-cudaError_t launch_mma4(const Problem& P, int ht, int group, float* part_o, float* part_m,
+// parts: 3 (binary32-class combine weights, the default) or 2 (the opt-in
+// fast precision)
+cudaError_t launch_mma4(const Problem& P, int ht, int group, int parts, float* part_o, float* part_m,
                         float* part_l, cudaStream_t stream);
 
 // Merges of n_parts partials; part p's O block starts o_stride floats after

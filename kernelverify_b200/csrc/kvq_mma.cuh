@@ -16,9 +16,9 @@
 //           the dot product is a reassociation of the reference's
 //           sum_d q_d (s c_d + b) (contract clause C2).
 //   combine O[h,d] = sum_t P'[h,t,g] * code[t,d] + sum_t p[h,t] * v_bias[t,g],
-//           P' = p * v_scale, carried as two bf16 parts hi + lo that
-//           reproduce P' to 2^-16 relative (the kernel serves fp16 outputs,
-//           whose tolerance is 4 fp16 ulps of max|ref|), times the exact bf16
+//           P' = p * v_scale, carried as three bf16 parts hi + mid + lo that
+//           reproduce P' to 2^-23 relative (binary32-class; PARTS = 2 keeps
+//           hi + lo, 2^-16, the opt-in fast precision), times the exact bf16
 //           codes on the tensor cores (mma m16n8k16 bf16, exact products,
 //           fp32 accumulation).
 // The MMA shapes are chosen so the score accumulator fragment IS the
@@ -216,6 +216,24 @@ __device__ __forceinline__ void split2(float x0, float x1, uint32_t& p_hi, uint3
     p_lo = pack_bf16(r.x, r.y);
 }
 
+// Three packed bf16x2 parts: hi and mid are truncations (each residual exact
+// in fp32), lo is the second residual rounded to nearest bf16, so
+// |x - hi - mid - lo| <= 2^-23 |x|: binary32-class, every intermediate of the
+// combine at least as precise as fp32 arithmetic (contract clause C1).
+__device__ __forceinline__ void split3(float x0, float x1, uint32_t& p_hi, uint32_t& p_mid,
+                                       uint32_t& p_lo) {
+    const float2 neg1 = make_float2(-1.0f, -1.0f);
+    p_hi = prmt<0x7632>(__float_as_uint(x0), __float_as_uint(x1));
+    const float2 r = __ffma2_rn(make_float2(__uint_as_float(p_hi * 65536u),
+                                            __uint_as_float(p_hi & 0xFFFF0000u)),
+                                neg1, make_float2(x0, x1));
+    p_mid = prmt<0x7632>(__float_as_uint(r.x), __float_as_uint(r.y));
+    const float2 r2 = __ffma2_rn(make_float2(__uint_as_float(p_mid * 65536u),
+                                             __uint_as_float(p_mid & 0xFFFF0000u)),
+                                 neg1, r);
+    p_lo = pack_bf16(r2.x, r2.y);
+}
+
 __device__ __forceinline__ float h2f(const __half* p) { return __half2float(*p); }
 
 // 2^x; flushes results below 2^-126 to zero (those weights are negligible
@@ -364,7 +382,7 @@ __device__ __forceinline__ void finish_partial(const Problem& P, unsigned char* 
 }
 
 // -----------------------------------------------------------------------------
-template <int HT, int GROUP>
+template <int HT, int GROUP, int PARTS>
 __global__ void __launch_bounds__(THREADS, GROUP == 32 ? 2 : KVQ_MMA_MINBLOCKS)
 partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m,
                float* __restrict__ part_l) {
@@ -623,7 +641,7 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                 // B fragments (k rows 2j, 2j+1 <-> positions j, j+4; 2j+8, 2j+9
                 // <-> 8+j, 12+j; column r): bf0/bf1 for the first MMA of a tile,
                 // bs0/bs1 for the second (HT = 8 only).
-                uint32_t bf0[G], bf1[G], bs0[G], bs1[G];
+                uint32_t bf0[G], bf1[G], bs0[G], bs1[G], bt0[G], bt1[G];
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
                     // bias with the codes' +128 offset folded in: b - 128 s
@@ -637,17 +655,37 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                         // from the partner lane r^4 (lane ^ 16), which holds the
                         // same head: one exchange carries what each side lacks.
                         const float2 v = __fmul2_rn(make_float2(e[0], e[1]), make_float2(vsf[0][g], vsf[1][g]));
-                        uint32_t hi, lo;
-                        split2(v.x, v.y, hi, lo);
-                        const uint32_t recv = __shfl_xor_sync(0xffffffffu, half ? hi : lo, 16);
+                        uint32_t hi, mid, lo;
+                        if constexpr (PARTS == 3) {
+                            split3(v.x, v.y, hi, mid, lo);
+                        } else {
+                            split2(v.x, v.y, hi, mid);
+                            lo = 0u;
+                        }
+                        // first MMA: hi (columns 0..3) and mid (or lo at PARTS = 2,
+                        // columns 4..7); second MMA (PARTS = 3): lo in columns 0..3
+                        const uint32_t recv = __shfl_xor_sync(0xffffffffu, half ? hi : mid, 16);
                         bf0[g] = half ? recv : hi;
-                        bf1[g] = half ? lo : recv;
-                        bs0[g] = bs1[g] = 0u;
+                        bf1[g] = half ? mid : recv;
+                        if constexpr (PARTS == 3) {
+                            const uint32_t recv_lo = __shfl_xor_sync(0xffffffffu, lo, 16);
+                            bs0[g] = half ? 0u : lo;
+                            bs1[g] = half ? 0u : recv_lo;
+                        } else {
+                            bs0[g] = bs1[g] = 0u;
+                        }
+                        bt0[g] = bt1[g] = 0u;
                     } else {
                         const float2 v01 = __fmul2_rn(make_float2(e[0], e[1]), make_float2(vsf[0][g], vsf[1][g]));
                         const float2 v23 = __fmul2_rn(make_float2(e[2], e[3]), make_float2(vsf[2][g], vsf[3][g]));
-                        split2(v01.x, v01.y, bf0[g], bs0[g]);
-                        split2(v23.x, v23.y, bf1[g], bs1[g]);
+                        if constexpr (PARTS == 3) {
+                            split3(v01.x, v01.y, bf0[g], bs0[g], bt0[g]);
+                            split3(v23.x, v23.y, bf1[g], bs1[g], bt1[g]);
+                        } else {
+                            split2(v01.x, v01.y, bf0[g], bs0[g]);
+                            split2(v23.x, v23.y, bf1[g], bs1[g]);
+                            bt0[g] = bt1[g] = 0u;
+                        }
                     }
                 }
                 // A fragments: V codes^T, rows = dims, cols = positions
@@ -695,8 +733,10 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
                         // a2/a3: the same for positions 8+j, 12+j
                         float (&acc)[4] = oacc[g * MTG + ii];
                         mma_bf16(acc, fa[ii][0], fa[ii][1], fa[ii][2], fa[ii][3], bf0[g], bf1[g]);
-                        if constexpr (HT == 8)
+                        if constexpr (HT == 8 || PARTS == 3)
                             mma_bf16(acc, fa[ii][0], fa[ii][1], fa[ii][2], fa[ii][3], bs0[g], bs1[g]);
+                        if constexpr (HT == 8 && PARTS == 3)
+                            mma_bf16(acc, fa[ii][0], fa[ii][1], fa[ii][2], fa[ii][3], bt0[g], bt1[g]);
                     }
                 }
             }
@@ -715,7 +755,7 @@ partial_kernel(Problem P, float* __restrict__ part_o, float* __restrict__ part_m
             if constexpr (HT == 4) bsum[g] += __shfl_xor_sync(0xffffffffu, bsum[g], 16);
         }
         if constexpr (HT == 4) {
-            // columns 4..7 carry the lo parts of heads 0..3: fold them in
+            // columns 4..7 carry the mid (or lo) parts of heads 0..3: fold them in
 #pragma unroll
             for (int i = 0; i < MT; ++i)
 #pragma unroll

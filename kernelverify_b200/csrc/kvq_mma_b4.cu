@@ -11,18 +11,18 @@ namespace kvq {
 
 constexpr int kMaxDevices = 64;
 
-template <int HT, int GROUP>
+template <int HT, int GROUP, int PARTS>
 constexpr auto mma4_kernel() {
     if constexpr (GROUP == 64)
-        return mma4::partial_kernel_t<HT>;
+        return mma4::partial_kernel_t<HT, PARTS>;
     else
-        return mma4::partial_kernel<HT, GROUP>;
+        return mma4::partial_kernel<HT, GROUP, PARTS>;
 }
 
 // The kernel's attributes (dynamic shared memory above 48 KB; a carveout that
 // prefers shared memory, so three CTAs fit on an SM), set once per device so
 // that later launches, captured ones included, make no attribute calls.
-template <int HT, int GROUP>
+template <int HT, int GROUP, int PARTS>
 static cudaError_t mma4_prepare() {
     static std::atomic<uint64_t> done{0};
     int dev = 0;
@@ -30,7 +30,7 @@ static cudaError_t mma4_prepare() {
     if (e != cudaSuccess) return e;
     const uint64_t bit = dev >= 0 && dev < kMaxDevices ? 1ull << dev : 0;
     if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
-    auto kernel = mma4_kernel<HT, GROUP>();
+    auto kernel = mma4_kernel<HT, GROUP, PARTS>();
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)mma4::smem_bytes<GROUP>());
     if (e != cudaSuccess) return e;
@@ -41,24 +41,25 @@ static cudaError_t mma4_prepare() {
     return cudaSuccess;
 }
 
-template <int HT, int GROUP>
+template <int HT, int GROUP, int PARTS>
 static cudaError_t mma4_one(const Problem& P, float* o, float* m, float* l, cudaStream_t stream) {
-    cudaError_t e = mma4_prepare<HT, GROUP>();
+    cudaError_t e = mma4_prepare<HT, GROUP, PARTS>();
     if (e != cudaSuccess) return e;
     dim3 grid(P.n_splits, P.n_kv_heads * P.head_tiles, P.b_rows);
-    mma4_kernel<HT, GROUP>()<<<grid, mma4::THREADS, mma4::smem_bytes<GROUP>(), stream>>>(P, o, m, l);
+    mma4_kernel<HT, GROUP, PARTS>()<<<grid, mma4::THREADS, mma4::smem_bytes<GROUP>(), stream>>>(P, o, m, l);
     return cudaGetLastError();
 }
 
 template <int HT, int GROUP>
 static int mma4_occupancy() {
+    constexpr int PARTS = 3;
     static std::atomic<int> cached[kMaxDevices] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
     int n = cached[dev].load(std::memory_order_relaxed);
     if (n > 0) return n;
-    if (mma4_prepare<HT, GROUP>() != cudaSuccess) return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, mma4_kernel<HT, GROUP>(),
+    if (mma4_prepare<HT, GROUP, PARTS>() != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, mma4_kernel<HT, GROUP, PARTS>(),
                                                       mma4::THREADS,
                                                       mma4::smem_bytes<GROUP>()) != cudaSuccess)
         return 0;
@@ -96,18 +97,25 @@ int sm_count() {
     return n;
 }
 
-cudaError_t launch_mma4(const Problem& P, int ht, int group, float* o, float* m, float* l,
-                        cudaStream_t stream) {
+template <int PARTS>
+static cudaError_t launch_parts(const Problem& P, int ht, int group, float* o, float* m, float* l,
+                                cudaStream_t stream) {
     if (ht == 4) {
-        if (group == 32) return mma4_one<4, 32>(P, o, m, l, stream);
-        if (group == 64) return mma4_one<4, 64>(P, o, m, l, stream);
-        if (group == 128) return mma4_one<4, 128>(P, o, m, l, stream);
+        if (group == 32) return mma4_one<4, 32, PARTS>(P, o, m, l, stream);
+        if (group == 64) return mma4_one<4, 64, PARTS>(P, o, m, l, stream);
+        if (group == 128) return mma4_one<4, 128, PARTS>(P, o, m, l, stream);
     } else if (ht == 8) {
-        if (group == 32) return mma4_one<8, 32>(P, o, m, l, stream);
-        if (group == 64) return mma4_one<8, 64>(P, o, m, l, stream);
-        if (group == 128) return mma4_one<8, 128>(P, o, m, l, stream);
+        if (group == 32) return mma4_one<8, 32, PARTS>(P, o, m, l, stream);
+        if (group == 64) return mma4_one<8, 64, PARTS>(P, o, m, l, stream);
+        if (group == 128) return mma4_one<8, 128, PARTS>(P, o, m, l, stream);
     }
     return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_mma4(const Problem& P, int ht, int group, int parts, float* o, float* m, float* l,
+                        cudaStream_t stream) {
+    return parts == 2 ? launch_parts<2>(P, ht, group, o, m, l, stream)
+                      : launch_parts<3>(P, ht, group, o, m, l, stream);
 }
 
 }  // namespace kvq

@@ -31,7 +31,7 @@ __device__ __forceinline__ uint32_t transpose8x8(uint32_t x) {
     return y;
 }
 
-template <int HT>
+template <int HT, int PARTS>
 __global__ void __launch_bounds__(THREADS, KVQ_MMA_MINBLOCKS)
 partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part_m,
                  float* __restrict__ part_l) {
@@ -275,7 +275,10 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
             for (int i = 0; i < NSC; ++i) l_part[i & 1] += e[i];
 
             // ---- combine: B fragments of P' = p * v_scale by transposition --
-            uint32_t bf0[G], bf1[G], bs0[G], bs1[G];
+            // first MMA (bf), second (bs), third (bt): at HT = 4 the first takes
+            // hi (columns 0..3) and mid (columns 4..7; lo at PARTS = 2), the
+            // second lo in columns 0..3; at HT = 8 one MMA per part
+            uint32_t bf0[G], bf1[G], bs0[G], bs1[G], bt0[G], bt1[G];
             if constexpr (HT == 4) {
                 const int lp = kr0 + 8 * half;
                 float vf[2 * G];
@@ -285,15 +288,26 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
                     bsum[g][0] = fmaf(e[0], vf[G + g], bsum[g][0]);
                     bsum[g][1] = fmaf(e[1], vf[G + g], bsum[g][1]);
                     const float2 v = __fmul2_rn(make_float2(e[0], e[1]), make_float2(vf[g], vf[g]));
-                    uint32_t phi, plo;
-                    split2(v.x, v.y, phi, plo);
-                    // matrix rows r <-> positions kr0 (m0) and kr0 + 8 (m1), columns
-                    // hi of heads 0..3 then lo of heads 0..3; the partner lane j^2
-                    // holds the other row's parts of the same heads
-                    const uint32_t recv = __shfl_xor_sync(0xffffffffu, half ? phi : plo, 2);
+                    uint32_t phi, pmid, plo;
+                    if constexpr (PARTS == 3) {
+                        split3(v.x, v.y, phi, pmid, plo);
+                    } else {
+                        split2(v.x, v.y, phi, pmid);
+                        plo = 0u;
+                    }
+                    // matrix rows r <-> positions kr0 (m0) and kr0 + 8 (m1); the
+                    // partner lane j^2 holds the other row's parts of the same heads
+                    const uint32_t recv = __shfl_xor_sync(0xffffffffu, half ? phi : pmid, 2);
                     bf0[g] = transpose8x8(half ? recv : phi);
-                    bf1[g] = transpose8x8(half ? plo : recv);
-                    bs0[g] = bs1[g] = 0u;
+                    bf1[g] = transpose8x8(half ? pmid : recv);
+                    if constexpr (PARTS == 3) {
+                        const uint32_t recv_lo = __shfl_xor_sync(0xffffffffu, plo, 2);
+                        bs0[g] = transpose8x8(half ? 0u : plo);
+                        bs1[g] = transpose8x8(half ? 0u : recv_lo);
+                    } else {
+                        bs0[g] = bs1[g] = 0u;
+                    }
+                    bt0[g] = bt1[g] = 0u;
                 }
             } else {
                 float vf[2][2 * G];
@@ -301,19 +315,30 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
                 load_f<2 * G>(vscr + (kr0 + 8) * 2 * G, vf[1]);
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    uint32_t phi[2], plo[2];
+                    uint32_t phi[2], pmid[2], plo[2];
 #pragma unroll
                     for (int rr = 0; rr < 2; ++rr) {
                         bsum[g][0] = fmaf(e[2 * rr], vf[rr][G + g], bsum[g][0]);
                         bsum[g][1] = fmaf(e[2 * rr + 1], vf[rr][G + g], bsum[g][1]);
                         const float2 v = __fmul2_rn(make_float2(e[2 * rr], e[2 * rr + 1]),
                                                     make_float2(vf[rr][g], vf[rr][g]));
-                        split2(v.x, v.y, phi[rr], plo[rr]);
+                        if constexpr (PARTS == 3) {
+                            split3(v.x, v.y, phi[rr], pmid[rr], plo[rr]);
+                        } else {
+                            split2(v.x, v.y, phi[rr], pmid[rr]);
+                            plo[rr] = 0u;
+                        }
                     }
                     bf0[g] = transpose8x8(phi[0]);
                     bf1[g] = transpose8x8(phi[1]);
-                    bs0[g] = transpose8x8(plo[0]);
-                    bs1[g] = transpose8x8(plo[1]);
+                    bs0[g] = transpose8x8(pmid[0]);
+                    bs1[g] = transpose8x8(pmid[1]);
+                    if constexpr (PARTS == 3) {
+                        bt0[g] = transpose8x8(plo[0]);
+                        bt1[g] = transpose8x8(plo[1]);
+                    } else {
+                        bt0[g] = bt1[g] = 0u;
+                    }
                 }
             }
             // A fragments (V codes^T) and the MMAs, as partial_kernel
@@ -335,7 +360,10 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
                 for (int ii = 0; ii < MTG; ++ii) {
                     float (&o)[4] = oacc[g * MTG + ii];
                     mma_bf16(o, fa[ii][0], fa[ii][1], fa[ii][2], fa[ii][3], bf0[g], bf1[g]);
-                    if constexpr (HT == 8) mma_bf16(o, fa[ii][0], fa[ii][1], fa[ii][2], fa[ii][3], bs0[g], bs1[g]);
+                    if constexpr (HT == 8 || PARTS == 3)
+                        mma_bf16(o, fa[ii][0], fa[ii][1], fa[ii][2], fa[ii][3], bs0[g], bs1[g]);
+                    if constexpr (HT == 8 && PARTS == 3)
+                        mma_bf16(o, fa[ii][0], fa[ii][1], fa[ii][2], fa[ii][3], bt0[g], bt1[g]);
                 }
             }
             __syncwarp();
@@ -358,7 +386,7 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
             }
         }
         if constexpr (HT == 4) {
-            // columns 4..7 carry the lo parts of heads 0..3: fold them in
+            // columns 4..7 carry the mid (or lo) parts of heads 0..3: fold them in
 #pragma unroll
             for (int i = 0; i < MT; ++i)
 #pragma unroll

@@ -1,9 +1,10 @@
 """The tensor-core kernels (fp16, 4-bit, head_dim 128, 8-row-aligned geometry)
 and the CUDA-core kernel on the same inputs: each passes the oracle, and they
 agree with each other to 2e-3 of the output's max magnitude (the tensor-core
-kernels carry the V-side weights to 2^-16 relative). KVQ_KERNEL=generic
-forces the CUDA-core kernel for a call, KVQ_KERNEL=umma the tcgen05 kernel
-(group 64; other groups keep the register-fragment kernel)."""
+kernels carry the V-side weights to 2^-23 relative by default, 2^-16 with
+KVQ_PRECISION=fast). KVQ_KERNEL=generic forces the CUDA-core kernel for a
+call, KVQ_KERNEL=umma the tcgen05 kernel (group 64; other groups keep the
+register-fragment kernel)."""
 
 from __future__ import annotations
 
@@ -18,18 +19,23 @@ from tests.kvq_cases import judge_gqa, judge_per_sequence, pack, run_decode, to_
 pytestmark = pytest.mark.gpu
 
 
-def run_with(kernel, fn):
+def run_with(kernel, fn, precision=None):
     if kernel is not None:
         os.environ["KVQ_KERNEL"] = kernel
+    if precision is not None:
+        os.environ["KVQ_PRECISION"] = precision
     try:
         return fn()
     finally:
         os.environ.pop("KVQ_KERNEL", None)
+        os.environ.pop("KVQ_PRECISION", None)
 
 
 def kernels(fn):
-    """(default tensor-core, tcgen05, CUDA-core) outputs of the same call."""
-    return run_with(None, fn), run_with("umma", fn), run_with("generic", fn)
+    """(default tensor-core, tcgen05, CUDA-core) outputs of the same call; the
+    default kernel's fast precision is checked against the oracle here too."""
+    fast = run_with(None, fn, "fast")
+    return run_with(None, fn), run_with("umma", fn), run_with("generic", fn), fast
 
 
 def close(a, b, rel=2e-3):
@@ -43,11 +49,11 @@ def test_tensor_core_path_gqa_and_groups(native, h, hkv, group):
     t = 1000   # not a multiple of the 64-position stage: the tail is masked
     q, kc, vc, nk, nv = cases.make_case(2, h, t, 128, seed=h * 7 + hkv + group)
     kc, vc, nk, nv = kc[:hkv], vc[:hkv], nk[:, :hkv], nv[:, :hkv]
-    mma, umma, gen = kernels(lambda: run_decode(q, kc, vc, nk, nv, 4, group))
-    for out in (mma, umma, gen):
+    mma, umma, gen, fast = kernels(lambda: run_decode(q, kc, vc, nk, nv, 4, group))
+    for out in (mma, umma, gen, fast):
         v = judge_gqa(q, kc, vc, nk, nv, 4, out, group)
         assert v.ok, v
-    assert close(mma, gen) and close(umma, gen)
+    assert close(mma, gen) and close(umma, gen) and close(fast, gen)
 
 
 @pytest.mark.parametrize("t", [1, 7, 8, 63, 64, 65, 129, 4096, 9000])
@@ -60,12 +66,12 @@ def test_tensor_core_path_lengths(native, t):
     junk = rng.standard_normal((2, t_pad - t, 128)).astype(np.float16) * 30
     k_art = pack(np.concatenate([kc, junk], axis=1), 4)
     v_art = pack(np.concatenate([vc, junk], axis=1), 4)
-    mma, umma, gen = kernels(lambda: run_decode(q, None, None, nk, nv, 4, t_cached=t, k_art=k_art,
+    mma, umma, gen, fast = kernels(lambda: run_decode(q, None, None, nk, nv, 4, t_cached=t, k_art=k_art,
                                                  v_art=v_art))
-    for out in (mma, umma, gen):
+    for out in (mma, umma, gen, fast):
         v = judge_gqa(q, kc, vc, nk, nv, 4, out)
         assert v.ok, (t, v)
-    assert close(mma, gen) and close(umma, gen)
+    assert close(mma, gen) and close(umma, gen) and close(fast, gen)
 
 
 def test_tensor_core_path_per_sequence_ragged(native):
@@ -77,12 +83,12 @@ def test_tensor_core_path_per_sequence_ragged(native):
     vc = rng.standard_normal((b, hkv, t_pad, 128)).astype(np.float16)
     nk = rng.standard_normal((b, hkv, 128)).astype(np.float16)
     nv = rng.standard_normal((b, hkv, 128)).astype(np.float16)
-    mma, umma, gen = kernels(lambda: run_decode(q, kc, vc, nk, nv, 4, t_cached=int(lens.max()),
+    mma, umma, gen, fast = kernels(lambda: run_decode(q, kc, vc, nk, nv, 4, t_cached=int(lens.max()),
                                                  seq_lens=lens))
-    for out in (mma, umma, gen):
+    for out in (mma, umma, gen, fast):
         for v in judge_per_sequence(q, kc, vc, nk, nv, 4, out, lens):
             assert v.ok, v
-    assert close(mma, gen) and close(umma, gen)
+    assert close(mma, gen) and close(umma, gen) and close(fast, gen)
 
 
 @pytest.mark.parametrize("kernel", [None, "umma"])
@@ -111,7 +117,7 @@ def test_outlier_caches(native):
     raw[rng.random(raw.shape) < 0.01] *= 20
     raw = raw.astype(np.float16)
     kc, vc = raw[0], raw[1]
-    mma, umma, gen = kernels(lambda: run_decode(q, kc, vc, nk, nv, 4))
-    for out in (mma, umma, gen):
+    mma, umma, gen, fast = kernels(lambda: run_decode(q, kc, vc, nk, nv, 4))
+    for out in (mma, umma, gen, fast):
         for v in judge_per_sequence(q, kc, vc, nk, nv, 4, out):
             assert v.ok, v
