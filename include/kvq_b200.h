@@ -212,6 +212,31 @@ int kvq_quantize(const void* w, uint64_t rows, uint32_t head_dim, uint32_t bits,
                  void* biases, void* stream);
 
 /*
+ * Append n_new positions of every (sequence, cache head) to a packed cache
+ * with the same quantizer: w [b_rows, n_kv_heads, n_new, head_dim] dtype;
+ * row (b, hk, j) is quantized into cache row
+ *   b * cache_batch_stride + hk * t_stride + pos_b + j
+ * of wq/scales/biases (the cache's base pointers), pos_b = positions[b] read
+ * on the device when `positions` is non-NULL (an int32 [b_rows] device
+ * array, so a captured decode step appends where the device says), else
+ * `position` for every row. Rows at or past t_stride are not written (a
+ * device position is not visible to the host check, which covers `position`).
+ * b_rows > 1 needs cache_batch_stride >= n_kv_heads * t_stride.
+ *
+ * The serving cache's update step: the reference's mlx-lm QuantizedKVCache
+ * quantizes each step's keys/values into its padded buffers before attention
+ * (reached through the runtime patch of bench/spike_mlx_e2e.py:103-123, whose
+ * fused arm then reads the padded buffers with the logical length); here the
+ * quantizer is the canonical one above, so appended rows are bit-identical to
+ * kvq_quantize of the same values.
+ */
+int kvq_cache_append(const void* w, uint32_t b_rows, uint32_t n_kv_heads, uint32_t n_new,
+                     uint32_t head_dim, uint32_t bits, uint32_t group_size, uint32_t dtype,
+                     const int32_t* positions, uint32_t position, uint32_t t_stride,
+                     uint64_t cache_batch_stride, uint32_t* wq, void* scales, void* biases,
+                     void* stream);
+
+/*
  * The full step like kvq_decode, for callers that cannot allocate device
  * memory: a host that binds this library through a plain C FFI and owns no
  * CUDA allocator (a cgo / JNI / ctypes worker), or a serving process that

@@ -24,7 +24,7 @@ KVQ_PEER_HANDLE_BYTES = 64
 # Every symbol include/kvq_b200.h declares.
 EXPORTS = ("kvq_workspace_bytes", "kvq_decode", "kvq_decode_partial", "kvq_split_count",
            "kvq_decode_splits", "kvq_lse_merge", "kvq_lse_merge_records", "kvq_decode_noalloc",
-           "kvq_dequant", "kvq_quantize", "kvq_supports", "kvq_last_error", "kvq_abi_version",
+           "kvq_dequant", "kvq_quantize", "kvq_cache_append", "kvq_supports", "kvq_last_error", "kvq_abi_version",
            "kvq_peer_region_bytes", "kvq_peer_record_offset", "kvq_peer_alloc", "kvq_peer_open",
            "kvq_peer_close", "kvq_peer_free", "kvq_peer_merge", "kvq_peer_status",
            "kvq_peer_last_error")
@@ -76,6 +76,7 @@ def _declare(lib) -> None:
         "kvq_decode_noalloc": (I, [AP, P, P]),
         "kvq_dequant": (I, [P, P, P, U64, U32, U32, U32, U32, P, P]),
         "kvq_quantize": (I, [P, U64, U32, U32, U32, U32, P, P, P, P]),
+        "kvq_cache_append": (I, [P, U64, U32, U32, U32, U32, P, P, P, U64, P]),
         "kvq_supports": (I, [U32, U32, U32, U32]),
         "kvq_last_error": (ctypes.c_char_p, []),
         "kvq_abi_version": (I, []),

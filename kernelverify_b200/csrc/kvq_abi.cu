@@ -506,6 +506,22 @@ int kvq_dequant(const uint32_t* wq, const void* scales, const void* biases, uint
     return KVQ_OK;
 }
 
+static int quantize_rows(const void* w, uint64_t rows, uint32_t head_dim, uint32_t bits,
+                         uint32_t group_size, uint32_t dtype, uint32_t* wq, void* scales,
+                         void* biases, const kvq::QuantDest& dst, void* stream) {
+    auto s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaErrorInvalidValue;
+    switch (bits) {
+        case 2: e = kvq::launch_quantize<2>(w, rows, head_dim, group_size, dtype, wq, scales, biases, dst, s); break;
+        case 3: e = kvq::launch_quantize<3>(w, rows, head_dim, group_size, dtype, wq, scales, biases, dst, s); break;
+        case 4: e = kvq::launch_quantize<4>(w, rows, head_dim, group_size, dtype, wq, scales, biases, dst, s); break;
+        case 6: e = kvq::launch_quantize<6>(w, rows, head_dim, group_size, dtype, wq, scales, biases, dst, s); break;
+        case 8: e = kvq::launch_quantize<8>(w, rows, head_dim, group_size, dtype, wq, scales, biases, dst, s); break;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "quantize kernel launch");
+    return KVQ_OK;
+}
+
 int kvq_quantize(const void* w, uint64_t rows, uint32_t head_dim, uint32_t bits, uint32_t group_size,
                  uint32_t dtype, uint32_t* wq, void* scales, void* biases, void* stream) {
     g_error.clear();
@@ -515,17 +531,36 @@ int kvq_quantize(const void* w, uint64_t rows, uint32_t head_dim, uint32_t bits,
     if (rows == 0) return KVQ_OK;
     rc = device_ok();
     if (rc) return rc;
-    auto s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaErrorInvalidValue;
-    switch (bits) {
-        case 2: e = kvq::launch_quantize<2>(w, rows, head_dim, group_size, dtype, wq, scales, biases, s); break;
-        case 3: e = kvq::launch_quantize<3>(w, rows, head_dim, group_size, dtype, wq, scales, biases, s); break;
-        case 4: e = kvq::launch_quantize<4>(w, rows, head_dim, group_size, dtype, wq, scales, biases, s); break;
-        case 6: e = kvq::launch_quantize<6>(w, rows, head_dim, group_size, dtype, wq, scales, biases, s); break;
-        case 8: e = kvq::launch_quantize<8>(w, rows, head_dim, group_size, dtype, wq, scales, biases, s); break;
-    }
-    if (e != cudaSuccess) return cuda_fail(e, "quantize kernel launch");
-    return KVQ_OK;
+    const kvq::QuantDest dst{nullptr, 0u, 1u, 0u, 0u, 0u};
+    return quantize_rows(w, rows, head_dim, bits, group_size, dtype, wq, scales, biases, dst, stream);
+}
+
+int kvq_cache_append(const void* w, uint32_t b_rows, uint32_t n_kv_heads, uint32_t n_new,
+                     uint32_t head_dim, uint32_t bits, uint32_t group_size, uint32_t dtype,
+                     const int32_t* positions, uint32_t position, uint32_t t_stride,
+                     uint64_t cache_batch_stride, uint32_t* wq, void* scales, void* biases,
+                     void* stream) {
+    g_error.clear();
+    int rc = check_format(head_dim, bits, group_size, dtype);
+    if (rc) return rc;
+    if (!w || !wq || !scales || !biases) return fail(KVQ_ERR_INVALID, "a pointer is NULL");
+    if (b_rows == 0 || n_kv_heads == 0 || n_new == 0) return KVQ_OK;
+    if (t_stride == 0) return fail(KVQ_ERR_INVALID, "t_stride is 0");
+    if (!positions && (uint64_t)position + n_new > t_stride)
+        return fail(KVQ_ERR_INVALID, "position %u + n_new %u runs past t_stride %u", position,
+                    n_new, t_stride);
+    if (b_rows > 1 && cache_batch_stride != 0 &&
+        cache_batch_stride < (uint64_t)n_kv_heads * t_stride)
+        return fail(KVQ_ERR_INVALID, "cache_batch_stride %llu overlaps the %u x %u rows of a "
+                    "sequence", (unsigned long long)cache_batch_stride, n_kv_heads, t_stride);
+    if (b_rows > 1 && cache_batch_stride == 0)
+        return fail(KVQ_ERR_INVALID, "b_rows > 1 needs one cache per sequence "
+                    "(cache_batch_stride > 0): appends of a shared cache would collide");
+    rc = device_ok();
+    if (rc) return rc;
+    const uint64_t rows = (uint64_t)b_rows * n_kv_heads * n_new;
+    const kvq::QuantDest dst{positions, position, n_kv_heads, n_new, t_stride, cache_batch_stride};
+    return quantize_rows(w, rows, head_dim, bits, group_size, dtype, wq, scales, biases, dst, stream);
 }
 
 }  // extern "C"

@@ -119,4 +119,19 @@ struct Problem {
     float scale;         // 1/sqrt(head_dim)
 };
 
+// Where quantized input rows land. The input is [seqs, heads, n_new, DH]
+// row-major; input row (b, hk, j) is written to output row
+//   b * batch_stride + hk * t_stride + pos_b + j,
+// pos_b = positions[b] (device) when positions is set, else `position`.
+// Rows whose position reaches t_stride are not written. n_new = 0 is a plain
+// quantize: input row r is output row r.
+struct QuantDest {
+    const int32_t* positions;
+    uint32_t position;
+    uint32_t heads;
+    uint32_t n_new;
+    uint32_t t_stride;
+    uint64_t batch_stride;
+};
+
 }  // namespace kvq

@@ -19,7 +19,7 @@ cudaError_t launch_partial(const Problem& P, int dtype, int head_dim, int ht, fl
 template <int BITS>
 cudaError_t launch_quantize(const void* w, uint64_t rows, uint32_t head_dim, uint32_t group,
                             int dtype, uint32_t* wq, void* scales, void* biases,
-                            cudaStream_t stream);
+                            const QuantDest& dst, cudaStream_t stream);
 
 template <int BITS>
 cudaError_t launch_dequant(const uint32_t* wq, const void* scales, const void* biases,

@@ -22,7 +22,8 @@ __device__ __forceinline__ float round_half_away(float x) {
 template <typename T, int BITS>
 __global__ void __launch_bounds__(128)
 quantize_kernel(const T* __restrict__ w, uint64_t rows, uint32_t head_dim, uint32_t group,
-                uint32_t* __restrict__ wq, T* __restrict__ scales, T* __restrict__ biases) {
+                uint32_t* __restrict__ wq, T* __restrict__ scales, T* __restrict__ biases,
+                QuantDest dst) {
     constexpr int CC = Chunk<BITS>::CODES;
     constexpr int CW = Chunk<BITS>::WORDS;
     const uint32_t groups = head_dim / group;
@@ -31,6 +32,18 @@ quantize_kernel(const T* __restrict__ w, uint64_t rows, uint32_t head_dim, uint3
     const uint64_t row = idx / groups;
     const uint32_t g = (uint32_t)(idx % groups);
     const T* x = w + row * head_dim + (uint64_t)g * group;
+    uint64_t orow = row;
+    if (dst.n_new) {
+        const uint64_t run = row / dst.n_new;
+        const uint32_t j = (uint32_t)(row - run * dst.n_new);
+        const uint64_t b = run / dst.heads;
+        const uint32_t hk = (uint32_t)(run - b * dst.heads);
+        const int32_t pos = dst.positions ? dst.positions[b] : (int32_t)dst.position;
+        if (pos < 0) return;
+        const uint64_t t = (uint64_t)(uint32_t)pos + j;
+        if (t >= dst.t_stride) return;
+        orow = b * dst.batch_stride + (uint64_t)hk * dst.t_stride + t;
+    }
 
     float lo = INFINITY, hi = -INFINITY;
     for (uint32_t i = 0; i < group; ++i) {
@@ -48,11 +61,11 @@ quantize_kernel(const T* __restrict__ w, uint64_t rows, uint32_t head_dim, uint3
     const bool degenerate = n_edge == 0.0f;
     if (!degenerate) step = __fdiv_rn(edge, n_edge);
     const float bias = degenerate ? 0.0f : edge;
-    scales[row * groups + g] = from_f32<T>(step);
-    biases[row * groups + g] = from_f32<T>(bias);
+    scales[orow * groups + g] = from_f32<T>(step);
+    biases[orow * groups + g] = from_f32<T>(bias);
 
     const uint32_t words_per_row = head_dim * BITS / 32;
-    uint32_t* out = wq + row * words_per_row + (uint64_t)g * group * BITS / 32;
+    uint32_t* out = wq + orow * words_per_row + (uint64_t)g * group * BITS / 32;
     for (uint32_t c = 0; c < group / CC; ++c) {
         uint32_t acc[CW];
 #pragma unroll

@@ -309,6 +309,43 @@ def quantize(w, bits: int, group_size: int = 64, stream=None):
     return words, scales, biases
 
 
+def cache_append(w, words, scales, biases, bits: int, *, position: int = 0, positions=None,
+                 stream=None):
+    """Quantize w [B, HKV, L, DH] into positions [pos_b, pos_b + L) of a
+    per-sequence packed cache (words [B, HKV, T_stride, DH*bits/32], scales and
+    biases [B, HKV, T_stride, DH/g]) -- or of a shared [HKV, T_stride, ...]
+    cache when B == 1. pos_b = positions[b] (an int32 [B] CUDA tensor, read on
+    the device) or `position`. Bit-identical to `quantize` of the same rows."""
+    torch = _torch()
+    if w.dim() != 4 or not w.is_cuda or not w.is_contiguous():
+        raise ValueError("w must be a contiguous CUDA tensor [B, HKV, L, DH]")
+    b, hkv, n_new, dh = w.shape
+    per_seq = words.dim() == 4
+    lead = tuple(words.shape[:-2]) if per_seq else (1,) + tuple(words.shape[:-2])
+    if lead != (b, hkv):
+        raise ValueError(f"cache leads with {tuple(words.shape[:-2])}; w is [{b}, {hkv}, ...]")
+    t_stride = words.shape[-2]
+    groups = scales.shape[-1]
+    if groups == 0 or dh % groups or words.shape[-1] * 32 != dh * bits:
+        raise ValueError(f"cache rows do not hold {dh} codes of {bits} bits")
+    for name, ten in (("words", words), ("scales", scales), ("biases", biases)):
+        if not ten.is_cuda or not ten.is_contiguous() or ten.device != w.device:
+            raise ValueError(f"{name} must be a contiguous CUDA tensor on {w.device}")
+        if tuple(ten.shape[:-1]) != tuple(words.shape[:-1]):
+            raise ValueError(f"{name} has shape {tuple(ten.shape)}")
+    if scales.dtype != w.dtype or biases.dtype != w.dtype:
+        raise ValueError("scales and biases must have w's dtype")
+    if positions is not None:
+        if positions.dtype != torch.int32 or tuple(positions.shape) != (b,) or not positions.is_cuda:
+            raise ValueError("positions must be a CUDA int32 tensor [B]")
+    s = stream if stream is not None else torch.cuda.current_stream(w.device)
+    _native.check(_native.lib().kvq_cache_append(
+        w.data_ptr(), b, hkv, n_new, dh, bits, dh // groups, _dtype_code(w.dtype),
+        positions.data_ptr() if positions is not None else None, int(position), t_stride,
+        hkv * t_stride if per_seq else 0, words.data_ptr(), scales.data_ptr(),
+        biases.data_ptr(), s.cuda_stream))
+
+
 def quantize_cache(cache, bits: int, group_size: int = 64):
     """Packed artefact triplet for an (H, T, DH) -- or (B, H, T, DH) -- cache,
     quantized row by row on the device (kernelverify/pack/kv_attention.py:270-283)."""

@@ -1,0 +1,48 @@
+"""The certificate data model, audit and rendering on the CPU: a certificate
+that reads stronger than its evidence is refused (a failing case, C1 missing,
+the fast precision, no byte-bound hashes, no chip)."""
+
+from __future__ import annotations
+
+import json
+
+from kernelverify_b200 import certificate as C
+
+
+def _cert(**kw):
+    base = dict(bits=4, head_dim=128, dtype="float16", policy="p", seed_protocol="s",
+                cases=[C.CaseEvidence("a", True, 1e-5, 1e-3, "00", "tensor-core"),
+                       C.CaseEvidence("b", True, 2e-5, 1e-3, "11", "CUDA-core")],
+                clauses=C.contract_clauses("contract"), translation_unit="ab" * 32,
+                library="cd" * 32, flags=["-O3"], chip="NVIDIA B200",
+                toolchain={"torch": "x"}, budget=2)
+    base.update(kw)
+    return C.Certificate(**base)
+
+
+def test_an_honest_certificate_has_no_complaints():
+    cert = _cert()
+    assert C.audit(cert) == []
+    doc = json.loads(cert.dumps())
+    assert doc["kernel"] == "kv_attn_decode-BITS4-DH128-float16"
+    assert doc["protocol_bound"]["all_passed"] is True
+    assert {c["clause"] for c in doc["attestation"]["clauses"]} == {"C1", "C4", "C5"}
+    assert "Audit complaints" not in C.render_markdown(cert)
+
+
+def test_the_audit_refuses_what_the_evidence_does_not_carry():
+    failing = _cert(cases=[C.CaseEvidence("a", False, 1.0, 1e-3, "00", "k")])
+    assert any("failed" in p for p in C.audit(failing))
+    fast = _cert(clauses=C.contract_clauses("fast"), precision="fast")
+    complaints = C.audit(fast)
+    assert any("C1" in p for p in complaints) and any("precision" in p for p in complaints)
+    assert any("byte-bound" in p for p in C.audit(_cert(library="")))
+    assert any("chip" in p for p in C.audit(_cert(chip="")))
+    assert any("budget" in p for p in C.audit(_cert(budget=5)))
+    assert "Audit complaints" in C.render_markdown(fast)
+
+
+def test_the_translation_unit_hash_covers_the_sources():
+    h = C.translation_unit_sha256()
+    assert len(h) == 64 and h == C.translation_unit_sha256()
+    assert any(f.startswith("-gencode") or "sm_100a" in f for f in C.build_flags())
