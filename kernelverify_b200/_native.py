@@ -76,7 +76,8 @@ def _declare(lib) -> None:
         "kvq_decode_noalloc": (I, [AP, P, P]),
         "kvq_dequant": (I, [P, P, P, U64, U32, U32, U32, U32, P, P]),
         "kvq_quantize": (I, [P, U64, U32, U32, U32, U32, P, P, P, P]),
-        "kvq_cache_append": (I, [P, U64, U32, U32, U32, U32, P, P, P, U64, P]),
+        "kvq_cache_append": (I, [P, U32, U32, U32, U32, U32, U32, U32, P, U32, U32, U64, P, P,
+                                 P, P]),
         "kvq_supports": (I, [U32, U32, U32, U32]),
         "kvq_last_error": (ctypes.c_char_p, []),
         "kvq_abi_version": (I, []),

@@ -1,0 +1,544 @@
+"""Calibration of kv_attention's K over its own ensemble -- TEST INFRASTRUCTURE.
+
+The kv tolerance is max(4 eps(dtype) max|ref|, K * floor), floor = the worst
+of the four fp32 members of KV_MEMBERS, with K = 4.0 borrowed from the
+quantized-matmul calibration and never derived for this operator
+(kernelverify/schemas/native_ops.py:376-394; the queued harness is
+TODOS.md:230-236, modelled on bench/calibrate_quant_bits.py's pre-registered
+rule and on bench/calibrate_k.py's anchored K). This module is that harness,
+CPU only.
+
+PRE-REGISTERED RULE (fixed in this docstring before any number was taken)
+==========================================================================
+Population. Besides the four shipped members, a HELD-OUT population of
+correct implementations of the contract (every intermediate binary32 or
+wider, C1; exponentials shifted by a maximum, C4; the specified formula, C5),
+none of which the floor ever sees:
+
+  split-merge-64 / split-merge-256  T split into chunks, per-chunk fp32
+        (O, m, l), log-sum-exp merge -- the flash-decoding shape of the
+        CUDA kernels here;
+  online-lazy   blockwise online softmax in base 2 with a reference point that
+        moves only when a block's max exceeds it by 8 (weights up to 2^8
+        before normalisation) -- the CUDA kernels' rescaling rule;
+  factored      scores and combine in the integer domain per quantisation
+        group: scale * sum(q * code) + bias * sum(q), and
+        sum_t (p_t scale_t) code_t + sum_t p_t bias_t -- the tensor-core
+        kernels' form (the "factored-form member" the queue names);
+  deferred-norm unnormalised exponentials through the combine, one divide
+        at the end;
+  blocked-16    reductions over DH and over T as serial fp32 sums of blocks
+        of 16, combined pairwise.
+
+Draws. The CALIBRATION draw is the 400-case battery (its case space and
+seeds). The INDEPENDENT draw is the same case space at fresh seeds
+(INDEPENDENT_SEED_BASE + case index), never used to choose anything.
+An EXTENSION draw carries the widths the CUDA library adds (bits 2, 3, 6 and
+groups 32 / 128) over the battery's shapes and both dtypes, iid modes.
+
+Per case:
+  floor_E = max over KV_MEMBERS of |member - ref|      (what ships)
+  floor_C = max over the held-out population of |impl - ref|
+  K_req   = 0 when floor_C <= base_tol, else floor_C / floor_E
+  K_anchored = max K_req over the calibration draw; K_indep over the
+  independent draw; K_ext over the extension draw.
+
+Gates:
+  G1 SOUNDNESS: K = 4.0 passes iff K_anchored, K_indep and K_ext are all
+     <= 4.0 -- no held-out correct implementation is rejected anywhere. A
+     violation is exhibited (case, implementation, err, tol), not inferred.
+  G2 DETECTION: for each K of K_GRID, every fault of the catalogue
+     (oracle/faults.py) is scored on every iid-mode case of the calibration
+     draw; a fault caught on no case at every K is an equivalent mutant at
+     that width and is excluded with that reason. A K "keeps detection" iff it
+     catches every (fault, case) pair K = 4.0 catches. The fp16-score fault is
+     the canary: a K that absolves it on any case it was caught at is
+     rejected outright.
+  G3 MEMBERSHIP: leave-one-member-out K_anchored per member is reported as a
+     necessity diagnostic; it never fails the ensemble.
+
+Decision. If G1 holds, K = 4.0 stands as calibrated, and the report also
+names the smallest grid K that is sound on all three draws and whether it
+keeps detection (if it does, 4.0 is loose by that factor and detection is
+inert between them). If G1 fails, the first repair is MEMBERSHIP: the
+offending held-out implementation's class joins the floor and G1 is re-scored;
+K moves only if membership cannot repair it, and then to the smallest sound
+grid value that keeps the canary.
+
+    python -m oracle.calibrate_k [--jobs 8] [--limit N] [--out report.json]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import sys
+from dataclasses import dataclass
+
+import numpy as np
+
+from oracle import battery, faults, kv
+from oracle.quant import canonical_quantize
+
+K_SHIPPED = kv.K_QUANT
+K_GRID = (0.5, 1.0, 1.25, 1.5, 2.0, 2.5, 3.0, 4.0, 6.0, 10.0)
+INDEPENDENT_SEED_BASE = 50_000
+EXTENSION_SEED_BASE = 90_000
+EXTENSION_BITS = (2, 3, 6)
+EXTENSION_GROUPS = (32, 128)
+CANARY = "kv_attention[scores_dtype=float16]"
+
+
+# ---------------------------------------------------------------------------
+# held-out correct implementations (fp32 throughout)
+# ---------------------------------------------------------------------------
+def _operands(inputs):
+    bits, g = int(inputs["bits"][0]), kv.group_of(inputs)
+    q = inputs["q"].astype(np.float32)
+    kd = kv.dequant64(inputs["k_cache"], bits, g).astype(np.float32)
+    vd = kv.dequant64(inputs["v_cache"], bits, g).astype(np.float32)
+    nk = inputs["new_k"].astype(np.float32)
+    nv = inputs["new_v"].astype(np.float32)
+    scale = np.float32(1.0 / math.sqrt(float(q.shape[-1])))
+    return q, kd, vd, nk, nv, scale
+
+
+def _scores(q, kd, nk, scale):
+    s = np.einsum("bhd,htd->bht", q, kd) * scale
+    s_new = np.sum(q * nk, axis=-1) * scale
+    return s.astype(np.float32), s_new.astype(np.float32)
+
+
+def split_merge(inputs, chunk: int) -> np.ndarray:
+    """Flash-decoding: per-chunk (O, m, l) in fp32, the new entry as its own
+    partial, a log-sum-exp merge in fp32."""
+    q, kd, vd, nk, nv, scale = _operands(inputs)
+    s, s_new = _scores(q, kd, nk, scale)
+    t = kd.shape[1]
+    parts = [(nv[:, :, :], s_new, np.ones_like(s_new))]       # (O, m, l)
+    for c0 in range(0, t, chunk):
+        sc = s[..., c0:c0 + chunk]
+        m = sc.max(axis=-1)
+        e = np.exp(sc - m[..., None]).astype(np.float32)
+        parts.append((np.einsum("bht,htd->bhd", e, vd[:, c0:c0 + chunk]).astype(np.float32),
+                      m, e.sum(axis=-1, dtype=np.float32)))
+    m = np.max(np.stack([p[1] for p in parts]), axis=0)
+    o = np.zeros_like(parts[0][0])
+    lsum = np.zeros_like(m)
+    for po, pm, pl in parts:
+        w = np.exp(pm - m).astype(np.float32)
+        o = (o + w[..., None] * po).astype(np.float32)
+        lsum = (lsum + w * pl).astype(np.float32)
+    return (o / lsum[..., None]).astype(inputs["q"].dtype)
+
+
+def online_lazy(inputs, block: int = 64, slack: float = 8.0) -> np.ndarray:
+    """Base-2 online softmax over blocks of positions; the reference point
+    moves only when a block max exceeds it by `slack` (log2 units)."""
+    q, kd, vd, nk, nv, scale = _operands(inputs)
+    log2e = np.float32(1.4426950408889634)
+    s, s_new = _scores(q, kd, nk, scale)
+    s2 = (s * log2e).astype(np.float32)
+    r = (s_new * log2e).astype(np.float32)                     # start from the new entry
+    acc = nv.copy()
+    lsum = np.ones_like(r)
+    for c0 in range(0, kd.shape[1], block):
+        sb = s2[..., c0:c0 + block]
+        bm = sb.max(axis=-1)
+        move = bm > r + np.float32(slack)
+        new_r = np.where(move, bm, r).astype(np.float32)
+        f = np.exp2(r - new_r).astype(np.float32)
+        acc = (acc * f[..., None]).astype(np.float32)
+        lsum = (lsum * f).astype(np.float32)
+        r = new_r
+        e = np.exp2(sb - r[..., None]).astype(np.float32)
+        acc = (acc + np.einsum("bht,htd->bhd", e, vd[:, c0:c0 + block])).astype(np.float32)
+        lsum = (lsum + e.sum(axis=-1, dtype=np.float32)).astype(np.float32)
+    return (acc / lsum[..., None]).astype(inputs["q"].dtype)
+
+
+def factored(inputs) -> np.ndarray:
+    """Integer-domain scores and combine per quantisation group."""
+    bits, g = int(inputs["bits"][0]), kv.group_of(inputs)
+    q = inputs["q"].astype(np.float32)
+    h, t, dh = inputs["k_cache"].shape
+    groups = dh // g
+
+    def art(cache):
+        codes, sc, bi = canonical_quantize(cache.reshape(h * t, dh), bits, g)
+        return (codes.astype(np.float32).reshape(h, t, groups, g),
+                sc.astype(np.float32).reshape(h, t, groups),
+                bi.astype(np.float32).reshape(h, t, groups))
+
+    kc, ks, kb = art(inputs["k_cache"])
+    vc, vs, vb = art(inputs["v_cache"])
+    scale = np.float32(1.0 / math.sqrt(float(dh)))
+    qg = q.reshape(q.shape[0], h, groups, g)
+    qc = np.einsum("bhgi,htgi->bhtg", qg, kc).astype(np.float32)     # sum q * code per group
+    qs = qg.sum(axis=-1, dtype=np.float32)                             # sum q per group
+    s = ((qc * ks[None] + qs[:, :, None, :] * kb[None]).sum(axis=-1, dtype=np.float32)
+         * scale).astype(np.float32)
+    s_new = (np.sum(q * inputs["new_k"].astype(np.float32), axis=-1) * scale).astype(np.float32)
+    allv = np.concatenate([s, s_new[..., None]], axis=-1)
+    m = allv.max(axis=-1, keepdims=True)
+    e = np.exp(allv - m).astype(np.float32)
+    lsum = e.sum(axis=-1, dtype=np.float32)
+    p = e[..., :t]
+    ps = (p[..., None] * vs[None]).astype(np.float32)                 # p_t * scale_t,g
+    o = np.einsum("bhtg,htgi->bhgi", ps, vc).astype(np.float32)
+    o = o + np.einsum("bht,htg->bhg", p, vb)[..., None].astype(np.float32)
+    o = o.reshape(q.shape) + e[..., t:] * inputs["new_v"].astype(np.float32)
+    return (o / lsum[..., None]).astype(inputs["q"].dtype)
+
+
+def factored_serial(inputs) -> np.ndarray:
+    """The factored form with serial fp32 sums: codes within a group, then
+    groups in order, and the combine over positions in order."""
+    bits, g = int(inputs["bits"][0]), kv.group_of(inputs)
+    q = inputs["q"].astype(np.float32)
+    h, t, dh = inputs["k_cache"].shape
+    groups = dh // g
+
+    def art(cache):
+        codes, sc, bi = canonical_quantize(cache.reshape(h * t, dh), bits, g)
+        return (codes.astype(np.float32).reshape(h, t, groups, g),
+                sc.astype(np.float32).reshape(h, t, groups),
+                bi.astype(np.float32).reshape(h, t, groups))
+
+    def serial(x, axis):
+        return np.add.accumulate(x, axis=axis, dtype=np.float32).take(-1, axis=axis)
+
+    kc, ks, kb = art(inputs["k_cache"])
+    vc, vs, vb = art(inputs["v_cache"])
+    scale = np.float32(1.0 / math.sqrt(float(dh)))
+    qg = q.reshape(q.shape[0], h, 1, groups, g)
+    qc = serial(qg * kc[None], axis=-1)                                # [B, H, T, groups]
+    qs = serial(qg, axis=-1)                                           # [B, H, 1, groups]
+    s = (serial(qc * ks[None] + qs * kb[None], axis=-1) * scale).astype(np.float32)
+    s_new = (serial(q * inputs["new_k"].astype(np.float32), axis=-1) * scale).astype(np.float32)
+    allv = np.concatenate([s, s_new[..., None]], axis=-1)
+    e = np.exp(allv - allv.max(axis=-1, keepdims=True)).astype(np.float32)
+    p = e[..., :t]
+    ps = (p[..., None] * vs[None]).astype(np.float32)                 # [B, H, T, groups]
+    o = serial(ps[..., None] * vc[None], axis=2)                       # [B, H, groups, g]
+    o = o + serial(p[..., None] * vb[None], axis=2)[..., None]
+    o = o.reshape(q.shape) + e[..., t:] * inputs["new_v"].astype(np.float32)
+    return (o / serial(e, axis=-1)[..., None]).astype(inputs["q"].dtype)
+
+
+def deferred_norm(inputs) -> np.ndarray:
+    """Unnormalised exponentials through the combine, one divide at the end."""
+    q, kd, vd, nk, nv, scale = _operands(inputs)
+    s, s_new = _scores(q, kd, nk, scale)
+    allv = np.concatenate([s, s_new[..., None]], axis=-1)
+    e = np.exp(allv - allv.max(axis=-1, keepdims=True)).astype(np.float32)
+    o = np.einsum("bht,htd->bhd", e[..., :-1], vd).astype(np.float32) + e[..., -1:] * nv
+    return (o / e.sum(axis=-1, dtype=np.float32)[..., None]).astype(inputs["q"].dtype)
+
+
+def _blocked_sum(x: np.ndarray, axis: int, block: int = 16) -> np.ndarray:
+    """Serial fp32 sums inside blocks of `block` along axis, then pairwise."""
+    n = x.shape[axis]
+    x = np.moveaxis(x, axis, -1)
+    pad = (-n) % block
+    if pad:
+        x = np.concatenate([x, np.zeros(x.shape[:-1] + (pad,), dtype=np.float32)], axis=-1)
+    xb = x.reshape(x.shape[:-1] + (-1, block))
+    serial = np.add.accumulate(xb, axis=-1, dtype=np.float32)[..., -1]
+    return np.add.reduce(serial, axis=-1, dtype=np.float32)
+
+
+def blocked16(inputs) -> np.ndarray:
+    q, kd, vd, nk, nv, scale = _operands(inputs)
+    s = (_blocked_sum(q[:, :, None, :] * kd[None], axis=-1) * scale).astype(np.float32)
+    s_new = (_blocked_sum(q * nk, axis=-1) * scale).astype(np.float32)
+    allv = np.concatenate([s, s_new[..., None]], axis=-1)
+    e = np.exp(allv - allv.max(axis=-1, keepdims=True)).astype(np.float32)
+    p = (e / e.sum(axis=-1, dtype=np.float32, keepdims=True)).astype(np.float32)
+    o = _blocked_sum(p[..., :-1, None] * vd[None], axis=2) + p[..., -1:] * nv
+    return o.astype(inputs["q"].dtype)
+
+
+HELD_OUT = {
+    "split-merge-64": lambda x: split_merge(x, 64),
+    "split-merge-256": lambda x: split_merge(x, 256),
+    "online-lazy": online_lazy,
+    "factored": factored,
+    "factored-serial": factored_serial,
+    "deferred-norm": deferred_norm,
+    "blocked-16": blocked16,
+}
+
+# Evaluation classes of the held-out population: what changes the rounding
+# sequence, not merely its order. The membership repair promotes one member of
+# an offending class into the floor and scores the class's other members.
+CLASSES = {
+    "split-merge-64": "split-T merge", "split-merge-256": "split-T merge",
+    "online-lazy": "online softmax",
+    "factored": "integer domain", "factored-serial": "integer domain",
+    "deferred-norm": "reduction order", "blocked-16": "reduction order",
+}
+
+
+# ---------------------------------------------------------------------------
+# per-case measurement
+# ---------------------------------------------------------------------------
+@dataclass(frozen=True)
+class Spec:
+    draw: str
+    dims: tuple
+    dtype: str
+    mode: str
+    seed: int
+    group: int = 64
+
+
+def _inputs(spec: Spec) -> dict:
+    case = battery.Case(spec.dims, spec.dtype, spec.mode, spec.seed)
+    x = battery.case_inputs(case)
+    if spec.group != 64:
+        x["group_size"] = spec.group
+    return x
+
+
+def measure(spec: Spec) -> dict:
+    """Everything the gates read, for one case."""
+    x = _inputs(spec)
+    ref = kv.kv_reference(x)
+    base = kv.base_tol(spec.dtype, ref)
+    members = {name: kv.max_abs_error(kv.kv_member(x, **kw), ref)
+               for name, kw in kv.KV_MEMBERS.items()}
+    held = {name: kv.max_abs_error(fn(x), ref) for name, fn in HELD_OUT.items()}
+    fault_err = {}
+    if spec.draw == "calibration" and spec.mode in battery.IID_MODES:
+        for params in faults.KV_FAULTS:
+            out = faults.faulty(params)(x)
+            fault_err[faults.fault_name(params)] = (
+                kv.max_abs_error(out, ref) if np.all(np.isfinite(out)) else math.inf)
+    return {"draw": spec.draw, "dims": dict(spec.dims), "dtype": spec.dtype, "mode": spec.mode,
+            "seed": spec.seed, "group": spec.group, "base": base, "members": members,
+            "held_out": held, "faults": fault_err}
+
+
+def k_required(base: float, floor_e: float, floor_c: float) -> float:
+    if floor_c <= base:
+        return 0.0
+    return math.inf if floor_e == 0.0 else floor_c / floor_e
+
+
+def draws(limit: int | None = None) -> list:
+    cal = battery.case_space()
+    specs = [Spec("calibration", c.dims, c.dtype, c.distribution, c.seed) for c in cal]
+    specs += [Spec("independent", c.dims, c.dtype, c.distribution, INDEPENDENT_SEED_BASE + i)
+              for i, c in enumerate(cal)]
+    i = 0
+    for dims in battery.all_dims(battery.KV_ATTENTION_META):
+        if dims["BITS"] != 4:
+            continue
+        for bits in EXTENSION_BITS:
+            for group in (64,) + EXTENSION_GROUPS:
+                if dims["DH"] % group:
+                    continue
+                for dtype in battery.KV_ATTENTION_META["dtypes"]:
+                    d = dict(dims, BITS=bits)
+                    specs.append(Spec("extension", tuple(sorted(d.items())), dtype,
+                                      battery.IID_MODES[i % 2], EXTENSION_SEED_BASE + i, group))
+                    i += 1
+    if limit:
+        by = {}
+        for s in specs:
+            by.setdefault(s.draw, []).append(s)
+        specs = [s for v in by.values() for s in v[:limit]]
+    return specs
+
+
+# ---------------------------------------------------------------------------
+# gates
+# ---------------------------------------------------------------------------
+def summarize(rows: list) -> dict:
+    out = {"k_shipped": K_SHIPPED, "cases": {}, "k_required": {}, "worst": {}}
+    for draw in ("calibration", "independent", "extension"):
+        rs = [r for r in rows if r["draw"] == draw]
+        out["cases"][draw] = len(rs)
+        worst, worst_row = 0.0, None
+        for r in rs:
+            fe = max(r["members"].values())
+            name, fc = max(r["held_out"].items(), key=lambda kvp: kvp[1])
+            k = k_required(r["base"], fe, fc)
+            if k > worst:
+                worst, worst_row = k, (r, name, fc, fe)
+        out["k_required"][draw] = worst
+        if worst_row:
+            r, name, fc, fe = worst_row
+            out["worst"][draw] = {"dims": r["dims"], "dtype": r["dtype"], "mode": r["mode"],
+                                  "seed": r["seed"], "group": r["group"], "impl": name,
+                                  "err": fc, "floor": fe, "base": r["base"]}
+    # G1
+    sound = {d: out["k_required"][d] <= K_SHIPPED for d in out["k_required"]}
+    out["G1_sound_at_shipped_K"] = all(sound.values())
+    out["G1_by_draw"] = sound
+    # held-out demand per implementation (max over all draws)
+    per_impl = {}
+    for r in rows:
+        fe = max(r["members"].values())
+        for name, err in r["held_out"].items():
+            per_impl[name] = max(per_impl.get(name, 0.0), k_required(r["base"], fe, err))
+    out["k_required_by_impl"] = per_impl
+    # G2
+    cal = [r for r in rows if r["draw"] == "calibration" and r["faults"]]
+    detect = {}
+    for k in K_GRID:
+        caught = set()
+        for idx, r in enumerate(cal):
+            tol = max(r["base"], k * max(r["members"].values()))
+            for f, err in r["faults"].items():
+                if err > tol:
+                    caught.add((f, idx))
+        detect[k] = caught
+    fault_names = sorted({f for r in cal for f in r["faults"]})
+    equivalent = [f for f in fault_names if not any(f == c[0] for k in K_GRID for c in detect[k])]
+    ref_caught = detect[K_SHIPPED]
+    out["G2"] = {}
+    for k in K_GRID:
+        lost = ref_caught - detect[k]
+        canary_lost = any(f == CANARY for f, _ in lost)
+        out["G2"][str(k)] = {"pairs_caught": len(detect[k]), "pairs_lost_vs_shipped": len(lost),
+                             "keeps_detection": not lost, "canary_absolved": canary_lost}
+    out["equivalent_mutants"] = equivalent
+    min_margin = {}
+    for f in fault_names:
+        ms = []
+        for r in cal:
+            tol = max(r["base"], K_SHIPPED * max(r["members"].values()))
+            if f in r["faults"] and r["faults"][f] > tol:
+                ms.append(r["faults"][f] / tol)
+        min_margin[f] = min(ms) if ms else None
+    out["min_margin_at_shipped_K"] = min_margin
+    # G3 leave-one-member-out (calibration draw)
+    loo = {}
+    for m in kv.KV_MEMBERS:
+        worst = 0.0
+        for r in rows:
+            if r["draw"] != "calibration":
+                continue
+            fe = max(v for n, v in r["members"].items() if n != m)
+            worst = max(worst, k_required(r["base"], fe, max(r["held_out"].values())))
+        loo[m] = worst
+    out["G3_leave_one_member_out"] = loo
+    # membership repair: promote the most demanding member of each offending
+    # class into the floor, score the rest of the population against it
+    offending = sorted({CLASSES.get(n, n) for n, k in per_impl.items() if k > K_SHIPPED})
+    if offending:
+        promoted = [max((n for n in per_impl if CLASSES.get(n, n) == c), key=per_impl.get)
+                    for c in offending]
+        rep = {}
+        for draw in ("calibration", "independent", "extension"):
+            worst = 0.0
+            for r in rows:
+                if r["draw"] != draw:
+                    continue
+                fe = max(list(r["members"].values()) + [r["held_out"][n] for n in promoted])
+                rest = [v for n, v in r["held_out"].items() if n not in promoted]
+                worst = max(worst, k_required(r["base"], fe, max(rest)))
+            rep[draw] = worst
+        same_class = [n for n in per_impl if CLASSES.get(n, n) in offending and n not in promoted]
+        out["repair"] = {"offending_classes": offending, "promoted_to_floor": promoted,
+                         "still_held_out_in_class": same_class, "k_required": rep,
+                         "sound_at_shipped_K": all(v <= K_SHIPPED for v in rep.values())}
+    # decision
+    need = max(out["k_required"].values())
+    sound_grid = [k for k in K_GRID if k >= need]
+    smallest = sound_grid[0] if sound_grid else None
+    out["smallest_sound_grid_K"] = smallest
+    if out["G1_sound_at_shipped_K"]:
+        keeps = smallest is not None and out["G2"][str(smallest)]["keeps_detection"]
+        out["decision"] = (f"K = {K_SHIPPED} stands: sound on every draw (largest demand "
+                           f"{need:.3g}); smallest sound grid K = {smallest}"
+                           + ("" if smallest is None else
+                              f", which {'keeps' if keeps else 'loses'} detection vs "
+                              f"{K_SHIPPED}"))
+    else:
+        rep = out["repair"]
+        worst_rep = max(rep["k_required"].values())
+        out["decision"] = (f"K = {K_SHIPPED} is UNSOUND over the shipped four members: a "
+                           f"held-out correct implementation needs K = {need:.3g}. Membership "
+                           f"repair (promote {', '.join(rep['promoted_to_floor'])} into the "
+                           f"floor): largest demand {worst_rep:.3g}, "
+                           + ("sound at K = %s without moving K" % K_SHIPPED
+                              if rep["sound_at_shipped_K"] else "still unsound; K must move"))
+    return out
+
+
+def run(jobs: int = 1, limit: int | None = None) -> tuple[list, dict]:
+    specs = draws(limit)
+    if jobs > 1:
+        import multiprocessing as mp
+        with mp.get_context("spawn").Pool(jobs) as pool:
+            rows = pool.map(measure, specs, chunksize=4)
+    else:
+        rows = [measure(s) for s in specs]
+    return rows, summarize(rows)
+
+
+def render(summary: dict) -> str:
+    lines = ["# kv_attention K calibration", "",
+             "Produced by `python -m oracle.calibrate_k` (rule in its docstring).", "",
+             f"**Decision:** {summary['decision']}", "",
+             "| draw | cases | largest K required | worst case |", "|---|---|---|---|"]
+    for d in ("calibration", "independent", "extension"):
+        w = summary["worst"].get(d)
+        desc = "" if not w else (f"{w['impl']} on {w['dims']} {w['dtype']} {w['mode']} "
+                                 f"seed {w['seed']} g{w['group']}: err {w['err']:.3g}, "
+                                 f"floor {w['floor']:.3g}, base {w['base']:.3g}")
+        lines.append(f"| {d} | {summary['cases'][d]} | {summary['k_required'][d]:.3g} | {desc} |")
+    lines += ["", "Held-out demand per implementation (max over all draws):", "",
+              "| implementation | K required |", "|---|---|"]
+    for n, k in summary["k_required_by_impl"].items():
+        lines.append(f"| {n} | {k:.3g} |")
+    lines += ["", "Detection by K (calibration draw, iid modes):", "",
+              "| K | (fault, case) pairs caught | lost vs shipped | canary absolved |",
+              "|---|---|---|---|"]
+    for k, g in summary["G2"].items():
+        lines.append(f"| {k} | {g['pairs_caught']} | {g['pairs_lost_vs_shipped']} | "
+                     f"{g['canary_absolved']} |")
+    lines += ["", "Smallest margin (err / tol) of each fault at the shipped K:", ""]
+    for f, m in summary["min_margin_at_shipped_K"].items():
+        lines.append(f"- `{f}`: " + ("never caught (equivalent at these widths)" if m is None
+                                     else f"{m:.3g}"))
+    if "repair" in summary:
+        rep = summary["repair"]
+        lines += ["", "Membership repair:", "",
+                  f"- offending classes: {', '.join(rep['offending_classes'])}",
+                  f"- promoted into the floor: {', '.join(rep['promoted_to_floor'])}",
+                  f"- same-class members still held out: "
+                  f"{', '.join(rep['still_held_out_in_class']) or 'none'}",
+                  "- largest K required after the repair: " + ", ".join(
+                      f"{d} {k:.3g}" for d, k in rep["k_required"].items()),
+                  f"- sound at the shipped K: {rep['sound_at_shipped_K']}"]
+    lines += ["", "Leave-one-member-out largest K required (calibration draw):", ""]
+    for m, k in summary["G3_leave_one_member_out"].items():
+        lines.append(f"- `{m}`: {k:.3g}")
+    return "\n".join(lines) + "\n"
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--jobs", type=int, default=1)
+    ap.add_argument("--limit", type=int, default=None, help="first N cases of each draw")
+    ap.add_argument("--out", default=None, help="write the JSON summary here")
+    ap.add_argument("--md", default=None, help="write the markdown report here")
+    args = ap.parse_args(argv)
+    _, summary = run(args.jobs, args.limit)
+    if args.out:
+        with open(args.out, "w") as f:
+            json.dump(summary, f, indent=1, default=str)
+    if args.md:
+        with open(args.md, "w") as f:
+            f.write(render(summary))
+    print(summary["decision"])
+    return 0 if summary["G1_sound_at_shipped_K"] else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

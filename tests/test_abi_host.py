@@ -31,6 +31,51 @@ def test_header_and_binding_agree():
     assert declared_functions() == set(_native.EXPORTS)
 
 
+def _prototypes() -> dict:
+    """name -> (return type, [parameter types]) of every prototype in the
+    header, comments stripped."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    protos = {}
+    for ret, name, params in re.findall(r"((?:const\s+)?\w+\s*\**)\s*(kvq_\w+)\s*\(([^)]*)\)\s*;",
+                                        text):
+        params = " ".join(params.split())
+        plist = [] if params in ("", "void") else [p.strip() for p in params.split(",")]
+        protos[name] = (" ".join(ret.split()), plist)
+    return protos
+
+
+def _ctype_of(decl: str):
+    """The ctypes type a C parameter or return declaration binds to."""
+    decl = " ".join(decl.replace("*", " * ").split())
+    if decl.count("*") == 2:
+        return ctypes.POINTER(ctypes.c_void_p)
+    if decl == "uint32_t * status" or decl.endswith("uint32_t * status"):
+        return ctypes.POINTER(ctypes.c_uint32)
+    if decl.startswith("const char *"):
+        return ctypes.c_char_p
+    if "kvq_args" in decl:
+        return ctypes.POINTER(_native.KvqArgs)
+    if "*" in decl:
+        return ctypes.c_void_p
+    base = decl.replace("const ", "").split()[0]
+    return {"int": ctypes.c_int, "uint32_t": ctypes.c_uint32, "uint64_t": ctypes.c_uint64,
+            "size_t": ctypes.c_size_t}[base]
+
+
+def test_binding_signatures_match_the_header_prototypes(lib):
+    """Every ctypes declaration has the header prototype's arity and types, so
+    a binding can never pass an argument the C side reads as something else."""
+    for name, (ret, params) in _prototypes().items():
+        fn = getattr(lib, name)
+        assert fn.restype == _ctype_of(ret), (name, ret, fn.restype)
+        want = [_ctype_of(p) for p in params]
+        assert len(fn.argtypes) == len(want), (name, len(fn.argtypes), len(want))
+        for i, (got, exp) in enumerate(zip(fn.argtypes, want)):
+            if "*" in params[i] and got is ctypes.c_void_p:
+                continue          # any pointer may travel as a plain address
+            assert got == exp, (name, i, params[i], got, exp)
+
+
 def test_library_exports_every_declared_symbol(lib):
     handle = ctypes.CDLL(str(_native.LIB_PATH))
     for name in declared_functions():
@@ -99,3 +144,26 @@ def test_missing_device_is_unsupported_not_a_crash(lib):
     status = lib.kvq_decode(ctypes.byref(a), 8192, 1 << 20, need, None)
     assert status == _native.KVQ_ERR_UNSUPPORTED
     assert lib.kvq_last_error()
+
+
+@pytest.mark.parametrize("over,needle", [
+    (dict(position=6), b"runs past t_stride"),
+    (dict(b_rows=2, batch_stride=0), b"one cache per sequence"),
+    (dict(b_rows=2, batch_stride=8), b"overlaps"),
+    (dict(bits=5), b"bits"),
+    (dict(w=0), b"NULL"),
+])
+def test_cache_append_rejects_bad_destinations(lib, over, needle):
+    """Host checks of kvq_cache_append, before any device work: a host
+    position past the buffer, a shared cache under several sequences, a batch
+    stride that overlaps, a bad width, a NULL pointer."""
+    a = dict(w=4096, b_rows=1, n_kv_heads=2, n_new=3, head_dim=64, bits=4, group=64, dtype=0,
+             positions=None, position=0, t_stride=8, batch_stride=16, wq=8192, scales=8192,
+             biases=8192)
+    a.update(over)
+    status = lib.kvq_cache_append(a["w"], a["b_rows"], a["n_kv_heads"], a["n_new"],
+                                  a["head_dim"], a["bits"], a["group"], a["dtype"],
+                                  a["positions"], a["position"], a["t_stride"],
+                                  a["batch_stride"], a["wq"], a["scales"], a["biases"], None)
+    assert status == _native.KVQ_ERR_INVALID
+    assert needle in lib.kvq_last_error()
