@@ -77,7 +77,11 @@ typedef struct kvq_args {
     uint32_t n_heads;         /* query heads                                   */
     uint32_t n_kv_heads;      /* cache heads; n_heads % n_kv_heads == 0         */
     uint32_t t_cached;        /* logical cached positions (when seq_lens NULL)  */
-    uint32_t t_stride;        /* physical rows per cache head (>= every length) */
+    uint32_t t_stride;        /* physical rows per cache head (>= every length);
+                                 the tensor-core kernels need it, the batch
+                                 stride and t_begin to be multiples of 8 and
+                                 every buffer 16-byte aligned, else the
+                                 CUDA-core kernel serves the call            */
     uint32_t head_dim;        /* 64 or 128                                     */
     uint32_t bits;            /* 2, 3, 4, 6 or 8                               */
     uint32_t group_size;      /* 32, 64 or 128; divides head_dim               */
@@ -114,6 +118,18 @@ int kvq_decode(const kvq_args* a, void* out, void* workspace, size_t workspace_b
  */
 int kvq_decode_partial(const kvq_args* a, float* part_o, float* part_m, float* part_l,
                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Which kernel kvq_decode would run for these arguments (host only, no device
+ * work): one of the KVQ_KERNEL_* values, or a negative status when the
+ * arguments are invalid. A serving loop checks it once per cache geometry:
+ * a call that silently left the tensor-core kernels (an unaligned t_stride,
+ * a format they do not carry) still computes the same step, only slower.
+ */
+#define KVQ_KERNEL_CUDA_CORE 0
+#define KVQ_KERNEL_TENSOR_CORE 1   /* register-fragment mma.sync kernels */
+#define KVQ_KERNEL_TCGEN05 2       /* the tcgen05 kernel (KVQ_KERNEL=umma)  */
+int kvq_plan_kernel(const kvq_args* a);
 
 /* Number of T splits kvq_decode_splits produces for these arguments (0 when
  * the arguments are invalid). */

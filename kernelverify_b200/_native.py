@@ -18,13 +18,14 @@ KVQ_OK, KVQ_ERR_INVALID, KVQ_ERR_LAUNCH, KVQ_ERR_UNSUPPORTED = 0, -1, -2, -3
 KVQ_F16, KVQ_F32 = 0, 1
 KVQ_T_END_ALL = 0xFFFFFFFF
 KVQ_NOALLOC_SCRATCH_BYTES = 16 << 20
+KVQ_KERNEL_CUDA_CORE, KVQ_KERNEL_TENSOR_CORE, KVQ_KERNEL_TCGEN05 = 0, 1, 2
 KVQ_PEER_MAX_RANKS = 8
 KVQ_PEER_HANDLE_BYTES = 64
 
 # Every symbol include/kvq_b200.h declares.
 EXPORTS = ("kvq_workspace_bytes", "kvq_decode", "kvq_decode_partial", "kvq_split_count",
            "kvq_decode_splits", "kvq_lse_merge", "kvq_lse_merge_records", "kvq_decode_noalloc",
-           "kvq_dequant", "kvq_quantize", "kvq_cache_append", "kvq_supports", "kvq_last_error", "kvq_abi_version",
+           "kvq_dequant", "kvq_quantize", "kvq_cache_append", "kvq_supports", "kvq_plan_kernel", "kvq_last_error", "kvq_abi_version",
            "kvq_peer_region_bytes", "kvq_peer_record_offset", "kvq_peer_alloc", "kvq_peer_open",
            "kvq_peer_close", "kvq_peer_free", "kvq_peer_merge", "kvq_peer_status",
            "kvq_peer_last_error")
@@ -70,6 +71,7 @@ def _declare(lib) -> None:
         "kvq_decode": (I, [AP, P, P, SZ, P]),
         "kvq_decode_partial": (I, [AP, P, P, P, P, SZ, P]),
         "kvq_split_count": (U32, [AP]),
+        "kvq_plan_kernel": (I, [AP]),
         "kvq_decode_splits": (I, [AP, P, P, P, P]),
         "kvq_lse_merge": (I, [P, P, P, U32, U32, U32, U32, P, P]),
         "kvq_lse_merge_records": (I, [P, U32, U32, U32, U32, P, P]),

@@ -435,6 +435,18 @@ uint32_t kvq_split_count(const kvq_args* a) {
     return n;
 }
 
+int kvq_plan_kernel(const kvq_args* a) {
+    g_error.clear();
+    Plan pl;
+    const int rc = plan(a, &pl);
+    if (rc) return rc;
+    switch (pl.kernel) {
+        case KERNEL_MMA4: return KVQ_KERNEL_TENSOR_CORE;
+        case KERNEL_UMMA4: return KVQ_KERNEL_TCGEN05;
+        default: return KVQ_KERNEL_CUDA_CORE;
+    }
+}
+
 int kvq_decode_splits(const kvq_args* a, float* part_o, float* part_m, float* part_l, void* stream) {
     g_error.clear();
     Plan pl;

@@ -161,6 +161,20 @@ def _args(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *
     return a
 
 
+KERNEL_NAMES = {0: "cuda-core", 1: "tensor-core", 2: "tcgen05"}
+
+
+def plan_kernel(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *, bits,
+                t_cached=None, seq_lens=None) -> str:
+    """Which kernel `decode` would run on these arguments ("tensor-core",
+    "tcgen05" or "cuda-core"); host only, nothing is launched."""
+    a = _args(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, bits=bits,
+              t_cached=t_cached, seq_lens=seq_lens)
+    kind = _native.lib().kvq_plan_kernel(a)
+    _native.check(min(kind, 0))
+    return KERNEL_NAMES[kind]
+
+
 class Workspace:
     """A reusable, growing scratch buffer on one device (the library never
     allocates; this is the caller-side allocation it asks for)."""

@@ -41,6 +41,9 @@ from dataclasses import dataclass, field
 from kernelverify_b200.pack import kv_attention as kva
 
 
+ROW_ALIGN = 64
+
+
 def _torch():
     import torch
     return torch
@@ -49,9 +52,9 @@ def _torch():
 class QuantizedKVCache:
     """One layer's packed K/V cache for a batch of sequences.
 
-    keys / values: (words int32 [B, HKV, capacity, DH*bits/32], scales
-    [B, HKV, capacity, DH/group], biases) -- the padded buffers the fused
-    kernel reads whole. `offset` is the logical length (positions written),
+    keys / values: (words int32 [B, HKV, t_stride, DH*bits/32], scales
+    [B, HKV, t_stride, DH/group], biases) -- the padded buffers the fused
+    kernel reads whole; t_stride is `capacity` rounded up to 64 rows. `offset` is the logical length (positions written),
     uniform over the batch; `positions` is its device copy (int32 [B]) for a
     captured step. `new_keys` / `new_values` hold the last update's
     full-precision entry ([B, HKV, L, DH])."""
@@ -73,7 +76,10 @@ class QuantizedKVCache:
                                                                       capacity)
         words = head_dim * bits // 32
         groups = head_dim // group_size
-        lead = (batch, n_kv_heads, capacity)
+        # physical rows per head: a multiple of 64, so the tensor-core kernels
+        # (8-row-aligned geometry) serve every length up to `capacity`
+        self.t_stride = -(-capacity // ROW_ALIGN) * ROW_ALIGN
+        lead = (batch, n_kv_heads, self.t_stride)
 
         def triplet():
             return (torch.zeros(lead + (words,), dtype=torch.int32, device=device),
@@ -114,6 +120,17 @@ class QuantizedKVCache:
         self.positions.fill_(self.offset)
         return self.keys, self.values
 
+    def append_at(self, keys, values, positions):
+        """Quantize keys / values [B, HKV, 1, DH] into each sequence's row
+        positions[b] (an int32 [B] device tensor) and stash them; the host
+        `offset` is left alone (a captured step advances `positions` on the
+        device)."""
+        keys = keys.to(self.dtype).contiguous()
+        values = values.to(self.dtype).contiguous()
+        kva.cache_append(keys, *self.keys, self.bits, positions=positions)
+        kva.cache_append(values, *self.values, self.bits, positions=positions)
+        self.new_keys, self.new_values = keys, values
+
     def dequantized(self, length: int | None = None):
         """(K, V) in the cache dtype, [B, HKV, length, DH]: positions
         [0, length) read back through the library's dequantizer."""
@@ -137,6 +154,15 @@ class FullPrecisionKVCache:
         self.k = torch.zeros(shape, dtype=dtype, device=device)
         self.v = torch.zeros(shape, dtype=dtype, device=device)
         self.capacity, self.offset, self.dtype = capacity, 0, dtype
+
+    def append_at(self, keys, values, positions):
+        """Write keys / values [B, HKV, 1, DH] at each sequence's row
+        positions[b] (int32 [B] device tensor); no host bookkeeping."""
+        torch = _torch()
+        rows = torch.arange(keys.shape[0], device=keys.device)
+        idx = positions.long()
+        self.k[rows, :, idx] = keys[:, :, 0]
+        self.v[rows, :, idx] = values[:, :, 0]
 
     def update_and_fetch(self, keys, values):
         n = keys.shape[2]
@@ -173,9 +199,13 @@ def stock_attention(queries, cache, scale: float, mask=None):
     else:
         k, v = cache.k[:, :, :cache.offset], cache.v[:, :, :cache.offset]
     n_q, n_kv = queries.shape[2], k.shape[2]
-    attn_mask = _causal_mask(n_q, n_kv, queries.device) if mask == "causal" else None
-    if mask is not None and mask != "causal":
-        attn_mask = mask
+    causal = isinstance(mask, str) and mask == "causal"
+    if causal and n_q == n_kv and n_q > 1:
+        # a first chunk: top-left and bottom-right alignment agree, and the
+        # flag keeps torch on its fused causal kernels (no [L, L] mask)
+        return F.scaled_dot_product_attention(queries, k, v, is_causal=True, scale=scale,
+                                              enable_gqa=k.shape[1] != queries.shape[1])
+    attn_mask = _causal_mask(n_q, n_kv, queries.device) if causal else mask
     return F.scaled_dot_product_attention(queries, k, v, attn_mask=attn_mask, scale=scale,
                                           enable_gqa=k.shape[1] != queries.shape[1])
 
@@ -205,6 +235,7 @@ def contract_reference(queries, cache):
 class RouterStats:
     calls: int = 0
     fallback: dict = field(default_factory=dict)
+    kernels: dict = field(default_factory=dict)   # fused calls by the kernel that served them
     shadow_fused_ref: float = 0.0
     shadow_stock_ref: float = 0.0
     shadow_ref_mag: float = 0.0
@@ -272,6 +303,12 @@ class DecodeRouter:
         q = queries.reshape(b, h, d).contiguous()
         nk = cache.new_keys.reshape(b, cache.n_kv_heads, d)
         nv = cache.new_values.reshape(b, cache.n_kv_heads, d)
+        # the kernel depends on the cache's geometry and format only: plan once
+        kernel = getattr(cache, "planned_kernel", None)
+        if kernel is None:
+            kernel = cache.planned_kernel = kva.plan_kernel(
+                q, *cache.keys, *cache.values, nk, nv, bits=cache.bits, t_cached=cache.offset - 1)
+        self.stats.kernels[kernel] = self.stats.kernels.get(kernel, 0) + 1
         out = kva.decode(q, *cache.keys, *cache.values, nk, nv, bits=cache.bits,
                          t_cached=cache.offset - 1, workspace=self.workspace)
         return out.reshape(b, h, 1, d)

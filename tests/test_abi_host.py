@@ -167,3 +167,13 @@ def test_cache_append_rejects_bad_destinations(lib, over, needle):
                                   a["batch_stride"], a["wq"], a["scales"], a["biases"], None)
     assert status == _native.KVQ_ERR_INVALID
     assert needle in lib.kvq_last_error()
+
+
+def test_plan_kernel_names_the_kernel_without_a_device(lib):
+    """Aligned fp16 4-bit DH-128 geometry plans the tensor-core kernels; a
+    t_stride that is not a multiple of 8 or an 8-bit cache the CUDA-core one;
+    invalid arguments a negative status."""
+    assert lib.kvq_plan_kernel(ctypes.byref(_args())) == _native.KVQ_KERNEL_TENSOR_CORE
+    assert lib.kvq_plan_kernel(ctypes.byref(_args(t_stride=130))) == _native.KVQ_KERNEL_CUDA_CORE
+    assert lib.kvq_plan_kernel(ctypes.byref(_args(bits=8))) == _native.KVQ_KERNEL_CUDA_CORE
+    assert lib.kvq_plan_kernel(ctypes.byref(_args(bits=5))) == _native.KVQ_ERR_INVALID

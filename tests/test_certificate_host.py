@@ -46,3 +46,24 @@ def test_the_translation_unit_hash_covers_the_sources():
     h = C.translation_unit_sha256()
     assert len(h) == 64 and h == C.translation_unit_sha256()
     assert any(f.startswith("-gencode") or "sm_100a" in f for f in C.build_flags())
+
+
+def test_committed_certificates_are_complete_and_honest():
+    """Every specialization (bits 2/3/4/6/8 x head_dim 64/128, fp16) has a
+    committed certificate that passed every case, attests C1/C4/C5 at the
+    contract precision, carries both byte-bound hashes and binds to a chip."""
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1] / "certificates"
+    names = {f"kv_attn_decode-BITS{b}-DH{d}-float16" for b in (2, 3, 4, 6, 8) for d in (64, 128)}
+    found = {p.name[:-len(".certificate.json")] for p in root.glob("*.certificate.json")}
+    assert found == names
+    for name in names:
+        doc = json.loads((root / f"{name}.certificate.json").read_text())
+        assert doc["kernel"] == name
+        pb, bb = doc["protocol_bound"], doc["byte_bound"]
+        assert pb["all_passed"] and pb["cases_passed"] == pb["cases_run"] > 0
+        assert bb["precision"] == "contract"
+        assert len(bb["translation_unit_sha256"]) == 64 and len(bb["library_sha256"]) == 64
+        assert {c["clause"] for c in doc["attestation"]["clauses"]} >= {"C1", "C4", "C5"}
+        assert "B200" in doc["validity"]["binding_on"]["chip_generation"]
+        assert (root / f"{name}.md").exists()

@@ -165,3 +165,64 @@ def test_decode_loop_arms_agree_on_first_token(torch_cuda):
     ta, _ = dl.generate(model, prompt, 4, 4, DecodeRouter(fused=True))
     tb, _ = dl.generate(model, prompt, 4, 4, DecodeRouter(fused=False))
     assert bool((ta[:, 0] == tb[:, 0]).all())
+
+
+@pytest.mark.parametrize("arm", ["fused", "stock", "fp16"])
+def test_captured_step_replays_the_eager_step(torch_cuda, arm):
+    """The captured decode step (device positions, device-side append, the
+    fused kernel with seq_lens) replays exactly what the same step computes
+    eagerly, token for token, and advances the device positions."""
+    torch = torch_cuda
+    from kernelverify_b200 import decode_loop as dl
+    model = dl.Decoder(dl.TINY, seed=4)
+    d = dl.CapturedDecode(model, batch=3, capacity=56, arm=arm, bits=4)
+    d.prefill_synthetic(40, seed=1)
+    d.tok.fill_(7)
+    d.capture()
+    replayed = []
+    for _ in range(4):
+        d.graph.replay()
+        replayed.append(d.tok.clone())
+    assert d.pos.tolist() == [44, 44, 44]
+    d.rewind(40)
+    d.tok.fill_(7)
+    eager = []
+    with torch.inference_mode():
+        for _ in range(4):
+            d._step()
+            eager.append(d.tok.clone())
+    torch.cuda.synchronize()
+    for a, b in zip(replayed, eager):
+        assert torch.equal(a, b)
+
+
+def test_captured_ab_reports_every_arm(torch_cuda):
+    from kernelverify_b200 import decode_loop as dl
+    model = dl.Decoder(dl.TINY)
+    row = dl.ab_graph(model, batch=2, prompt=64, steps=8, bits=4, rounds=2)
+    for arm in dl.CapturedDecode.ARMS:
+        assert row[f"{arm}_tps"] > 0
+    assert "ratio_AB" in row and "demotion_C_beats_A" in row
+
+
+def test_serving_caches_keep_the_tensor_core_kernels(torch_cuda):
+    """Any capacity: the cache pads its rows so 4-bit DH-128 fp16 steps plan
+    the tensor-core kernels, in the router and in the captured step."""
+    torch = torch_cuda
+    from kernelverify_b200 import decode_loop as dl
+    from kernelverify_b200.serving import DecodeRouter, QuantizedKVCache
+    cache = QuantizedKVCache(2, 2, 128, 1001, 4, 64, torch.float16, "cuda")
+    assert cache.t_stride % 64 == 0 and cache.t_stride >= 1001
+    k = torch.randn(2, 2, 37, 128, device="cuda", dtype=torch.float16)
+    cache.update_and_fetch(k, k)
+    cache.update_and_fetch(k[:, :, :1].contiguous(), k[:, :, :1].contiguous())
+    router = DecodeRouter()
+    router(torch.randn(2, 8, 1, 128, device="cuda", dtype=torch.float16), cache=cache,
+           scale=128 ** -0.5)
+    assert router.stats.kernels == {"tensor-core": 1}
+    shape = dl.DecoderShape(n_layers=1, hidden=512, n_heads=4, n_kv_heads=2, head_dim=128,
+                            intermediate=512, vocab=256)
+    d = dl.CapturedDecode(dl.Decoder(shape), batch=2, capacity=8258, arm="fused", bits=4)
+    d.prefill_synthetic(100)
+    d.capture()
+    assert d.fused_kernel == "tensor-core"
