@@ -208,7 +208,8 @@ int plan(const kvq_args* a, Plan* pl) {
             // final reduction) is worth about two tiles
             mma4_splits(span, units, kvq::umma4_ctas_per_sm(pl->ht), &P.chunk, &P.n_splits, 128, 256);
         else
-            mma4_splits(span, units, kvq::mma4_ctas_per_sm(pl->ht, a->group_size), &P.chunk, &P.n_splits);
+            mma4_splits(span, units, kvq::mma4_ctas_per_sm(pl->ht, a->group_size), &P.chunk,
+                        &P.n_splits, (uint64_t)kvq::mma4_stage_positions(), kMmaRamp);
         pl->part_bytes = align_up((size_t)P.n_splits * pl->rows * a->head_dim * sizeof(float));
         pl->ml_bytes = align_up((size_t)P.n_splits * pl->rows * sizeof(float));
         return KVQ_OK;

@@ -54,5 +54,8 @@ int umma4_ctas_per_sm(int ht);
 // device cannot be queried).
 int mma4_ctas_per_sm(int ht, int group);
 int sm_count();
+// Positions per stage of the register-fragment kernels (split chunks are
+// multiples of it).
+int mma4_stage_positions();
 
 }  // namespace kvq

@@ -3,9 +3,9 @@
 // Data path: one producer warp streams each stage of TP positions -- packed K
 // and V codes, K/V scales and biases, six contiguous runs of the cache --
 // into a STAGES-deep shared-memory ring with cp.async.bulk (TMA, 1-D) and
-// mbarrier transaction counts. CWARPS consumer warps take whole stages round
-// robin; each keeps its own online-softmax state, and the warps' partials
-// are merged once at the end of the CTA.
+// mbarrier transaction counts. Each of the CWARPS consumer warps takes its
+// own 16-position block of every stage; each keeps its own online-softmax
+// state, and the warps' partials are merged once at the end of the CTA.
 //
 // Arithmetic (all intermediates fp32 or exact):
 //   scores  s[h,t] = scale * sum_g ( k_scale[t,g] * X_g[h,t] + k_bias[t,g] * Qsum_g[h] )
@@ -35,9 +35,12 @@
 namespace kvq {
 namespace mma4 {
 
-constexpr int CWARPS = 4;                    // consumer warps
+#ifndef KVQ_MMA_CWARPS
+#define KVQ_MMA_CWARPS 4                     // consumer warps
+#endif
+constexpr int CWARPS = KVQ_MMA_CWARPS;
 constexpr int THREADS = 32 * (CWARPS + 1);   // + one producer warp
-constexpr int TP = 64;                       // positions per stage
+constexpr int TP = 16 * CWARPS;              // positions per stage: 16 per consumer warp
 #ifndef KVQ_MMA_STAGES
 #define KVQ_MMA_STAGES 6                     // depth of the shared-memory stage ring
 #endif

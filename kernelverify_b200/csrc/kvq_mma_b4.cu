@@ -80,6 +80,8 @@ int mma4_ctas_per_sm(int ht, int group) {
     return n;
 }
 
+int mma4_stage_positions() { return mma4::TP; }
+
 int sm_count() {
     static std::atomic<int> cached[kMaxDevices] = {};
     int dev = 0;
