@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark: quantized-KV decode attention on B200 (the pack_kv_attention path).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|5] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5] [--impl ours|reference]
 
 Default workload (the Llama-3-8B decode shape): per GPU a
 batch of 32 sequences, 32 query / 8 KV heads, head_dim 128, T = 8192 cached
@@ -16,6 +16,13 @@ on the data path).
 4-bit g64): T is sharded into N equal contiguous ranges, each rank computes
 its shard's partial (O, m, l), the partials are all-gathered over NCCL and
 merged by log-sum-exp on every rank (strong scaling).
+
+--config 3: the bits x group sweep (B=16, 32/8 heads, T=16384, N(0,1) sources
+with 1% of entries x20); one JSON line per (bits, group) variant, or only the
+one --bits/--group name. --config 4: the ragged batch (B=64, 28/4 heads,
+8-bit g64, per-sequence lengths seeded U[256, 32768], one cache per
+sequence, `seq_lens` on the device). Both are the full step through
+kvq_decode, timed like config 2, weak scaling on N ranks.
 
 Timing: W untimed eager warm-up steps, then each cache set's step is captured
 as a CUDA graph (config 5 on N > 1 ranks: the local partial only, the NCCL
@@ -54,7 +61,18 @@ FALLBACK_HBM_GBS = 6650.0
 METRIC = "qKV decode attention: µs/step, HBM GB/s & % of roofline at 1/2/4/8 B200"
 
 CONFIG2 = dict(B=32, H=32, HKV=8, DH=128, T=8192, bits=4, group=64)
+CONFIG3 = dict(B=16, H=32, HKV=8, DH=128, T=16384, bits=4, group=64, outliers=0.01)
+CONFIG4 = dict(B=64, H=28, HKV=4, DH=128, T=32768, bits=8, group=64, lens=(256, 32768, 0))
 CONFIG5 = dict(B=1, H=64, HKV=8, DH=128, T=131072, bits=4, group=64)
+SWEEP_BITS = (2, 3, 4, 6, 8)
+SWEEP_GROUPS = (32, 64, 128)
+
+
+def ragged_lengths(b: int, lo: int, hi: int, seed: int):
+    """Config 4's per-sequence lengths, inclusive U[lo, hi] from a seeded
+    numpy generator (seed 0: sum 1,077,211, min 345, max 32678)."""
+    import numpy as np
+    return np.random.default_rng(seed).integers(lo, hi, b, endpoint=True)
 
 
 def parse_args(argv=None):
@@ -62,7 +80,9 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--config", type=int, default=2, choices=(2, 5))
+    ap.add_argument("--config", type=int, default=2, choices=(2, 3, 4, 5))
+    ap.add_argument("--bits", type=int, default=None, help="config 3: one width of the sweep")
+    ap.add_argument("--group", type=int, default=None, help="config 3: one group of the sweep")
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch size (small cases for ncu captures)")
@@ -211,13 +231,19 @@ def barrier(dist):
 # ---------------------------------------------------------------------------
 # workload on the device
 # ---------------------------------------------------------------------------
-def device_caches(kva, shape, bits, group, seed, device):
-    """Packed (words, scales, biases) for an N(0,1) fp16 cache of `shape`,
-    quantized on the device by the library's canonical quantizer."""
+def device_caches(kva, shape, bits, group, seed, device, outliers: float = 0.0):
+    """Packed (words, scales, biases) for an N(0,1) fp16 cache of `shape`
+    (a fraction `outliers` of its entries scaled x20), quantized on the device
+    by the library's canonical quantizer."""
     import torch
     g = torch.Generator(device=device)
     g.manual_seed(seed)
-    raw = torch.randn(shape, dtype=torch.float32, device=device, generator=g).half()
+    raw = torch.randn(shape, dtype=torch.float32, device=device, generator=g)
+    if outliers:
+        hit = torch.rand(shape, device=device, generator=g) < outliers
+        raw = torch.where(hit, raw * 20.0, raw)
+        del hit
+    raw = raw.half()
     words, scales, biases = kva.quantize(raw, bits, group)
     del raw
     return words, scales, biases
@@ -476,6 +502,164 @@ def run_ours(args) -> dict | None:
 
 
 # ---------------------------------------------------------------------------
+# configs 3 and 4: variants of the full step on one GPU per rank
+# ---------------------------------------------------------------------------
+def measure_variant(args, cfg, device, dist, workload: str) -> dict:
+    """The full step (kvq_decode: split stage + merge) of one variant, timed as
+    config 2 is, and its split stage alone for the roofline."""
+    import numpy as np
+    import torch
+
+    from kernelverify_b200 import _native
+    from kernelverify_b200.pack import kv_attention as kva
+
+    lib = _native.lib()
+    rank, world, local = dist_env()
+    b, h, hkv, dh = cfg["B"], cfg["H"], cfg["HKV"], cfg["DH"]
+    lens = None
+    if "lens" in cfg:
+        lo, hi, seed = cfg["lens"]
+        lens = ragged_lengths(b, lo, hi, seed)
+        t_rows = -(-int(lens.max()) // 64) * 64
+        t_sum = int(lens.sum())
+    else:
+        t_rows, t_sum = cfg["T"], b * cfg["T"]
+    local_kv = kv_bytes(cfg, t_sum)
+    per_set = kv_bytes(cfg, b * t_rows)            # what a cache set occupies
+    n_sets = max(2, math.ceil(2 * L2_BYTES / local_kv) + 1)
+    g = torch.Generator(device=device)
+    g.manual_seed(7 + rank)
+    q = torch.randn((b, h, dh), generator=g, device=device).half()
+    nk = torch.randn((b, hkv, dh), generator=g, device=device).half()
+    nv = torch.randn((b, hkv, dh), generator=g, device=device).half()
+    sl = torch.from_numpy(lens.astype(np.int32)).to(device) if lens is not None else None
+    sets = []
+    for i in range(n_sets):
+        arts = [device_caches(kva, (b, hkv, t_rows, dh), cfg["bits"], cfg["group"],
+                              1000 * (rank + 1) + 2 * i + kv, device, cfg.get("outliers", 0.0))
+                for kv in (0, 1)]
+        sets.append((*arts[0], *arts[1]))
+    out = torch.empty_like(q)
+    margs = [kva._args(q, *st[:3], *st[3:], nk, nv, bits=cfg["bits"], t_cached=t_rows,
+                       seq_lens=sl) for st in sets]
+    kernel = kva.KERNEL_NAMES[lib.kvq_plan_kernel(margs[0])]
+    rows = b * h
+    n_splits = lib.kvq_split_count(margs[0])
+    po = torch.empty((n_splits, rows, dh), dtype=torch.float32, device=device)
+    pm = torch.empty((n_splits, rows), dtype=torch.float32, device=device)
+    pl = torch.empty((n_splits, rows), dtype=torch.float32, device=device)
+    ws_need = lib.kvq_workspace_bytes(margs[0])
+    ws = torch.empty(ws_need + 256, dtype=torch.uint8, device=device)
+    ws_base = (ws.data_ptr() + 255) // 256 * 256
+    stream = torch.cuda.current_stream(device)
+
+    def step(i):
+        _native.check(lib.kvq_decode(margs[i % n_sets], out.data_ptr(), ws_base, ws_need,
+                                     stream.cuda_stream))
+
+    def splits(i):
+        _native.check(lib.kvq_decode_splits(margs[i % n_sets], po.data_ptr(), pm.data_ptr(),
+                                            pl.data_ptr(), stream.cuda_stream))
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    for i in range(args.warmup):
+        step(i)
+    barrier(dist)
+    graphs = []
+    for i in range(n_sets):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            step(i)
+        graphs.append(gr)
+    for gr in graphs:
+        gr.replay()
+    barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    e0.record(stream)
+    for i in range(args.steps):
+        graphs[i % n_sets].replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall1 = time.time()
+    barrier(dist)
+    for i in range(3):
+        splits(i)
+    barrier(dist)
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record(stream)
+    for i in range(args.steps):
+        splits(i)
+    k1.record(stream)
+    torch.cuda.synchronize()
+    barrier(dist)
+    clocks = sampler.stop(wall0, wall1)
+    step_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, dist)
+    kern_ms = max_over_ranks(k0.elapsed_time(k1) / args.steps, dist)
+    del graphs, sets
+    peak, peak_kind = measured_hbm()
+    alg_kernel = local_kv + io_bytes(cfg)
+    achieved = alg_kernel / (kern_ms * 1e-3) / 1e9
+    value = world * local_kv / (step_ms * 1e-3) / 1e9
+    key = (f"partial_kernel_config3_b{cfg['bits']}_g{cfg['group']}_n1" if "lens" not in cfg
+           else "partial_kernel_config4_n1")
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5),
+        "us_per_step": round(step_ms * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": f"u{cfg['bits']} codes, fp16 scales/q/out, fp32 accumulate",
+        "data": ("synthetic: N(0,1) fp32" + (f" with {cfg['outliers']:.0%} of entries x20"
+                                             if cfg.get("outliers") else "")
+                 + " -> fp16 -> canonical MLX-affine quantizer on device, seeded"),
+        "config": {"workload": workload, "B": b, "n_heads": h, "n_kv_heads": hkv,
+                   "head_dim": dh, "t_cached": (f"ragged U[{cfg['lens'][0]}, {cfg['lens'][1]}] "
+                                                f"seed {cfg['lens'][2]}, sum {t_sum}"
+                                                if lens is not None else cfg["T"]),
+                   "bits": cfg["bits"], "group": cfg["group"], "n_splits": n_splits,
+                   "kernel": kernel,
+                   "l2": f"inputs larger than L2: {n_sets} cache sets of {per_set / 1e6:.1f} MB rotated",
+                   "kv_bytes_per_step": local_kv, "parallelism": f"dp{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4),
+                     "peak_kind": (f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
+                                   if peak_kind == "measured" else "fallback 6.65 TB/s"),
+                     "kernel": f"{kernel} partial kernel (kvq_decode_splits), timed alone",
+                     "kernel_us": round(kern_ms * 1e3, 2), "alg_bytes_per_launch": alg_kernel,
+                     "traffic": profiled_traffic(key)},
+        "clocks": clocks,
+        "e2e": None,
+        "gpu_launches": 2 * args.steps,
+    }
+
+
+def run_variants(args) -> list:
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = dist_init(world, local)
+    lines = []
+    if args.config == 4:
+        cfg = dict(CONFIG4)
+        if args.batch:
+            cfg["B"] = args.batch
+        lines.append(measure_variant(args, cfg, device, dist, "config4-ragged-8bit"))
+    else:
+        for bits in ([args.bits] if args.bits else SWEEP_BITS):
+            for group in ([args.group] if args.group else SWEEP_GROUPS):
+                cfg = dict(CONFIG3, bits=bits, group=group)
+                if args.batch:
+                    cfg["B"] = args.batch
+                lines.append(measure_variant(args, cfg, device, dist,
+                                             f"config3-sweep-b{bits}-g{group}"))
+    if dist is not None:
+        dist.destroy_process_group()
+    return lines if rank == 0 else []
+
+
+# ---------------------------------------------------------------------------
 # the reference CPU path (numpy port in oracle/)
 # ---------------------------------------------------------------------------
 def _cpu_unit(payload):
@@ -579,6 +763,10 @@ def run_reference(args) -> dict | None:
 
 def main(argv=None) -> int:
     args = parse_args(argv)
+    if args.impl == "ours" and args.config in (3, 4):
+        for line in run_variants(args):
+            print(json.dumps(line), flush=True)
+        return 0
     line = run_reference(args) if args.impl == "reference" else run_ours(args)
     if line is not None:
         print(json.dumps(line), flush=True)
