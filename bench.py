@@ -553,13 +553,16 @@ def measure_variant(args, cfg, device, dist, workload: str) -> dict:
     ws_base = (ws.data_ptr() + 255) // 256 * 256
     stream = torch.cuda.current_stream(device)
 
+    # the stream is looked up at each call: under graph capture it is the
+    # capturing stream
     def step(i):
         _native.check(lib.kvq_decode(margs[i % n_sets], out.data_ptr(), ws_base, ws_need,
-                                     stream.cuda_stream))
+                                     torch.cuda.current_stream(device).cuda_stream))
 
     def splits(i):
         _native.check(lib.kvq_decode_splits(margs[i % n_sets], po.data_ptr(), pm.data_ptr(),
-                                            pl.data_ptr(), stream.cuda_stream))
+                                            pl.data_ptr(),
+                                            torch.cuda.current_stream(device).cuda_stream))
 
     sampler = ClockSampler(local)
     sampler.start()

@@ -176,18 +176,20 @@ int plan(const kvq_args* a, Plan* pl) {
     P.t_begin = a->t_begin; P.t_end = a->t_end;
     P.r = a->n_heads / a->n_kv_heads;
     // The tensor-core kernels stream 16-byte-aligned runs of 8 rows with TMA:
-    // they need the fp16 / 4-bit / DH 128 format, at most 8 query heads per
-    // cache head, and 8-row-aligned geometry (the tcgen05 kernel, when asked
-    // for, group 64 as well); everything else runs on the CUDA-core kernel.
+    // they need fp16 steps, head_dim 128, 4-bit codes (or 8-bit at group 64),
+    // at most 8 query heads per cache head, and 8-row-aligned geometry (the
+    // tcgen05 kernel, when asked for, 4-bit group 64); everything else runs on
+    // the CUDA-core kernel.
     const bool tma_ok = aligned(a->k_wq, 16) && aligned(a->v_wq, 16) && aligned(a->k_scales, 16) &&
                         aligned(a->k_biases, 16) && aligned(a->v_scales, 16) &&
                         aligned(a->v_biases, 16) && a->t_stride % 8 == 0 &&
                         a->cache_batch_stride % 8 == 0 && a->t_begin % 8 == 0;
-    const bool tc = a->dtype == KVQ_F16 && a->bits == 4 && a->head_dim == 128 && P.r <= 8 && tma_ok;
+    const bool tc_format = a->bits == 4 || (a->bits == 8 && a->group_size == 64);
+    const bool tc = a->dtype == KVQ_F16 && tc_format && a->head_dim == 128 && P.r <= 8 && tma_ok;
     const int forced = kernel_override();
     if (!tc || forced == KERNEL_GENERIC)
         pl->kernel = KERNEL_GENERIC;
-    else if (a->group_size == 64 && forced == KERNEL_UMMA4)
+    else if (a->group_size == 64 && a->bits == 4 && forced == KERNEL_UMMA4)
         pl->kernel = KERNEL_UMMA4;
     else
         pl->kernel = KERNEL_MMA4;
@@ -208,7 +210,7 @@ int plan(const kvq_args* a, Plan* pl) {
             // final reduction) is worth about two tiles
             mma4_splits(span, units, kvq::umma4_ctas_per_sm(pl->ht), &P.chunk, &P.n_splits, 128, 256);
         else
-            mma4_splits(span, units, kvq::mma4_ctas_per_sm(pl->ht, a->group_size), &P.chunk,
+            mma4_splits(span, units, kvq::mma4_ctas_per_sm(pl->ht, a->group_size, a->bits), &P.chunk,
                         &P.n_splits, (uint64_t)kvq::mma4_stage_positions(), kMmaRamp);
         pl->part_bytes = align_up((size_t)P.n_splits * pl->rows * a->head_dim * sizeof(float));
         pl->ml_bytes = align_up((size_t)P.n_splits * pl->rows * sizeof(float));
@@ -234,7 +236,8 @@ cudaError_t launch_partial_any(const Plan& pl, uint32_t bits, uint32_t dtype, ui
                                float* o, float* m, float* l, cudaStream_t s) {
     if (pl.kernel == KERNEL_UMMA4) return kvq::launch_umma4(pl.P, pl.ht, o, m, l, s);
     if (pl.kernel == KERNEL_MMA4)
-        return kvq::launch_mma4(pl.P, pl.ht, pl.P.group_size, fast_precision() ? 2 : 3, o, m, l, s);
+        return kvq::launch_mma4(pl.P, pl.ht, pl.P.group_size, (int)bits, fast_precision() ? 2 : 3,
+                                o, m, l, s);
     switch (bits) {
         case 2: return kvq::launch_partial<2>(pl.P, dtype, dh, pl.ht, o, m, l, s);
         case 3: return kvq::launch_partial<3>(pl.P, dtype, dh, pl.ht, o, m, l, s);

@@ -26,11 +26,12 @@ cudaError_t launch_dequant(const uint32_t* wq, const void* scales, const void* b
                            uint64_t rows, uint32_t head_dim, uint32_t group, int dtype,
                            float* out, cudaStream_t stream);
 
-// Tensor-core partial kernel: fp16, 4-bit, head_dim 128, ht in {4, 8}.
-// parts: 3 (binary32-class combine weights, the default) or 2 (the opt-in
-// fast precision)
-cudaError_t launch_mma4(const Problem& P, int ht, int group, int parts, float* part_o, float* part_m,
-                        float* part_l, cudaStream_t stream);
+// Register-fragment tensor-core partial kernels: fp16, head_dim 128, ht in
+// {4, 8}; 4-bit codes at groups 32/64/128, 8-bit codes at group 64. parts: 3
+// (binary32-class combine weights, the default) or 2 (the opt-in fast
+// precision)
+cudaError_t launch_mma4(const Problem& P, int ht, int group, int bits, int parts, float* part_o,
+                        float* part_m, float* part_l, cudaStream_t stream);
 
 // Merges of n_parts partials; part p's O block starts o_stride floats after
 // part p-1's, its m and l ml_stride floats after (stacked partials:
@@ -52,7 +53,7 @@ int umma4_ctas_per_sm(int ht);
 // Resident tensor-core CTAs per SM for (ht, group) on the current device,
 // and the device's SM count (both cached per device; fixed fallbacks when the
 // device cannot be queried).
-int mma4_ctas_per_sm(int ht, int group);
+int mma4_ctas_per_sm(int ht, int group, int bits);
 int sm_count();
 // Positions per stage of the register-fragment kernels (split chunks are
 // multiples of it).

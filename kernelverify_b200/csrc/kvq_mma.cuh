@@ -52,18 +52,22 @@ constexpr uint32_t WAIT_LIMIT = 1u << 22;    // bounded mbarrier waits
 #define KVQ_MMA_MINBLOCKS 3                  // resident CTAs per SM the register budget targets
 #endif
 
-template <int GROUP>
+template <int GROUP, int BITS = 4>
 struct Layout {
     static constexpr int G = DH / GROUP;
-    static constexpr int KC = 0;                          // K codes   [TP][64]
-    static constexpr int VC = KC + TP * ROWB;             // V codes   [TP][64]
-    static constexpr int KS = VC + TP * ROWB;             // K scales  [TP][G] fp16
+    static constexpr int RB = DH * BITS / 8;              // code bytes per row
+    static constexpr int KC = 0;                          // K codes   [TP][RB]
+    static constexpr int VC = KC + TP * RB;               // V codes   [TP][RB]
+    static constexpr int KS = VC + TP * RB;               // K scales  [TP][G] fp16
     static constexpr int KB = KS + TP * G * 2;
     static constexpr int VS = KB + TP * G * 2;
     static constexpr int VB = VS + TP * G * 2;
     static constexpr int STAGE = VB + TP * G * 2;         // bytes per stage
     static_assert(STAGE % 128 == 0, "stage size");
-    static constexpr int RING = STAGE * STAGES;
+    // ring depth: 8-bit stages are twice the bytes, so fewer of them keep
+    // three CTAs' rings on an SM with about the same bytes in flight
+    static constexpr int NST = BITS == 8 ? (STAGES * 2 + 2) / 3 : STAGES;
+    static constexpr int RING = STAGE * NST;
     // per consumer warp: fp32 [16][G] k_scale, k_bias, v_scale, v_bias - 128 v_scale
     // of the warp's 16-position block
     static constexpr int SCR_WARP = 4 * 16 * G * 4;
@@ -71,11 +75,11 @@ struct Layout {
     static constexpr int RING_SCR = RING + CWARPS * SCR_WARP;
     // merge area (reuses the ring once it drains): per warp O[8][128], m[8], l[8], bsum[8][G]
     static constexpr int MERGE = CWARPS * (8 * DH + 8 + 8 + 8 * G) * 4 + 8 * 4;
-    static constexpr int BYTES = (RING_SCR > MERGE ? RING_SCR : MERGE) + 2 * STAGES * 8 + 16;
+    static constexpr int BYTES = (RING_SCR > MERGE ? RING_SCR : MERGE) + 2 * NST * 8 + 16;
 };
 
-template <int GROUP>
-constexpr size_t smem_bytes() { return Layout<GROUP>::BYTES; }
+template <int GROUP, int BITS = 4>
+constexpr size_t smem_bytes() { return Layout<GROUP, BITS>::BYTES; }
 
 // ---- PTX wrappers ------------------------------------------------------------
 __device__ __forceinline__ uint32_t s_addr(const void* p) {
@@ -286,12 +290,14 @@ __device__ __forceinline__ void load_g(const __half* p, float (&out)[G]) {
 // set of six contiguous runs (K codes, V codes, K/V scales and biases) of the
 // stage's rows, rounded up to whole 8-row runs; it waits (bounded) for every
 // consumer warp to release a slot before refilling it.
-template <int GROUP>
+template <int GROUP, int BITS = 4>
 __device__ __forceinline__ void produce(const Problem& P, unsigned char* smem, uint64_t* full,
                                         uint64_t* empty, int* err_flag, uint32_t lo, uint32_t hi,
                                         int n_stages, uint64_t rowbase) {
-    using Lay = Layout<GROUP>;
+    using Lay = Layout<GROUP, BITS>;
     constexpr int G = Lay::G;
+    constexpr int RB = Lay::RB;
+    constexpr int NST = Lay::NST;
     const uint64_t pol = evict_first_policy();
     const unsigned char* kw = reinterpret_cast<const unsigned char*>(P.k_wq);
     const unsigned char* vw = reinterpret_cast<const unsigned char*>(P.v_wq);
@@ -300,8 +306,8 @@ __device__ __forceinline__ void produce(const Problem& P, unsigned char* smem, u
     const unsigned char* vs = static_cast<const unsigned char*>(P.v_scales);
     const unsigned char* vb = static_cast<const unsigned char*>(P.v_biases);
     for (int s = 0; s < n_stages; ++s) {
-        const int slot = s % STAGES, round = s / STAGES;
-        if (s >= STAGES && !mbar_wait(&empty[slot], (round - 1) & 1)) {
+        const int slot = s % NST, round = s / NST;
+        if (s >= NST && !mbar_wait(&empty[slot], (round - 1) & 1)) {
             atomicExch(err_flag, 1);
             break;
         }
@@ -310,9 +316,9 @@ __device__ __forceinline__ void produce(const Problem& P, unsigned char* smem, u
         const uint32_t nr = (n + 7) & ~7u;
         const uint64_t row = rowbase + t0;
         unsigned char* st = smem + slot * Lay::STAGE;
-        mbar_expect_tx(&full[slot], nr * (2 * ROWB + 4 * G * 2));
-        bulk_g2s(st + Lay::KC, kw + row * ROWB, nr * ROWB, &full[slot], pol);
-        bulk_g2s(st + Lay::VC, vw + row * ROWB, nr * ROWB, &full[slot], pol);
+        mbar_expect_tx(&full[slot], nr * (2 * RB + 4 * G * 2));
+        bulk_g2s(st + Lay::KC, kw + row * RB, nr * RB, &full[slot], pol);
+        bulk_g2s(st + Lay::VC, vw + row * RB, nr * RB, &full[slot], pol);
         bulk_g2s(st + Lay::KS, ks + row * G * 2, nr * G * 2, &full[slot], pol);
         bulk_g2s(st + Lay::KB, kb + row * G * 2, nr * G * 2, &full[slot], pol);
         bulk_g2s(st + Lay::VS, vs + row * G * 2, nr * G * 2, &full[slot], pol);

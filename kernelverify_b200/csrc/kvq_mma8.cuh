@@ -1,0 +1,448 @@
+// Register-fragment tensor-core partial kernel for 8-bit caches: fp16 steps,
+// head_dim 128, group 64.
+//
+// The structure is the 4-bit transposed kernel's (kvq_mmat.cuh): the same
+// stage ring and producer (rows of 128 code bytes), score MMAs with the 16
+// positions of a warp's block as M rows, the score fragment transposed into
+// the combine's B fragment with movmatrix, the CTA merge. What the code width
+// changes:
+//
+// * Scores. A k-step covers 16 dims of one group: lane j holds dims
+//   64g + 16j + 4i + {0,1 | 2,3} at k-slots {2j, 2j+1 | 2j+8, 2j+9} of k-step
+//   c = 4g + i, so a lane reads its dims of a row as one 16-byte run per group
+//   and turns each code byte into fp16 exactly: a byte permute makes
+//   0x64cc = 1024 + c, one subtract leaves c. Q's B fragment follows the same
+//   dim order.
+// * Combine. An 8-bit code c = 16 h + l is carried as two bf16 values, both
+//   exact: 128 + l (0x4300 | l) and 2048 + 16 h (0x4500 | h), in two MMAs that
+//   share the P' fragments, so
+//     sum_t P'_t (128 + l_t) + sum_t P'_t (2048 + 16 h_t) = sum_t P'_t c_t + 2176 sum_t P'_t
+//   and the 2176 sum_t P'_t = sum_t p_t 2176 s_t is taken out through the bias
+//   term (v_bias - 2176 v_scale), as the 4-bit kernel takes out 128.
+//   Every M-tile keeps to one group (P' carries that group's scale): M-tile
+//   4g + mm, row r is dim 64g + 8r + 2mm, row r + 8 is that dim + 1, so a lane
+//   reads each position's bytes of a group as one 8-byte run.
+#pragma once
+
+#include "kvq_mmat.cuh"
+
+namespace kvq {
+namespace mma4 {
+
+// fp16 pairs of the exact code values of a word of four byte codes:
+// (c0, c1) and (c2, c3)
+__device__ __forceinline__ void bytes_f16(uint32_t w, uint32_t& h01, uint32_t& h23) {
+    h01 = h2_sub1024(prmt<0x4140>(w, 0x64646464u));
+    h23 = h2_sub1024(prmt<0x4342>(w, 0x64646464u));
+}
+
+// Bytes K, K+1 of words a and b -> the low-nibble (128 + l) and high-nibble
+// (2048 + 16 h) bf16 pairs (a.K, b.K) and (a.K+1, b.K+1).
+template <int K>
+__device__ __forceinline__ void byte_nibbles_bf16(uint32_t a, uint32_t b, uint32_t& lo0,
+                                                  uint32_t& hi0, uint32_t& lo1, uint32_t& hi1) {
+    constexpr uint32_t sel = K | ((K + 1) << 4) | ((4 + K) << 8) | ((5 + K) << 12);
+    const uint32_t u = prmt<sel>(a, b);
+    lo0 = and_or<0x000F000Fu, 0x43004300u>(u);
+    hi0 = and_or<0x000F000Fu, 0x45004500u>(u >> 4);
+    lo1 = and_or<0x000F000Fu, 0x43004300u>(u >> 8);
+    hi1 = and_or<0x000F000Fu, 0x45004500u>(u >> 12);
+}
+
+template <int HT, int PARTS>
+__global__ void __launch_bounds__(THREADS, KVQ_MMA_MINBLOCKS)
+partial_kernel_t8(Problem P, float* __restrict__ part_o, float* __restrict__ part_m,
+                  float* __restrict__ part_l) {
+    constexpr int GROUP = 64, BITS = 8;
+    using Lay = Layout<GROUP, BITS>;
+    constexpr int G = Lay::G;
+    constexpr int RB = Lay::RB;         // 128 code bytes per row
+    constexpr int NST = Lay::NST;       // ring depth of the 8-bit layout
+    constexpr int MTG = GROUP / 16;     // M-tiles per group
+    constexpr int MT = DH / 16;         // M-tiles
+    constexpr int NACC = HT == 4 ? 1 : G;
+    constexpr int NSC = HT == 4 ? 2 : 4;
+    constexpr float L2E = 1.4426950408889634f;
+    constexpr float VOFF = 2176.0f;     // 128 + 2048: the code offset the combine carries
+    static_assert(HT == 4 || HT == 8, "head tile");
+    static_assert(G == 2, "group 64 at head_dim 128");
+    const float scale2 = P.scale * L2E;
+
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (Lay::RING_SCR > Lay::MERGE ? Lay::RING_SCR : Lay::MERGE));
+    uint64_t* empty = full + NST;
+    int* err_flag = reinterpret_cast<int*>(empty + NST);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t split = blockIdx.x;
+    const uint32_t hk = blockIdx.y / P.head_tiles;
+    const uint32_t tile_h = blockIdx.y % P.head_tiles;
+    const uint32_t b = blockIdx.z;
+    const uint32_t h0 = hk * P.r + tile_h * HT;
+    const int nh = min(HT, (int)(P.r - tile_h * HT));
+    const uint32_t H = P.n_heads;
+
+    uint32_t len = P.t_cached;
+    if (P.seq_lens != nullptr) len = min((uint32_t)max(P.seq_lens[b], 0), P.t_cached);
+    const uint32_t end = min(P.t_end, len);
+    const uint32_t lo = P.t_begin + split * P.chunk;
+    const uint32_t hi = min(end, lo + P.chunk);
+    const int n_stages = hi > lo ? (int)((hi - lo + TP - 1) / TP) : 0;
+    const bool with_new = P.has_new_entry && split == P.n_splits - 1;
+    const uint64_t rowbase = (uint64_t)b * P.cache_batch_stride + (uint64_t)hk * P.t_stride;
+
+    if (tid == 0) {
+        for (int s = 0; s < NST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], CWARPS);
+        }
+        *err_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == CWARPS) {
+        if (lane == 0) produce<GROUP, BITS>(P, smem, full, empty, err_flag, lo, hi, n_stages, rowbase);
+    } else {
+        const int r = lane >> 2, j = lane & 3;
+        const int hp = HT == 4 ? (j & 1) : j;
+        const int half = HT == 4 ? (j >> 1) : 0;
+
+        // Q as the score MMA's B fragment: column n = r, k-step c = 4g + i over
+        // dims 64g + 16j + 4i + {0, 1} (b0) and {2, 3} (b1)
+        uint32_t qb[8][2];
+        float qcol[G] = {0.0f, 0.0f};
+        {
+            const int colh = HT == 4 ? (r & 3) : r;
+            const int colg = HT == 4 ? (r >> 2) : -1;
+            const bool qvalid = colh < nh;
+            const __half* q = static_cast<const __half*>(P.q) + ((size_t)b * H + h0 + colh) * DH;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const int g = c >> 2;
+                const int d = 64 * g + 16 * j + 4 * (c & 3);
+                const bool live = qvalid && (colg < 0 || colg == g);
+                __half2 x0 = live ? __halves2half2(q[d], q[d + 1]) : __half2(0, 0);
+                __half2 x1 = live ? __halves2half2(q[d + 2], q[d + 3]) : __half2(0, 0);
+                qcol[g] += __low2float(x0) + __high2float(x0) + __low2float(x1) + __high2float(x1);
+                qb[c][0] = *reinterpret_cast<uint32_t*>(&x0);
+                qb[c][1] = *reinterpret_cast<uint32_t*>(&x1);
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                qcol[g] += __shfl_xor_sync(0xffffffffu, qcol[g], 1);
+                qcol[g] += __shfl_xor_sync(0xffffffffu, qcol[g], 2);
+            }
+        }
+        float qs[G][2];
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int col = HT == 4 ? g * 4 + 2 * hp + k : 2 * hp + k;
+                qs[g][k] = __shfl_sync(0xffffffffu, qcol[g], 4 * col);
+            }
+
+        float m_run[2] = {-INFINITY, -INFINITY}, l_part[2] = {0.0f, 0.0f};
+        float bsum[G][2];
+        float oacc[MT][4];
+#pragma unroll
+        for (int g = 0; g < G; ++g) bsum[g][0] = bsum[g][1] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < MT; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.0f;
+
+        const int kr0 = (r >> 1) + 4 * (r & 1);   // position of fragment row r (row r+8: +8)
+
+        for (int s = 0; s < n_stages; ++s) {
+            const int slot = s % NST, round = s / NST;
+            if (!mbar_wait(&full[slot], round & 1)) {
+                atomicExch(err_flag, 1);
+                break;
+            }
+            unsigned char* st = smem + slot * Lay::STAGE;
+            const uint32_t t0 = lo + s * TP;
+            const int blk = warp;
+            const int nvalid = (int)min((uint32_t)TP, hi - t0);
+            if (nvalid <= blk * 16) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+                continue;
+            }
+            float* scr = reinterpret_cast<float*>(smem + Lay::SCR + warp * Lay::SCR_WARP);
+            {
+                const __half* kss = reinterpret_cast<const __half*>(st + Lay::KS) + blk * 16 * G;
+                const __half* kbs = reinterpret_cast<const __half*>(st + Lay::KB) + blk * 16 * G;
+                const __half* vss = reinterpret_cast<const __half*>(st + Lay::VS) + blk * 16 * G;
+                const __half* vbs = reinterpret_cast<const __half*>(st + Lay::VB) + blk * 16 * G;
+                const int nv_blk = nvalid - blk * 16;
+                for (int i = lane; i < 16 * G; i += 32) {
+                    const int pos = i / G, g = i % G;
+                    const bool live = pos < nv_blk;
+                    const float vsv = live ? __half2float(vss[i]) : 0.0f;
+                    const float vbv = live ? __half2float(vbs[i]) : 0.0f;
+                    scr[pos * 2 * G + g] = __half2float(kss[i]) * scale2;
+                    scr[pos * 2 * G + G + g] = __half2float(kbs[i]) * scale2;
+                    scr[16 * 2 * G + pos * 2 * G + g] = vsv;
+                    scr[16 * 2 * G + pos * 2 * G + G + g] = fmaf(vsv, -VOFF, vbv);
+                }
+                __syncwarp();
+            }
+            const float* kscr = scr;
+            const float* vscr = scr + 16 * 2 * G;
+
+            // ---- scores: 8 MMAs over the byte codes -----------------------
+            float acc[NACC][4];
+#pragma unroll
+            for (int n = 0; n < NACC; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+            {
+                const unsigned char* row0 = st + Lay::KC + (blk * 16 + kr0) * RB;
+                const unsigned char* row1 = row0 + 8 * RB;
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const uint4 w0 = *reinterpret_cast<const uint4*>(row0 + 64 * g + 16 * j);
+                    const uint4 w1 = *reinterpret_cast<const uint4*>(row1 + 64 * g + 16 * j);
+                    const uint32_t a[4] = {w0.x, w0.y, w0.z, w0.w};
+                    const uint32_t bw[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        uint32_t a01, a23, b01, b23;
+                        bytes_f16(a[i], a01, a23);
+                        bytes_f16(bw[i], b01, b23);
+                        float (&A)[4] = acc[HT == 4 ? 0 : g];
+                        const int c = 4 * g + i;
+                        mma_f16(A, a01, b01, a23, b23, qb[c][0], qb[c][1]);
+                    }
+                }
+            }
+            float sc[NSC];
+            if constexpr (HT == 4) {
+                const float s0 = half ? acc[0][0] : acc[0][2];
+                const float s1 = half ? acc[0][1] : acc[0][3];
+                const float r0 = __shfl_xor_sync(0xffffffffu, s0, 2);
+                const float r1 = __shfl_xor_sync(0xffffffffu, s1, 2);
+                const float x00 = half ? r0 : acc[0][0], x01 = half ? r1 : acc[0][1];   // group 0
+                const float x10 = half ? acc[0][2] : r0, x11 = half ? acc[0][3] : r1;   // group 1
+                const int lp = kr0 + 8 * half;
+                float kf[2 * G];
+                load_f<2 * G>(kscr + lp * 2 * G, kf);
+                const bool live = blk * 16 + lp < nvalid;
+                const float a0 = fmaf(kf[0], x00, fmaf(kf[1], x10, fmaf(kf[2], qs[0][0], kf[3] * qs[1][0])));
+                const float a1 = fmaf(kf[0], x01, fmaf(kf[1], x11, fmaf(kf[2], qs[0][1], kf[3] * qs[1][1])));
+                sc[0] = live ? a0 : -INFINITY;
+                sc[1] = live ? a1 : -INFINITY;
+            } else {
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) {
+                    const int lp = kr0 + 8 * rr;
+                    float kf[2 * G];
+                    load_f<2 * G>(kscr + lp * 2 * G, kf);
+                    const bool live = blk * 16 + lp < nvalid;
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        const float a = fmaf(kf[0], acc[0][2 * rr + k],
+                                             fmaf(kf[1], acc[1][2 * rr + k],
+                                                  fmaf(kf[2], qs[0][k], kf[3] * qs[1][k])));
+                        sc[2 * rr + k] = live ? a : -INFINITY;
+                    }
+                }
+            }
+
+            // ---- online softmax, lazy rescaling ----------------------------
+            float mx[2];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) mx[k] = HT == 4 ? sc[k] : fmaxf(sc[k], sc[2 + k]);
+            if (__any_sync(0xffffffffu, mx[0] > m_run[0] + 8.0f || mx[1] > m_run[1] + 8.0f)) {
+                float alpha[2];
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    float v = mx[k];
+                    if constexpr (HT == 4) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+                    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+                    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+                    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+                    const float m_new = v > m_run[k] + 8.0f ? v : m_run[k];
+                    alpha[k] = ex2(m_run[k] - m_new);
+                    m_run[k] = m_new;
+                    l_part[k] *= alpha[k];
+#pragma unroll
+                    for (int g = 0; g < G; ++g) bsum[g][k] *= alpha[k];
+                }
+                const float2 a01 = make_float2(alpha[0], alpha[1]);
+#pragma unroll
+                for (int i = 0; i < MT; ++i) {
+                    const float2 u = __fmul2_rn(make_float2(oacc[i][0], oacc[i][1]), a01);
+                    const float2 v = __fmul2_rn(make_float2(oacc[i][2], oacc[i][3]), a01);
+                    oacc[i][0] = u.x; oacc[i][1] = u.y; oacc[i][2] = v.x; oacc[i][3] = v.y;
+                }
+            }
+            float e[NSC];
+#pragma unroll
+            for (int i = 0; i < NSC; ++i) e[i] = ex2(sc[i] - m_run[i & 1]);
+#pragma unroll
+            for (int i = 0; i < NSC; ++i) l_part[i & 1] += e[i];
+
+            // ---- combine: B fragments of P' = p * v_scale by transposition --
+            uint32_t bf0[G], bf1[G], bs0[G], bs1[G], bt0[G], bt1[G];
+            if constexpr (HT == 4) {
+                const int lp = kr0 + 8 * half;
+                float vf[2 * G];
+                load_f<2 * G>(vscr + lp * 2 * G, vf);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    bsum[g][0] = fmaf(e[0], vf[G + g], bsum[g][0]);
+                    bsum[g][1] = fmaf(e[1], vf[G + g], bsum[g][1]);
+                    const float2 v = __fmul2_rn(make_float2(e[0], e[1]), make_float2(vf[g], vf[g]));
+                    uint32_t phi, pmid, plo;
+                    if constexpr (PARTS == 3) {
+                        split3(v.x, v.y, phi, pmid, plo);
+                    } else {
+                        split2(v.x, v.y, phi, pmid);
+                        plo = 0u;
+                    }
+                    const uint32_t recv = __shfl_xor_sync(0xffffffffu, half ? phi : pmid, 2);
+                    bf0[g] = transpose8x8(half ? recv : phi);
+                    bf1[g] = transpose8x8(half ? pmid : recv);
+                    if constexpr (PARTS == 3) {
+                        const uint32_t recv_lo = __shfl_xor_sync(0xffffffffu, plo, 2);
+                        bs0[g] = transpose8x8(half ? 0u : plo);
+                        bs1[g] = transpose8x8(half ? 0u : recv_lo);
+                    } else {
+                        bs0[g] = bs1[g] = 0u;
+                    }
+                    bt0[g] = bt1[g] = 0u;
+                }
+            } else {
+                float vf[2][2 * G];
+                load_f<2 * G>(vscr + kr0 * 2 * G, vf[0]);
+                load_f<2 * G>(vscr + (kr0 + 8) * 2 * G, vf[1]);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    uint32_t phi[2], pmid[2], plo[2];
+#pragma unroll
+                    for (int rr = 0; rr < 2; ++rr) {
+                        bsum[g][0] = fmaf(e[2 * rr], vf[rr][G + g], bsum[g][0]);
+                        bsum[g][1] = fmaf(e[2 * rr + 1], vf[rr][G + g], bsum[g][1]);
+                        const float2 v = __fmul2_rn(make_float2(e[2 * rr], e[2 * rr + 1]),
+                                                    make_float2(vf[rr][g], vf[rr][g]));
+                        if constexpr (PARTS == 3) {
+                            split3(v.x, v.y, phi[rr], pmid[rr], plo[rr]);
+                        } else {
+                            split2(v.x, v.y, phi[rr], pmid[rr]);
+                            plo[rr] = 0u;
+                        }
+                    }
+                    bf0[g] = transpose8x8(phi[0]);
+                    bf1[g] = transpose8x8(phi[1]);
+                    bs0[g] = transpose8x8(pmid[0]);
+                    bs1[g] = transpose8x8(pmid[1]);
+                    if constexpr (PARTS == 3) {
+                        bt0[g] = transpose8x8(plo[0]);
+                        bt1[g] = transpose8x8(plo[1]);
+                    } else {
+                        bt0[g] = bt1[g] = 0u;
+                    }
+                }
+            }
+            // A fragments (V codes^T, two nibble passes) and the MMAs: lane
+            // (r, j) reads dims 64g + 8r .. + 7 of positions j, j+4, j+8, j+12
+            const int p0 = blk * 16 + j;
+            const unsigned char* vrow = st + Lay::VC;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const int boff = 64 * g + 8 * r;
+                const uint2 wA = *reinterpret_cast<const uint2*>(vrow + (p0) * RB + boff);
+                const uint2 wB = *reinterpret_cast<const uint2*>(vrow + (p0 + 4) * RB + boff);
+                const uint2 wC = *reinterpret_cast<const uint2*>(vrow + (p0 + 8) * RB + boff);
+                const uint2 wD = *reinterpret_cast<const uint2*>(vrow + (p0 + 12) * RB + boff);
+#pragma unroll
+                for (int mm = 0; mm < MTG; ++mm) {
+                    // M-tile 4g + mm: bytes 2mm, 2mm + 1 of the lane's run
+                    const uint32_t xa = mm < 2 ? wA.x : wA.y, xb = mm < 2 ? wB.x : wB.y;
+                    const uint32_t xc = mm < 2 ? wC.x : wC.y, xd = mm < 2 ? wD.x : wD.y;
+                    uint32_t l0, h0v, l1, h1v, l2, h2v, l3, h3v;
+                    if ((mm & 1) == 0) {
+                        byte_nibbles_bf16<0>(xa, xb, l0, h0v, l1, h1v);
+                        byte_nibbles_bf16<0>(xc, xd, l2, h2v, l3, h3v);
+                    } else {
+                        byte_nibbles_bf16<2>(xa, xb, l0, h0v, l1, h1v);
+                        byte_nibbles_bf16<2>(xc, xd, l2, h2v, l3, h3v);
+                    }
+                    float (&o)[4] = oacc[g * MTG + mm];
+                    mma_bf16(o, l0, l1, l2, l3, bf0[g], bf1[g]);
+                    mma_bf16(o, h0v, h1v, h2v, h3v, bf0[g], bf1[g]);
+                    if constexpr (HT == 8 || PARTS == 3) {
+                        mma_bf16(o, l0, l1, l2, l3, bs0[g], bs1[g]);
+                        mma_bf16(o, h0v, h1v, h2v, h3v, bs0[g], bs1[g]);
+                    }
+                    if constexpr (HT == 8 && PARTS == 3) {
+                        mma_bf16(o, l0, l1, l2, l3, bt0[g], bt1[g]);
+                        mma_bf16(o, h0v, h1v, h2v, h3v, bt0[g], bt1[g]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+
+        // ---- warp partial ----------------------------------------------------
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+#pragma unroll
+            for (int x = 4; x <= 16; x <<= 1) {
+                l_part[k] += __shfl_xor_sync(0xffffffffu, l_part[k], x);
+#pragma unroll
+                for (int g = 0; g < G; ++g) bsum[g][k] += __shfl_xor_sync(0xffffffffu, bsum[g][k], x);
+            }
+            if constexpr (HT == 4) {
+                l_part[k] += __shfl_xor_sync(0xffffffffu, l_part[k], 2);
+#pragma unroll
+                for (int g = 0; g < G; ++g) bsum[g][k] += __shfl_xor_sync(0xffffffffu, bsum[g][k], 2);
+            }
+        }
+        if constexpr (HT == 4) {
+#pragma unroll
+            for (int i = 0; i < MT; ++i)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) oacc[i][c] += __shfl_xor_sync(0xffffffffu, oacc[i][c], 2);
+        }
+        named_sync(1, CWARPS * 32);  // every consumer is done with the ring
+        float* mo = reinterpret_cast<float*>(smem);                 // [CWARPS][8][DH]
+        float* mm_ = mo + CWARPS * 8 * DH;                          // [CWARPS][8]
+        float* ml = mm_ + CWARPS * 8;                               // [CWARPS][8]
+        float* mb = ml + CWARPS * 8;                                // [CWARPS][8][G]
+        if (r == 0 && (HT == 8 || j < 2)) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int h = 2 * hp + k;
+                mm_[warp * 8 + h] = m_run[k];
+                ml[warp * 8 + h] = l_part[k];
+#pragma unroll
+                for (int g = 0; g < G; ++g) mb[(warp * 8 + h) * G + g] = bsum[g][k];
+            }
+        }
+        if (HT == 8 || j < 2) {
+#pragma unroll
+            for (int i = 0; i < MT; ++i) {
+                const int g = i / MTG, mm = i % MTG;
+                const int d = 64 * g + 8 * r + 2 * mm;    // row r; row r + 8 is d + 1
+                const int c0 = 2 * j, c1 = 2 * j + 1;
+                mo[(warp * 8 + c0) * DH + d] = oacc[i][0];
+                mo[(warp * 8 + c1) * DH + d] = oacc[i][1];
+                mo[(warp * 8 + c0) * DH + d + 1] = oacc[i][2];
+                mo[(warp * 8 + c1) * DH + d + 1] = oacc[i][3];
+            }
+        }
+        finish_partial<HT, GROUP>(P, smem, tid, warp, lane, split, b, hk, h0, nh, with_new, scale2,
+                                  err_flag, part_o, part_m, part_l);
+    }
+    __syncthreads();
+    if (tid == CWARPS * 32 && *(volatile int*)err_flag) {
+        for (int s = 0; s < NST && s < n_stages; ++s) {
+            const int last = ((n_stages - 1 - s) / NST) * NST + s;
+            (void)mbar_wait(&full[s], (last / NST) & 1);
+        }
+    }
+}
+
+}  // namespace mma4
+}  // namespace kvq

@@ -1,19 +1,22 @@
-// Register-fragment tensor-core partial kernels (fp16 steps, 4-bit caches,
-// head_dim 128): the transposed-score kernel for group 64, the original one
-// for groups 32 and 128.
+// Register-fragment tensor-core partial kernels (fp16 steps, head_dim 128):
+// for 4-bit caches the transposed-score kernel (group 64) and the original
+// one (groups 32 and 128); for 8-bit caches the byte-code kernel (group 64).
 #include <atomic>
 
 #include "kvq_launch.h"
 #include "kvq_mma.cuh"
+#include "kvq_mma8.cuh"
 #include "kvq_mmat.cuh"
 
 namespace kvq {
 
 constexpr int kMaxDevices = 64;
 
-template <int HT, int GROUP, int PARTS>
+template <int HT, int GROUP, int PARTS, int BITS>
 constexpr auto mma4_kernel() {
-    if constexpr (GROUP == 64)
+    if constexpr (BITS == 8)
+        return mma4::partial_kernel_t8<HT, PARTS>;
+    else if constexpr (GROUP == 64)
         return mma4::partial_kernel_t<HT, PARTS>;
     else
         return mma4::partial_kernel<HT, GROUP, PARTS>;
@@ -22,7 +25,7 @@ constexpr auto mma4_kernel() {
 // The kernel's attributes (dynamic shared memory above 48 KB; a carveout that
 // prefers shared memory, so three CTAs fit on an SM), set once per device so
 // that later launches, captured ones included, make no attribute calls.
-template <int HT, int GROUP, int PARTS>
+template <int HT, int GROUP, int PARTS, int BITS>
 static cudaError_t mma4_prepare() {
     static std::atomic<uint64_t> done{0};
     int dev = 0;
@@ -30,9 +33,9 @@ static cudaError_t mma4_prepare() {
     if (e != cudaSuccess) return e;
     const uint64_t bit = dev >= 0 && dev < kMaxDevices ? 1ull << dev : 0;
     if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
-    auto kernel = mma4_kernel<HT, GROUP, PARTS>();
+    auto kernel = mma4_kernel<HT, GROUP, PARTS, BITS>();
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)mma4::smem_bytes<GROUP>());
+                             (int)mma4::smem_bytes<GROUP, BITS>());
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared);
@@ -41,16 +44,17 @@ static cudaError_t mma4_prepare() {
     return cudaSuccess;
 }
 
-template <int HT, int GROUP, int PARTS>
+template <int HT, int GROUP, int PARTS, int BITS>
 static cudaError_t mma4_one(const Problem& P, float* o, float* m, float* l, cudaStream_t stream) {
-    cudaError_t e = mma4_prepare<HT, GROUP, PARTS>();
+    cudaError_t e = mma4_prepare<HT, GROUP, PARTS, BITS>();
     if (e != cudaSuccess) return e;
     dim3 grid(P.n_splits, P.n_kv_heads * P.head_tiles, P.b_rows);
-    mma4_kernel<HT, GROUP, PARTS>()<<<grid, mma4::THREADS, mma4::smem_bytes<GROUP>(), stream>>>(P, o, m, l);
+    mma4_kernel<HT, GROUP, PARTS, BITS>()<<<grid, mma4::THREADS, mma4::smem_bytes<GROUP, BITS>(),
+                                            stream>>>(P, o, m, l);
     return cudaGetLastError();
 }
 
-template <int HT, int GROUP>
+template <int HT, int GROUP, int BITS>
 static int mma4_occupancy() {
     constexpr int PARTS = 3;
     static std::atomic<int> cached[kMaxDevices] = {};
@@ -58,21 +62,23 @@ static int mma4_occupancy() {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
     int n = cached[dev].load(std::memory_order_relaxed);
     if (n > 0) return n;
-    if (mma4_prepare<HT, GROUP, PARTS>() != cudaSuccess) return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, mma4_kernel<HT, GROUP, PARTS>(),
+    if (mma4_prepare<HT, GROUP, PARTS, BITS>() != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, mma4_kernel<HT, GROUP, PARTS, BITS>(),
                                                       mma4::THREADS,
-                                                      mma4::smem_bytes<GROUP>()) != cudaSuccess)
+                                                      mma4::smem_bytes<GROUP, BITS>()) != cudaSuccess)
         return 0;
     cached[dev].store(n, std::memory_order_relaxed);
     return n;
 }
 
-int mma4_ctas_per_sm(int ht, int group) {
+int mma4_ctas_per_sm(int ht, int group, int bits) {
     int n = 0;
-    if (ht == 4)
-        n = group == 32 ? mma4_occupancy<4, 32>() : group == 64 ? mma4_occupancy<4, 64>() : mma4_occupancy<4, 128>();
+    if (bits == 8)
+        n = ht == 4 ? mma4_occupancy<4, 64, 8>() : mma4_occupancy<8, 64, 8>();
+    else if (ht == 4)
+        n = group == 32 ? mma4_occupancy<4, 32, 4>() : group == 64 ? mma4_occupancy<4, 64, 4>() : mma4_occupancy<4, 128, 4>();
     else
-        n = group == 32 ? mma4_occupancy<8, 32>() : group == 64 ? mma4_occupancy<8, 64>() : mma4_occupancy<8, 128>();
+        n = group == 32 ? mma4_occupancy<8, 32, 4>() : group == 64 ? mma4_occupancy<8, 64, 4>() : mma4_occupancy<8, 128, 4>();
     if (n <= 0) {
         cudaGetLastError();  // a failed query leaves no error behind
         n = group == 32 ? 2 : 3;
@@ -100,24 +106,31 @@ int sm_count() {
 }
 
 template <int PARTS>
-static cudaError_t launch_parts(const Problem& P, int ht, int group, float* o, float* m, float* l,
-                                cudaStream_t stream) {
+static cudaError_t launch_parts(const Problem& P, int ht, int group, int bits, float* o, float* m,
+                                float* l, cudaStream_t stream) {
+    if (bits == 8) {
+        if (group != 64) return cudaErrorInvalidValue;
+        if (ht == 4) return mma4_one<4, 64, PARTS, 8>(P, o, m, l, stream);
+        if (ht == 8) return mma4_one<8, 64, PARTS, 8>(P, o, m, l, stream);
+        return cudaErrorInvalidValue;
+    }
+    if (bits != 4) return cudaErrorInvalidValue;
     if (ht == 4) {
-        if (group == 32) return mma4_one<4, 32, PARTS>(P, o, m, l, stream);
-        if (group == 64) return mma4_one<4, 64, PARTS>(P, o, m, l, stream);
-        if (group == 128) return mma4_one<4, 128, PARTS>(P, o, m, l, stream);
+        if (group == 32) return mma4_one<4, 32, PARTS, 4>(P, o, m, l, stream);
+        if (group == 64) return mma4_one<4, 64, PARTS, 4>(P, o, m, l, stream);
+        if (group == 128) return mma4_one<4, 128, PARTS, 4>(P, o, m, l, stream);
     } else if (ht == 8) {
-        if (group == 32) return mma4_one<8, 32, PARTS>(P, o, m, l, stream);
-        if (group == 64) return mma4_one<8, 64, PARTS>(P, o, m, l, stream);
-        if (group == 128) return mma4_one<8, 128, PARTS>(P, o, m, l, stream);
+        if (group == 32) return mma4_one<8, 32, PARTS, 4>(P, o, m, l, stream);
+        if (group == 64) return mma4_one<8, 64, PARTS, 4>(P, o, m, l, stream);
+        if (group == 128) return mma4_one<8, 128, PARTS, 4>(P, o, m, l, stream);
     }
     return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_mma4(const Problem& P, int ht, int group, int parts, float* o, float* m, float* l,
-                        cudaStream_t stream) {
-    return parts == 2 ? launch_parts<2>(P, ht, group, o, m, l, stream)
-                      : launch_parts<3>(P, ht, group, o, m, l, stream);
+cudaError_t launch_mma4(const Problem& P, int ht, int group, int bits, int parts, float* o,
+                        float* m, float* l, cudaStream_t stream) {
+    return parts == 2 ? launch_parts<2>(P, ht, group, bits, o, m, l, stream)
+                      : launch_parts<3>(P, ht, group, bits, o, m, l, stream);
 }
 
 }  // namespace kvq
