@@ -1,27 +1,31 @@
-// Register-fragment tensor-core partial kernel for 8-bit caches: fp16 steps,
-// head_dim 128, group 64.
+// Register-fragment tensor-core partial kernel over byte codes: fp16 steps,
+// head_dim 128, group 64, caches of 2-, 3-, 6- or 8-bit codes.
 //
 // The structure is the 4-bit transposed kernel's (kvq_mmat.cuh): the same
-// stage ring and producer (rows of 128 code bytes), score MMAs with the 16
-// positions of a warp's block as M rows, the score fragment transposed into
-// the combine's B fragment with movmatrix, the CTA merge. What the code width
-// changes:
+// stage ring and producer (rows of DH * BITS / 8 code bytes), score MMAs with
+// the 16 positions of a warp's block as M rows, the score fragment transposed
+// into the combine's B fragment with movmatrix, the CTA merge. A lane reads
+// the packed bits of the codes it needs (an aligned word load and one funnel
+// shift bring the first code to bit 0) and spreads them to one code per byte
+// in registers; from there every width is the 8-bit arithmetic:
 //
 // * Scores. A k-step covers 16 dims of one group: lane j holds dims
 //   64g + 16j + 4i + {0,1 | 2,3} at k-slots {2j, 2j+1 | 2j+8, 2j+9} of k-step
-//   c = 4g + i, so a lane reads its dims of a row as one 16-byte run per group
+//   c = 4g + i, so a lane reads its dims of a row as one run per group
 //   and turns each code byte into fp16 exactly: a byte permute makes
 //   0x64cc = 1024 + c, one subtract leaves c. Q's B fragment follows the same
 //   dim order.
-// * Combine. An 8-bit code c = 16 h + l is carried as two bf16 values, both
+// * Combine. A code c = 16 h + l is carried as two bf16 values, both
 //   exact: 128 + l (0x4300 | l) and 2048 + 16 h (0x4500 | h), in two MMAs that
 //   share the P' fragments, so
 //     sum_t P'_t (128 + l_t) + sum_t P'_t (2048 + 16 h_t) = sum_t P'_t c_t + 2176 sum_t P'_t
 //   and the 2176 sum_t P'_t = sum_t p_t 2176 s_t is taken out through the bias
-//   term (v_bias - 2176 v_scale), as the 4-bit kernel takes out 128.
+//   term (v_bias - 2176 v_scale), as the 4-bit kernel takes out 128. Codes
+//   below 16 (2 and 3 bits) have h = 0: the second MMA is left out and the
+//   offset is 128.
 //   Every M-tile keeps to one group (P' carries that group's scale): M-tile
 //   4g + mm, row r is dim 64g + 8r + 2mm, row r + 8 is that dim + 1, so a lane
-//   reads each position's bytes of a group as one 8-byte run.
+//   reads each position's codes of a group as one run of 8 codes.
 #pragma once
 
 #include "kvq_mmat.cuh"
@@ -34,6 +38,61 @@ namespace mma4 {
 __device__ __forceinline__ void bytes_f16(uint32_t w, uint32_t& h01, uint32_t& h23) {
     h01 = h2_sub1024(prmt<0x4140>(w, 0x64646464u));
     h23 = h2_sub1024(prmt<0x4342>(w, 0x64646464u));
+}
+
+// Four BITS-bit codes at bits 0 .. 4 BITS - 1 of x -> one code per byte.
+template <int BITS>
+__device__ __forceinline__ uint32_t spread4(uint32_t x) {
+    if constexpr (BITS == 8) {
+        return x;
+    } else if constexpr (BITS == 2) {
+        x &= 0xFFu;
+        const uint32_t t = (x | (x << 12)) & 0x000F000Fu;          // (c0 c1 | c2 c3)
+        return (t | (t << 6)) & 0x03030303u;
+    } else if constexpr (BITS == 3) {
+        x &= 0xFFFu;
+        const uint32_t t = (x | (x << 10)) & 0x003F003Fu;
+        return (t | (t << 5)) & 0x07070707u;
+    } else {
+        static_assert(BITS == 6, "code width");
+        x &= 0xFFFFFFu;
+        const uint32_t t = (x & 0xFFFu) | ((x << 4) & 0x0FFF0000u);  // bits 12..15 unused
+        return (t & 0x003F003Fu) | ((t << 2) & 0x3F003F00u);
+    }
+}
+
+// N codes (a multiple of 4) starting at code k0 (a multiple of 8) of a row of
+// packed BITS-bit codes -> N / 4 words, one code per byte. Only the 4-byte
+// aligned words that hold bits of the run are read, so every read lies in the
+// row.
+template <int BITS, int N>
+__device__ __forceinline__ void codes_to_bytes(const unsigned char* row, int k0,
+                                               uint32_t (&out)[N / 4]) {
+    if constexpr (BITS == 8) {
+#pragma unroll
+        for (int m = 0; m < N / 4; ++m)
+            out[m] = *reinterpret_cast<const uint32_t*>(row + k0 + 4 * m);
+    } else {
+        constexpr int NBITS = N * BITS;
+        constexpr int NW = (NBITS + 24 + 31) / 32;      // words that can hold the run
+        const int ob = k0 * BITS / 8;                   // first byte (k0 * BITS is a multiple of 8)
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(row + (ob & ~3));
+        const uint32_t sh = (uint32_t)(ob & 3) * 8u;
+        uint32_t raw[NW + 1];
+#pragma unroll
+        for (int i = 0; i < NW; ++i) raw[i] = (32 * i < NBITS + (int)sh) ? w[i] : 0u;
+        raw[NW] = 0u;
+        uint32_t v[NW];
+#pragma unroll
+        for (int i = 0; i < NW; ++i) v[i] = __funnelshift_r(raw[i], raw[i + 1], sh);
+#pragma unroll
+        for (int m = 0; m < N / 4; ++m) {
+            const int bit = 4 * BITS * m;               // compile-time after unrolling
+            const int wi = bit >> 5, bs = bit & 31;
+            const uint32_t x = bs == 0 ? v[wi] : __funnelshift_r(v[wi], wi + 1 < NW ? v[wi + 1] : 0u, bs);
+            out[m] = spread4<BITS>(x);
+        }
+    }
 }
 
 // Bytes K, K+1 of words a and b -> the low-nibble (128 + l) and high-nibble
@@ -49,21 +108,23 @@ __device__ __forceinline__ void byte_nibbles_bf16(uint32_t a, uint32_t b, uint32
     hi1 = and_or<0x000F000Fu, 0x45004500u>(u >> 12);
 }
 
-template <int HT, int PARTS>
+template <int HT, int PARTS, int BITS>
 __global__ void __launch_bounds__(THREADS, KVQ_MMA_MINBLOCKS)
-partial_kernel_t8(Problem P, float* __restrict__ part_o, float* __restrict__ part_m,
+partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ part_m,
                   float* __restrict__ part_l) {
-    constexpr int GROUP = 64, BITS = 8;
+    constexpr int GROUP = 64;
+    static_assert(BITS == 2 || BITS == 3 || BITS == 6 || BITS == 8, "code width");
     using Lay = Layout<GROUP, BITS>;
     constexpr int G = Lay::G;
-    constexpr int RB = Lay::RB;         // 128 code bytes per row
-    constexpr int NST = Lay::NST;       // ring depth of the 8-bit layout
+    constexpr int RB = Lay::RB;         // code bytes per row
+    constexpr int NST = Lay::NST;       // ring depth of this width's layout
+    constexpr bool HI = BITS > 4;       // codes of 16 and above: the high-nibble pass
     constexpr int MTG = GROUP / 16;     // M-tiles per group
     constexpr int MT = DH / 16;         // M-tiles
     constexpr int NACC = HT == 4 ? 1 : G;
     constexpr int NSC = HT == 4 ? 2 : 4;
     constexpr float L2E = 1.4426950408889634f;
-    constexpr float VOFF = 2176.0f;     // 128 + 2048: the code offset the combine carries
+    constexpr float VOFF = HI ? 2176.0f : 128.0f;   // the code offset the combine carries
     static_assert(HT == 4 || HT == 8, "head tile");
     static_assert(G == 2, "group 64 at head_dim 128");
     const float scale2 = P.scale * L2E;
@@ -199,10 +260,16 @@ partial_kernel_t8(Problem P, float* __restrict__ part_o, float* __restrict__ par
                 const unsigned char* row1 = row0 + 8 * RB;
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
-                    const uint4 w0 = *reinterpret_cast<const uint4*>(row0 + 64 * g + 16 * j);
-                    const uint4 w1 = *reinterpret_cast<const uint4*>(row1 + 64 * g + 16 * j);
-                    const uint32_t a[4] = {w0.x, w0.y, w0.z, w0.w};
-                    const uint32_t bw[4] = {w1.x, w1.y, w1.z, w1.w};
+                    uint32_t a[4], bw[4];
+                    if constexpr (BITS == 8) {
+                        const uint4 w0 = *reinterpret_cast<const uint4*>(row0 + 64 * g + 16 * j);
+                        const uint4 w1 = *reinterpret_cast<const uint4*>(row1 + 64 * g + 16 * j);
+                        a[0] = w0.x; a[1] = w0.y; a[2] = w0.z; a[3] = w0.w;
+                        bw[0] = w1.x; bw[1] = w1.y; bw[2] = w1.z; bw[3] = w1.w;
+                    } else {
+                        codes_to_bytes<BITS, 16>(row0, 64 * g + 16 * j, a);
+                        codes_to_bytes<BITS, 16>(row1, 64 * g + 16 * j, bw);
+                    }
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         uint32_t a01, a23, b01, b23;
@@ -349,11 +416,20 @@ partial_kernel_t8(Problem P, float* __restrict__ part_o, float* __restrict__ par
             const unsigned char* vrow = st + Lay::VC;
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-                const int boff = 64 * g + 8 * r;
-                const uint2 wA = *reinterpret_cast<const uint2*>(vrow + (p0) * RB + boff);
-                const uint2 wB = *reinterpret_cast<const uint2*>(vrow + (p0 + 4) * RB + boff);
-                const uint2 wC = *reinterpret_cast<const uint2*>(vrow + (p0 + 8) * RB + boff);
-                const uint2 wD = *reinterpret_cast<const uint2*>(vrow + (p0 + 12) * RB + boff);
+                const int k0 = 64 * g + 8 * r;
+                uint2 wA, wB, wC, wD;
+                if constexpr (BITS == 8) {
+                    wA = *reinterpret_cast<const uint2*>(vrow + (p0) * RB + k0);
+                    wB = *reinterpret_cast<const uint2*>(vrow + (p0 + 4) * RB + k0);
+                    wC = *reinterpret_cast<const uint2*>(vrow + (p0 + 8) * RB + k0);
+                    wD = *reinterpret_cast<const uint2*>(vrow + (p0 + 12) * RB + k0);
+                } else {
+                    uint32_t t[2];
+                    codes_to_bytes<BITS, 8>(vrow + (p0) * RB, k0, t);      wA = make_uint2(t[0], t[1]);
+                    codes_to_bytes<BITS, 8>(vrow + (p0 + 4) * RB, k0, t);  wB = make_uint2(t[0], t[1]);
+                    codes_to_bytes<BITS, 8>(vrow + (p0 + 8) * RB, k0, t);  wC = make_uint2(t[0], t[1]);
+                    codes_to_bytes<BITS, 8>(vrow + (p0 + 12) * RB, k0, t); wD = make_uint2(t[0], t[1]);
+                }
 #pragma unroll
                 for (int mm = 0; mm < MTG; ++mm) {
                     // M-tile 4g + mm: bytes 2mm, 2mm + 1 of the lane's run
@@ -369,14 +445,14 @@ partial_kernel_t8(Problem P, float* __restrict__ part_o, float* __restrict__ par
                     }
                     float (&o)[4] = oacc[g * MTG + mm];
                     mma_bf16(o, l0, l1, l2, l3, bf0[g], bf1[g]);
-                    mma_bf16(o, h0v, h1v, h2v, h3v, bf0[g], bf1[g]);
+                    if constexpr (HI) mma_bf16(o, h0v, h1v, h2v, h3v, bf0[g], bf1[g]);
                     if constexpr (HT == 8 || PARTS == 3) {
                         mma_bf16(o, l0, l1, l2, l3, bs0[g], bs1[g]);
-                        mma_bf16(o, h0v, h1v, h2v, h3v, bs0[g], bs1[g]);
+                        if constexpr (HI) mma_bf16(o, h0v, h1v, h2v, h3v, bs0[g], bs1[g]);
                     }
                     if constexpr (HT == 8 && PARTS == 3) {
                         mma_bf16(o, l0, l1, l2, l3, bt0[g], bt1[g]);
-                        mma_bf16(o, h0v, h1v, h2v, h3v, bt0[g], bt1[g]);
+                        if constexpr (HI) mma_bf16(o, h0v, h1v, h2v, h3v, bt0[g], bt1[g]);
                     }
                 }
             }

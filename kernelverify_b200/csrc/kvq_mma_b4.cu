@@ -1,6 +1,7 @@
 // Register-fragment tensor-core partial kernels (fp16 steps, head_dim 128):
 // for 4-bit caches the transposed-score kernel (group 64) and the original
-// one (groups 32 and 128); for 8-bit caches the byte-code kernel (group 64).
+// one (groups 32 and 128); for 2-, 3-, 6- and 8-bit caches the byte-code
+// kernel (group 64).
 #include <atomic>
 
 #include "kvq_launch.h"
@@ -14,8 +15,8 @@ constexpr int kMaxDevices = 64;
 
 template <int HT, int GROUP, int PARTS, int BITS>
 constexpr auto mma4_kernel() {
-    if constexpr (BITS == 8)
-        return mma4::partial_kernel_t8<HT, PARTS>;
+    if constexpr (BITS != 4)
+        return mma4::partial_kernel_tb<HT, PARTS, BITS>;
     else if constexpr (GROUP == 64)
         return mma4::partial_kernel_t<HT, PARTS>;
     else
@@ -73,9 +74,14 @@ static int mma4_occupancy() {
 
 int mma4_ctas_per_sm(int ht, int group, int bits) {
     int n = 0;
-    if (bits == 8)
-        n = ht == 4 ? mma4_occupancy<4, 64, 8>() : mma4_occupancy<8, 64, 8>();
-    else if (ht == 4)
+    if (bits != 4) {
+        switch (bits) {
+            case 2: n = ht == 4 ? mma4_occupancy<4, 64, 2>() : mma4_occupancy<8, 64, 2>(); break;
+            case 3: n = ht == 4 ? mma4_occupancy<4, 64, 3>() : mma4_occupancy<8, 64, 3>(); break;
+            case 6: n = ht == 4 ? mma4_occupancy<4, 64, 6>() : mma4_occupancy<8, 64, 6>(); break;
+            default: n = ht == 4 ? mma4_occupancy<4, 64, 8>() : mma4_occupancy<8, 64, 8>(); break;
+        }
+    } else if (ht == 4)
         n = group == 32 ? mma4_occupancy<4, 32, 4>() : group == 64 ? mma4_occupancy<4, 64, 4>() : mma4_occupancy<4, 128, 4>();
     else
         n = group == 32 ? mma4_occupancy<8, 32, 4>() : group == 64 ? mma4_occupancy<8, 64, 4>() : mma4_occupancy<8, 128, 4>();
@@ -108,10 +114,18 @@ int sm_count() {
 template <int PARTS>
 static cudaError_t launch_parts(const Problem& P, int ht, int group, int bits, float* o, float* m,
                                 float* l, cudaStream_t stream) {
-    if (bits == 8) {
-        if (group != 64) return cudaErrorInvalidValue;
-        if (ht == 4) return mma4_one<4, 64, PARTS, 8>(P, o, m, l, stream);
-        if (ht == 8) return mma4_one<8, 64, PARTS, 8>(P, o, m, l, stream);
+    if (bits != 4) {
+        if (group != 64 || (ht != 4 && ht != 8)) return cudaErrorInvalidValue;
+        switch (bits) {
+            case 2: return ht == 4 ? mma4_one<4, 64, PARTS, 2>(P, o, m, l, stream)
+                                   : mma4_one<8, 64, PARTS, 2>(P, o, m, l, stream);
+            case 3: return ht == 4 ? mma4_one<4, 64, PARTS, 3>(P, o, m, l, stream)
+                                   : mma4_one<8, 64, PARTS, 3>(P, o, m, l, stream);
+            case 6: return ht == 4 ? mma4_one<4, 64, PARTS, 6>(P, o, m, l, stream)
+                                   : mma4_one<8, 64, PARTS, 6>(P, o, m, l, stream);
+            case 8: return ht == 4 ? mma4_one<4, 64, PARTS, 8>(P, o, m, l, stream)
+                                   : mma4_one<8, 64, PARTS, 8>(P, o, m, l, stream);
+        }
         return cudaErrorInvalidValue;
     }
     if (bits != 4) return cudaErrorInvalidValue;

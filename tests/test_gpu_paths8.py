@@ -1,10 +1,10 @@
-"""The 8-bit tensor-core kernel (fp16, head_dim 128, group 64, 8-row-aligned
-geometry) against the oracle and against the CUDA-core kernel on the same
-inputs, in both precisions: GQA ratios up to 8 (config 4's 28/4 among them),
-lengths that end mid-stage, ragged per-sequence caches, T-range shards and
-outlier caches. Each case first checks that the library planned the
-tensor-core kernel, so the comparison is never the CUDA-core kernel with
-itself."""
+"""The byte-code tensor-core kernel (fp16, head_dim 128, group 64, 2-, 3-, 6-
+and 8-bit codes, 8-row-aligned geometry) against the oracle and against the
+CUDA-core kernel on the same inputs, in both precisions: GQA ratios up to 8
+(config 4's 28/4 among them), lengths that end mid-stage, ragged per-sequence
+caches, T-range shards and outlier caches. Each case first checks that the
+library planned the tensor-core kernel, so the comparison is never the
+CUDA-core kernel with itself."""
 
 from __future__ import annotations
 
@@ -17,10 +17,10 @@ from tests.test_gpu_paths import close, run_with
 
 pytestmark = pytest.mark.gpu
 
-BITS = 8
+WIDTHS = (2, 3, 6, 8)
 
 
-def planned(q, kc, vc, nk, nv, t_cached=None, seq_lens=None, k_art=None, v_art=None):
+def planned(q, kc, vc, nk, nv, BITS, t_cached=None, seq_lens=None, k_art=None, v_art=None):
     from kernelverify_b200.pack import kv_attention as kva
     kw, ks, kb = k_art if k_art is not None else pack(kc, BITS)
     vw, vs, vb = v_art if v_art is not None else pack(vc, BITS)
@@ -34,12 +34,13 @@ def three(fn):
     return run_with(None, fn), run_with(None, fn, "fast"), run_with("generic", fn)
 
 
+@pytest.mark.parametrize("BITS", WIDTHS)
 @pytest.mark.parametrize("h,hkv", [(8, 8), (8, 4), (8, 2), (32, 8), (28, 4), (64, 8), (6, 2)])
-def test_8bit_tensor_core_gqa(native, h, hkv):
+def test_byte_kernel_gqa(native, h, hkv, BITS):
     t = 1000
     q, kc, vc, nk, nv = cases.make_case(2, h, t, 128, seed=h * 11 + hkv)
     kc, vc, nk, nv = kc[:hkv], vc[:hkv], nk[:, :hkv], nv[:, :hkv]
-    assert planned(q, kc, vc, nk, nv) == "tensor-core"
+    assert planned(q, kc, vc, nk, nv, BITS) == "tensor-core"
     tc, fast, gen = three(lambda: run_decode(q, kc, vc, nk, nv, BITS))
     for out in (tc, fast, gen):
         v = judge_gqa(q, kc, vc, nk, nv, BITS, out)
@@ -47,8 +48,9 @@ def test_8bit_tensor_core_gqa(native, h, hkv):
     assert close(tc, gen) and close(fast, gen)
 
 
+@pytest.mark.parametrize("BITS", WIDTHS)
 @pytest.mark.parametrize("t", [1, 7, 8, 63, 64, 65, 129, 4096, 9000])
-def test_8bit_tensor_core_lengths(native, t):
+def test_byte_kernel_lengths(native, t, BITS):
     q, kc, vc, nk, nv = cases.make_case(1, 8, max(t, 8), 128, seed=2000 + t)
     kc, vc = kc[:2, :t], vc[:2, :t]
     nk, nv = nk[:, :2], nv[:, :2]
@@ -57,7 +59,8 @@ def test_8bit_tensor_core_lengths(native, t):
     junk = rng.standard_normal((2, t_pad - t, 128)).astype(np.float16) * 30
     k_art = pack(np.concatenate([kc, junk], axis=1), BITS)
     v_art = pack(np.concatenate([vc, junk], axis=1), BITS)
-    assert planned(q, None, None, nk, nv, t_cached=t, k_art=k_art, v_art=v_art) == "tensor-core"
+    assert planned(q, None, None, nk, nv, BITS, t_cached=t, k_art=k_art,
+                   v_art=v_art) == "tensor-core"
     tc, fast, gen = three(lambda: run_decode(q, None, None, nk, nv, BITS, t_cached=t, k_art=k_art,
                                              v_art=v_art))
     for out in (tc, fast, gen):
@@ -66,7 +69,8 @@ def test_8bit_tensor_core_lengths(native, t):
     assert close(tc, gen) and close(fast, gen)
 
 
-def test_8bit_tensor_core_ragged_per_sequence(native):
+@pytest.mark.parametrize("BITS", WIDTHS)
+def test_byte_kernel_ragged_per_sequence(native, BITS):
     """Config 4's form: one cache per sequence, device lengths, GQA 7."""
     rng = np.random.default_rng(18)
     b, h, hkv, t_pad = 5, 28, 4, 2048
@@ -76,7 +80,8 @@ def test_8bit_tensor_core_ragged_per_sequence(native):
     vc = rng.standard_normal((b, hkv, t_pad, 128)).astype(np.float16)
     nk = rng.standard_normal((b, hkv, 128)).astype(np.float16)
     nv = rng.standard_normal((b, hkv, 128)).astype(np.float16)
-    assert planned(q, kc, vc, nk, nv, t_cached=int(lens.max()), seq_lens=lens) == "tensor-core"
+    assert planned(q, kc, vc, nk, nv, BITS, t_cached=int(lens.max()),
+                   seq_lens=lens) == "tensor-core"
     tc, fast, gen = three(lambda: run_decode(q, kc, vc, nk, nv, BITS, t_cached=int(lens.max()),
                                              seq_lens=lens))
     for out in (tc, fast, gen):
@@ -85,7 +90,8 @@ def test_8bit_tensor_core_ragged_per_sequence(native):
     assert close(tc, gen) and close(fast, gen)
 
 
-def test_8bit_tensor_core_t_split_shards(native):
+@pytest.mark.parametrize("BITS", WIDTHS)
+def test_byte_kernel_t_split_shards(native, BITS):
     import torch
     from kernelverify_b200.pack import kv_attention as kva
     q, kc, vc, nk, nv = cases.make_case(1, 64, 4096, 128, seed=5)
@@ -100,7 +106,8 @@ def test_8bit_tensor_core_t_split_shards(native):
     assert v.ok, v
 
 
-def test_8bit_tensor_core_outlier_caches(native):
+@pytest.mark.parametrize("BITS", WIDTHS)
+def test_byte_kernel_outlier_caches(native, BITS):
     rng = np.random.default_rng(44)
     q, nk, nv = (rng.standard_normal(s).astype(np.float16)
                  for s in ((2, 32, 128), (2, 8, 128), (2, 8, 128)))
@@ -108,7 +115,7 @@ def test_8bit_tensor_core_outlier_caches(native):
     raw[rng.random(raw.shape) < 0.01] *= 20
     raw = raw.astype(np.float16)
     kc, vc = raw[0], raw[1]
-    assert planned(q, kc, vc, nk, nv) == "tensor-core"
+    assert planned(q, kc, vc, nk, nv, BITS) == "tensor-core"
     tc, fast, gen = three(lambda: run_decode(q, kc, vc, nk, nv, BITS))
     for out in (tc, fast, gen):
         for v in judge_per_sequence(q, kc, vc, nk, nv, BITS, out):
