@@ -128,9 +128,8 @@ int kvq_decode_partial(const kvq_args* a, float* part_o, float* part_m, float* p
  */
 #define KVQ_KERNEL_CUDA_CORE 0
 #define KVQ_KERNEL_TENSOR_CORE 1   /* register-fragment mma.sync kernels: fp16,
-                                      head_dim 128, 4-bit codes at any group or
-                                      any width at group 64, <= 8 query heads
-                                      per cache head */
+                                      head_dim 128, <= 8 query heads per cache
+                                      head, every width and group */
 #define KVQ_KERNEL_TCGEN05 2       /* the tcgen05 kernel (KVQ_KERNEL=umma)  */
 int kvq_plan_kernel(const kvq_args* a);
 

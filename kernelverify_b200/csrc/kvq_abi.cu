@@ -176,16 +176,14 @@ int plan(const kvq_args* a, Plan* pl) {
     P.t_begin = a->t_begin; P.t_end = a->t_end;
     P.r = a->n_heads / a->n_kv_heads;
     // The tensor-core kernels stream 16-byte-aligned runs of 8 rows with TMA:
-    // they need fp16 steps, head_dim 128, 4-bit codes (any other width at
-    // group 64), at most 8 query heads per cache head, and 8-row-aligned geometry (the
-    // tcgen05 kernel, when asked for, 4-bit group 64); everything else runs on
-    // the CUDA-core kernel.
+    // they need fp16 steps, head_dim 128, at most 8 query heads per cache
+    // head, and 8-row-aligned geometry (the tcgen05 kernel, when asked for,
+    // 4-bit group 64); everything else runs on the CUDA-core kernel.
     const bool tma_ok = aligned(a->k_wq, 16) && aligned(a->v_wq, 16) && aligned(a->k_scales, 16) &&
                         aligned(a->k_biases, 16) && aligned(a->v_scales, 16) &&
                         aligned(a->v_biases, 16) && a->t_stride % 8 == 0 &&
                         a->cache_batch_stride % 8 == 0 && a->t_begin % 8 == 0;
-    const bool tc_format = a->bits == 4 || a->group_size == 64;
-    const bool tc = a->dtype == KVQ_F16 && tc_format && a->head_dim == 128 && P.r <= 8 && tma_ok;
+    const bool tc = a->dtype == KVQ_F16 && a->head_dim == 128 && P.r <= 8 && tma_ok;
     const int forced = kernel_override();
     if (!tc || forced == KERNEL_GENERIC)
         pl->kernel = KERNEL_GENERIC;

@@ -1,5 +1,5 @@
 // Register-fragment tensor-core partial kernel over byte codes: fp16 steps,
-// head_dim 128, group 64, caches of 2-, 3-, 6- or 8-bit codes.
+// head_dim 128, caches of 2-, 3-, 6- or 8-bit codes at groups 32, 64, 128.
 //
 // The structure is the 4-bit transposed kernel's (kvq_mmat.cuh): the same
 // stage ring and producer (rows of DH * BITS / 8 code bytes), score MMAs with
@@ -9,12 +9,10 @@
 // shift bring the first code to bit 0) and spreads them to one code per byte
 // in registers; from there every width is the 8-bit arithmetic:
 //
-// * Scores. A k-step covers 16 dims of one group: lane j holds dims
-//   64g + 16j + 4i + {0,1 | 2,3} at k-slots {2j, 2j+1 | 2j+8, 2j+9} of k-step
-//   c = 4g + i, so a lane reads its dims of a row as one run per group
-//   and turns each code byte into fp16 exactly: a byte permute makes
-//   0x64cc = 1024 + c, one subtract leaves c. Q's B fragment follows the same
-//   dim order.
+// * Scores. Each score k-step covers 16 dims of one group; a lane reads its
+//   dims of a row as one run per dim block and turns each code byte into fp16
+//   exactly: a byte permute makes 0x64cc = 1024 + c, one subtract leaves c.
+//   Q's B fragment follows the same dim order.
 // * Combine. A code c = 16 h + l is carried as two bf16 values, both
 //   exact: 128 + l (0x4300 | l) and 2048 + 16 h (0x4500 | h), in two MMAs that
 //   share the P' fragments, so
@@ -22,10 +20,7 @@
 //   and the 2176 sum_t P'_t = sum_t p_t 2176 s_t is taken out through the bias
 //   term (v_bias - 2176 v_scale), as the 4-bit kernel takes out 128. Codes
 //   below 16 (2 and 3 bits) have h = 0: the second MMA is left out and the
-//   offset is 128.
-//   Every M-tile keeps to one group (P' carries that group's scale): M-tile
-//   4g + mm, row r is dim 64g + 8r + 2mm, row r + 8 is that dim + 1, so a lane
-//   reads each position's codes of a group as one run of 8 codes.
+//   offset is 128. Every M-tile keeps to one group, whose scale P' carries.
 #pragma once
 
 #include "kvq_mmat.cuh"
@@ -61,37 +56,31 @@ __device__ __forceinline__ uint32_t spread4(uint32_t x) {
     }
 }
 
-// N codes (a multiple of 4) starting at code k0 (a multiple of 8) of a row of
-// packed BITS-bit codes -> N / 4 words, one code per byte. Only the 4-byte
-// aligned words that hold bits of the run are read, so every read lies in the
-// row.
+// N codes (a multiple of 4) starting at code k0 of a row of packed BITS-bit
+// codes -> N / 4 words, one code per byte. Only the 4-byte aligned words that
+// hold bits of the run are read, so every read lies in the row (rows are whole
+// words).
 template <int BITS, int N>
 __device__ __forceinline__ void codes_to_bytes(const unsigned char* row, int k0,
                                                uint32_t (&out)[N / 4]) {
-    if constexpr (BITS == 8) {
+    constexpr int NBITS = N * BITS;
+    constexpr int NW = (NBITS + 31 + 31) / 32;          // words that can hold the run
+    const int bitpos = k0 * BITS;
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(row) + (bitpos >> 5);
+    const uint32_t sh = (uint32_t)(bitpos & 31);
+    uint32_t raw[NW + 1];
 #pragma unroll
-        for (int m = 0; m < N / 4; ++m)
-            out[m] = *reinterpret_cast<const uint32_t*>(row + k0 + 4 * m);
-    } else {
-        constexpr int NBITS = N * BITS;
-        constexpr int NW = (NBITS + 24 + 31) / 32;      // words that can hold the run
-        const int ob = k0 * BITS / 8;                   // first byte (k0 * BITS is a multiple of 8)
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(row + (ob & ~3));
-        const uint32_t sh = (uint32_t)(ob & 3) * 8u;
-        uint32_t raw[NW + 1];
+    for (int i = 0; i < NW; ++i) raw[i] = (32 * i < NBITS + (int)sh) ? w[i] : 0u;
+    raw[NW] = 0u;
+    uint32_t v[NW];
 #pragma unroll
-        for (int i = 0; i < NW; ++i) raw[i] = (32 * i < NBITS + (int)sh) ? w[i] : 0u;
-        raw[NW] = 0u;
-        uint32_t v[NW];
+    for (int i = 0; i < NW; ++i) v[i] = __funnelshift_r(raw[i], raw[i + 1], sh);
 #pragma unroll
-        for (int i = 0; i < NW; ++i) v[i] = __funnelshift_r(raw[i], raw[i + 1], sh);
-#pragma unroll
-        for (int m = 0; m < N / 4; ++m) {
-            const int bit = 4 * BITS * m;               // compile-time after unrolling
-            const int wi = bit >> 5, bs = bit & 31;
-            const uint32_t x = bs == 0 ? v[wi] : __funnelshift_r(v[wi], wi + 1 < NW ? v[wi + 1] : 0u, bs);
-            out[m] = spread4<BITS>(x);
-        }
+    for (int m = 0; m < N / 4; ++m) {
+        const int bit = 4 * BITS * m;                   // compile-time after unrolling
+        const int wi = bit >> 5, bs = bit & 31;
+        const uint32_t x = bs == 0 ? v[wi] : __funnelshift_r(v[wi], wi + 1 < NW ? v[wi + 1] : 0u, bs);
+        out[m] = spread4<BITS>(x);
     }
 }
 
@@ -108,25 +97,61 @@ __device__ __forceinline__ void byte_nibbles_bf16(uint32_t a, uint32_t b, uint32
     hi1 = and_or<0x000F000Fu, 0x45004500u>(u >> 12);
 }
 
-template <int HT, int PARTS, int BITS>
+// Byte loads of an 8-bit run (16, 8 or 4 codes) with the widest aligned load.
+template <int N>
+__device__ __forceinline__ void byte_run(const unsigned char* p, uint32_t (&out)[N / 4]) {
+    if constexpr (N == 16) {
+        const uint4 w = *reinterpret_cast<const uint4*>(p);
+        out[0] = w.x; out[1] = w.y; out[2] = w.z; out[3] = w.w;
+    } else if constexpr (N == 8) {
+        const uint2 w = *reinterpret_cast<const uint2*>(p);
+        out[0] = w.x; out[1] = w.y;
+    } else {
+        out[0] = *reinterpret_cast<const uint32_t*>(p);
+    }
+}
+
+// N codes of a row starting at code k0, one per byte
+template <int BITS, int N>
+__device__ __forceinline__ void run_bytes(const unsigned char* row, int k0, uint32_t (&out)[N / 4]) {
+    if constexpr (BITS == 8)
+        byte_run<N>(row + k0, out);
+    else
+        codes_to_bytes<BITS, N>(row, k0, out);
+}
+
+// Dims are taken in NB blocks of BD: 64-dim blocks up to group 64, one block
+// per group at group 32, so every score k-step and every combine M-tile lies
+// in one group. Score side: block b holds k-steps b * KPB + i, lane j the
+// dims BD b + SRUN j + 4 i + {0, 1 | 2, 3}. Combine side: M-tile b * MTB + mm,
+// row r is dim BD b + VRUN r + 2 mm, row r + 8 that dim + 1. At group 64 with
+// at most 4 query heads per cache head the score MMA's 8 columns are (group,
+// head) pairs (COLS); otherwise columns are heads, with one accumulator chain
+// per group.
+template <int HT, int PARTS, int BITS, int GROUP>
 __global__ void __launch_bounds__(THREADS, KVQ_MMA_MINBLOCKS)
 partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ part_m,
                   float* __restrict__ part_l) {
-    constexpr int GROUP = 64;
     static_assert(BITS == 2 || BITS == 3 || BITS == 6 || BITS == 8, "code width");
     using Lay = Layout<GROUP, BITS>;
     constexpr int G = Lay::G;
     constexpr int RB = Lay::RB;         // code bytes per row
     constexpr int NST = Lay::NST;       // ring depth of this width's layout
     constexpr bool HI = BITS > 4;       // codes of 16 and above: the high-nibble pass
-    constexpr int MTG = GROUP / 16;     // M-tiles per group
+    constexpr int NB = G > 2 ? G : 2;   // dim blocks
+    constexpr int BD = DH / NB;         // dims per block (64 or 32)
+    constexpr int KPB = BD / 16;        // score k-steps per block
+    constexpr int SRUN = BD / 4;        // score-side codes of a lane per (row, block)
+    constexpr int VRUN = BD / 8;        // combine-side codes of a lane per (position, block)
+    constexpr int MTB = BD / 16;        // M-tiles per block
     constexpr int MT = DH / 16;         // M-tiles
-    constexpr int NACC = HT == 4 ? 1 : G;
-    constexpr int NSC = HT == 4 ? 2 : 4;
+    constexpr bool COLS = HT == 4 && G == 2;
+    constexpr int NACC = COLS ? 1 : G;
+    constexpr int NSC = COLS ? 2 : 4;
     constexpr float L2E = 1.4426950408889634f;
     constexpr float VOFF = HI ? 2176.0f : 128.0f;   // the code offset the combine carries
-    static_assert(HT == 4 || HT == 8, "head tile");
-    static_assert(G == 2, "group 64 at head_dim 128");
+    static_assert(HT == 8 || COLS, "head tile 4 only with the (group, head) columns");
+    static_assert(NB * KPB == 8 && NB * MTB == MT, "block shape");
     const float scale2 = P.scale * L2E;
 
     extern __shared__ __align__(128) unsigned char smem[];
@@ -166,22 +191,24 @@ partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ par
         if (lane == 0) produce<GROUP, BITS>(P, smem, full, empty, err_flag, lo, hi, n_stages, rowbase);
     } else {
         const int r = lane >> 2, j = lane & 3;
-        const int hp = HT == 4 ? (j & 1) : j;
-        const int half = HT == 4 ? (j >> 1) : 0;
+        const int hp = COLS ? (j & 1) : j;
+        const int half = COLS ? (j >> 1) : 0;
 
-        // Q as the score MMA's B fragment: column n = r, k-step c = 4g + i over
-        // dims 64g + 16j + 4i + {0, 1} (b0) and {2, 3} (b1)
+        // Q as the score MMA's B fragment: column n = r, k-step c = KPB bb + i
+        // over dims BD bb + SRUN j + 4 i + {0, 1} (b0) and {2, 3} (b1)
         uint32_t qb[8][2];
-        float qcol[G] = {0.0f, 0.0f};
+        float qcol[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) qcol[g] = 0.0f;
         {
-            const int colh = HT == 4 ? (r & 3) : r;
-            const int colg = HT == 4 ? (r >> 2) : -1;
+            const int colh = COLS ? (r & 3) : r;
+            const int colg = COLS ? (r >> 2) : -1;
             const bool qvalid = colh < nh;
             const __half* q = static_cast<const __half*>(P.q) + ((size_t)b * H + h0 + colh) * DH;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-                const int g = c >> 2;
-                const int d = 64 * g + 16 * j + 4 * (c & 3);
+                const int bb = c / KPB, g = bb * G / NB;
+                const int d = BD * bb + SRUN * j + 4 * (c % KPB);
                 const bool live = qvalid && (colg < 0 || colg == g);
                 __half2 x0 = live ? __halves2half2(q[d], q[d + 1]) : __half2(0, 0);
                 __half2 x1 = live ? __halves2half2(q[d + 2], q[d + 3]) : __half2(0, 0);
@@ -200,7 +227,7 @@ partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ par
         for (int g = 0; g < G; ++g)
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
-                const int col = HT == 4 ? g * 4 + 2 * hp + k : 2 * hp + k;
+                const int col = COLS ? g * 4 + 2 * hp + k : 2 * hp + k;
                 qs[g][k] = __shfl_sync(0xffffffffu, qcol[g], 4 * col);
             }
 
@@ -259,30 +286,23 @@ partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ par
                 const unsigned char* row0 = st + Lay::KC + (blk * 16 + kr0) * RB;
                 const unsigned char* row1 = row0 + 8 * RB;
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    uint32_t a[4], bw[4];
-                    if constexpr (BITS == 8) {
-                        const uint4 w0 = *reinterpret_cast<const uint4*>(row0 + 64 * g + 16 * j);
-                        const uint4 w1 = *reinterpret_cast<const uint4*>(row1 + 64 * g + 16 * j);
-                        a[0] = w0.x; a[1] = w0.y; a[2] = w0.z; a[3] = w0.w;
-                        bw[0] = w1.x; bw[1] = w1.y; bw[2] = w1.z; bw[3] = w1.w;
-                    } else {
-                        codes_to_bytes<BITS, 16>(row0, 64 * g + 16 * j, a);
-                        codes_to_bytes<BITS, 16>(row1, 64 * g + 16 * j, bw);
-                    }
+                for (int bb = 0; bb < NB; ++bb) {
+                    uint32_t a[SRUN / 4], bw[SRUN / 4];
+                    run_bytes<BITS, SRUN>(row0, BD * bb + SRUN * j, a);
+                    run_bytes<BITS, SRUN>(row1, BD * bb + SRUN * j, bw);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
+                    for (int i = 0; i < KPB; ++i) {
                         uint32_t a01, a23, b01, b23;
                         bytes_f16(a[i], a01, a23);
                         bytes_f16(bw[i], b01, b23);
-                        float (&A)[4] = acc[HT == 4 ? 0 : g];
-                        const int c = 4 * g + i;
+                        float (&A)[4] = acc[COLS ? 0 : bb * G / NB];
+                        const int c = KPB * bb + i;
                         mma_f16(A, a01, b01, a23, b23, qb[c][0], qb[c][1]);
                     }
                 }
             }
             float sc[NSC];
-            if constexpr (HT == 4) {
+            if constexpr (COLS) {
                 const float s0 = half ? acc[0][0] : acc[0][2];
                 const float s1 = half ? acc[0][1] : acc[0][3];
                 const float r0 = __shfl_xor_sync(0xffffffffu, s0, 2);
@@ -306,9 +326,10 @@ partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ par
                     const bool live = blk * 16 + lp < nvalid;
 #pragma unroll
                     for (int k = 0; k < 2; ++k) {
-                        const float a = fmaf(kf[0], acc[0][2 * rr + k],
-                                             fmaf(kf[1], acc[1][2 * rr + k],
-                                                  fmaf(kf[2], qs[0][k], kf[3] * qs[1][k])));
+                        float a = 0.0f;
+#pragma unroll
+                        for (int g = 0; g < G; ++g)
+                            a = fmaf(kf[g], acc[g][2 * rr + k], fmaf(kf[G + g], qs[g][k], a));
                         sc[2 * rr + k] = live ? a : -INFINITY;
                     }
                 }
@@ -317,13 +338,13 @@ partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ par
             // ---- online softmax, lazy rescaling ----------------------------
             float mx[2];
 #pragma unroll
-            for (int k = 0; k < 2; ++k) mx[k] = HT == 4 ? sc[k] : fmaxf(sc[k], sc[2 + k]);
+            for (int k = 0; k < 2; ++k) mx[k] = COLS ? sc[k] : fmaxf(sc[k], sc[2 + k]);
             if (__any_sync(0xffffffffu, mx[0] > m_run[0] + 8.0f || mx[1] > m_run[1] + 8.0f)) {
                 float alpha[2];
 #pragma unroll
                 for (int k = 0; k < 2; ++k) {
                     float v = mx[k];
-                    if constexpr (HT == 4) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+                    if constexpr (COLS) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
                     v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
                     v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
                     v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
@@ -348,17 +369,19 @@ partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ par
 #pragma unroll
             for (int i = 0; i < NSC; ++i) l_part[i & 1] += e[i];
 
-            // ---- combine: B fragments of P' = p * v_scale by transposition --
-            uint32_t bf0[G], bf1[G], bs0[G], bs1[G], bt0[G], bt1[G];
-            if constexpr (HT == 4) {
-                const int lp = kr0 + 8 * half;
-                float vf[2 * G];
-                load_f<2 * G>(vscr + lp * 2 * G, vf);
+            // ---- combine, group by group: B fragments of P' = p * v_scale by
+            // transposition, then the group's M-tiles (V codes^T, nibble passes)
+            const int p0 = blk * 16 + j;
+            const unsigned char* vrow = st + Lay::VC;
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    bsum[g][0] = fmaf(e[0], vf[G + g], bsum[g][0]);
-                    bsum[g][1] = fmaf(e[1], vf[G + g], bsum[g][1]);
-                    const float2 v = __fmul2_rn(make_float2(e[0], e[1]), make_float2(vf[g], vf[g]));
+            for (int g = 0; g < G; ++g) {
+                uint32_t bf0, bf1, bs0, bs1, bt0 = 0u, bt1 = 0u;
+                if constexpr (COLS) {
+                    const int lp = kr0 + 8 * half;
+                    const float vs_ = vscr[lp * 2 * G + g], vb_ = vscr[lp * 2 * G + G + g];
+                    bsum[g][0] = fmaf(e[0], vb_, bsum[g][0]);
+                    bsum[g][1] = fmaf(e[1], vb_, bsum[g][1]);
+                    const float2 v = __fmul2_rn(make_float2(e[0], e[1]), make_float2(vs_, vs_));
                     uint32_t phi, pmid, plo;
                     if constexpr (PARTS == 3) {
                         split3(v.x, v.y, phi, pmid, plo);
@@ -367,30 +390,25 @@ partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ par
                         plo = 0u;
                     }
                     const uint32_t recv = __shfl_xor_sync(0xffffffffu, half ? phi : pmid, 2);
-                    bf0[g] = transpose8x8(half ? recv : phi);
-                    bf1[g] = transpose8x8(half ? pmid : recv);
+                    bf0 = transpose8x8(half ? recv : phi);
+                    bf1 = transpose8x8(half ? pmid : recv);
                     if constexpr (PARTS == 3) {
                         const uint32_t recv_lo = __shfl_xor_sync(0xffffffffu, plo, 2);
-                        bs0[g] = transpose8x8(half ? 0u : plo);
-                        bs1[g] = transpose8x8(half ? 0u : recv_lo);
+                        bs0 = transpose8x8(half ? 0u : plo);
+                        bs1 = transpose8x8(half ? 0u : recv_lo);
                     } else {
-                        bs0[g] = bs1[g] = 0u;
+                        bs0 = bs1 = 0u;
                     }
-                    bt0[g] = bt1[g] = 0u;
-                }
-            } else {
-                float vf[2][2 * G];
-                load_f<2 * G>(vscr + kr0 * 2 * G, vf[0]);
-                load_f<2 * G>(vscr + (kr0 + 8) * 2 * G, vf[1]);
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
+                } else {
                     uint32_t phi[2], pmid[2], plo[2];
 #pragma unroll
                     for (int rr = 0; rr < 2; ++rr) {
-                        bsum[g][0] = fmaf(e[2 * rr], vf[rr][G + g], bsum[g][0]);
-                        bsum[g][1] = fmaf(e[2 * rr + 1], vf[rr][G + g], bsum[g][1]);
+                        const int lp = kr0 + 8 * rr;
+                        const float vs_ = vscr[lp * 2 * G + g], vb_ = vscr[lp * 2 * G + G + g];
+                        bsum[g][0] = fmaf(e[2 * rr], vb_, bsum[g][0]);
+                        bsum[g][1] = fmaf(e[2 * rr + 1], vb_, bsum[g][1]);
                         const float2 v = __fmul2_rn(make_float2(e[2 * rr], e[2 * rr + 1]),
-                                                    make_float2(vf[rr][g], vf[rr][g]));
+                                                    make_float2(vs_, vs_));
                         if constexpr (PARTS == 3) {
                             split3(v.x, v.y, phi[rr], pmid[rr], plo[rr]);
                         } else {
@@ -398,61 +416,47 @@ partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ par
                             plo[rr] = 0u;
                         }
                     }
-                    bf0[g] = transpose8x8(phi[0]);
-                    bf1[g] = transpose8x8(phi[1]);
-                    bs0[g] = transpose8x8(pmid[0]);
-                    bs1[g] = transpose8x8(pmid[1]);
+                    bf0 = transpose8x8(phi[0]);
+                    bf1 = transpose8x8(phi[1]);
+                    bs0 = transpose8x8(pmid[0]);
+                    bs1 = transpose8x8(pmid[1]);
                     if constexpr (PARTS == 3) {
-                        bt0[g] = transpose8x8(plo[0]);
-                        bt1[g] = transpose8x8(plo[1]);
-                    } else {
-                        bt0[g] = bt1[g] = 0u;
+                        bt0 = transpose8x8(plo[0]);
+                        bt1 = transpose8x8(plo[1]);
                     }
                 }
-            }
-            // A fragments (V codes^T, two nibble passes) and the MMAs: lane
-            // (r, j) reads dims 64g + 8r .. + 7 of positions j, j+4, j+8, j+12
-            const int p0 = blk * 16 + j;
-            const unsigned char* vrow = st + Lay::VC;
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const int k0 = 64 * g + 8 * r;
-                uint2 wA, wB, wC, wD;
-                if constexpr (BITS == 8) {
-                    wA = *reinterpret_cast<const uint2*>(vrow + (p0) * RB + k0);
-                    wB = *reinterpret_cast<const uint2*>(vrow + (p0 + 4) * RB + k0);
-                    wC = *reinterpret_cast<const uint2*>(vrow + (p0 + 8) * RB + k0);
-                    wD = *reinterpret_cast<const uint2*>(vrow + (p0 + 12) * RB + k0);
-                } else {
-                    uint32_t t[2];
-                    codes_to_bytes<BITS, 8>(vrow + (p0) * RB, k0, t);      wA = make_uint2(t[0], t[1]);
-                    codes_to_bytes<BITS, 8>(vrow + (p0 + 4) * RB, k0, t);  wB = make_uint2(t[0], t[1]);
-                    codes_to_bytes<BITS, 8>(vrow + (p0 + 8) * RB, k0, t);  wC = make_uint2(t[0], t[1]);
-                    codes_to_bytes<BITS, 8>(vrow + (p0 + 12) * RB, k0, t); wD = make_uint2(t[0], t[1]);
-                }
+                for (int bb = g * NB / G; bb < (g + 1) * NB / G; ++bb) {
+                    const int k0 = BD * bb + VRUN * r;
+                    uint32_t wA[VRUN / 4], wB[VRUN / 4], wC[VRUN / 4], wD[VRUN / 4];
+                    run_bytes<BITS, VRUN>(vrow + (p0) * RB, k0, wA);
+                    run_bytes<BITS, VRUN>(vrow + (p0 + 4) * RB, k0, wB);
+                    run_bytes<BITS, VRUN>(vrow + (p0 + 8) * RB, k0, wC);
+                    run_bytes<BITS, VRUN>(vrow + (p0 + 12) * RB, k0, wD);
 #pragma unroll
-                for (int mm = 0; mm < MTG; ++mm) {
-                    // M-tile 4g + mm: bytes 2mm, 2mm + 1 of the lane's run
-                    const uint32_t xa = mm < 2 ? wA.x : wA.y, xb = mm < 2 ? wB.x : wB.y;
-                    const uint32_t xc = mm < 2 ? wC.x : wC.y, xd = mm < 2 ? wD.x : wD.y;
-                    uint32_t l0, h0v, l1, h1v, l2, h2v, l3, h3v;
-                    if ((mm & 1) == 0) {
-                        byte_nibbles_bf16<0>(xa, xb, l0, h0v, l1, h1v);
-                        byte_nibbles_bf16<0>(xc, xd, l2, h2v, l3, h3v);
-                    } else {
-                        byte_nibbles_bf16<2>(xa, xb, l0, h0v, l1, h1v);
-                        byte_nibbles_bf16<2>(xc, xd, l2, h2v, l3, h3v);
-                    }
-                    float (&o)[4] = oacc[g * MTG + mm];
-                    mma_bf16(o, l0, l1, l2, l3, bf0[g], bf1[g]);
-                    if constexpr (HI) mma_bf16(o, h0v, h1v, h2v, h3v, bf0[g], bf1[g]);
-                    if constexpr (HT == 8 || PARTS == 3) {
-                        mma_bf16(o, l0, l1, l2, l3, bs0[g], bs1[g]);
-                        if constexpr (HI) mma_bf16(o, h0v, h1v, h2v, h3v, bs0[g], bs1[g]);
-                    }
-                    if constexpr (HT == 8 && PARTS == 3) {
-                        mma_bf16(o, l0, l1, l2, l3, bt0[g], bt1[g]);
-                        if constexpr (HI) mma_bf16(o, h0v, h1v, h2v, h3v, bt0[g], bt1[g]);
+                    for (int mm = 0; mm < MTB; ++mm) {
+                        // M-tile MTB bb + mm: bytes 2mm, 2mm + 1 of the lane's run
+                        const uint32_t xa = wA[mm >> 1], xb = wB[mm >> 1];
+                        const uint32_t xc = wC[mm >> 1], xd = wD[mm >> 1];
+                        uint32_t l0, h0v, l1, h1v, l2, h2v, l3, h3v;
+                        if ((mm & 1) == 0) {
+                            byte_nibbles_bf16<0>(xa, xb, l0, h0v, l1, h1v);
+                            byte_nibbles_bf16<0>(xc, xd, l2, h2v, l3, h3v);
+                        } else {
+                            byte_nibbles_bf16<2>(xa, xb, l0, h0v, l1, h1v);
+                            byte_nibbles_bf16<2>(xc, xd, l2, h2v, l3, h3v);
+                        }
+                        float (&o)[4] = oacc[bb * MTB + mm];
+                        mma_bf16(o, l0, l1, l2, l3, bf0, bf1);
+                        if constexpr (HI) mma_bf16(o, h0v, h1v, h2v, h3v, bf0, bf1);
+                        if constexpr (HT == 8 || PARTS == 3) {
+                            mma_bf16(o, l0, l1, l2, l3, bs0, bs1);
+                            if constexpr (HI) mma_bf16(o, h0v, h1v, h2v, h3v, bs0, bs1);
+                        }
+                        if constexpr (HT == 8 && PARTS == 3) {
+                            mma_bf16(o, l0, l1, l2, l3, bt0, bt1);
+                            if constexpr (HI) mma_bf16(o, h0v, h1v, h2v, h3v, bt0, bt1);
+                        }
                     }
                 }
             }
@@ -469,13 +473,13 @@ partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ par
 #pragma unroll
                 for (int g = 0; g < G; ++g) bsum[g][k] += __shfl_xor_sync(0xffffffffu, bsum[g][k], x);
             }
-            if constexpr (HT == 4) {
+            if constexpr (COLS) {
                 l_part[k] += __shfl_xor_sync(0xffffffffu, l_part[k], 2);
 #pragma unroll
                 for (int g = 0; g < G; ++g) bsum[g][k] += __shfl_xor_sync(0xffffffffu, bsum[g][k], 2);
             }
         }
-        if constexpr (HT == 4) {
+        if constexpr (COLS) {
 #pragma unroll
             for (int i = 0; i < MT; ++i)
 #pragma unroll
@@ -486,7 +490,7 @@ partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ par
         float* mm_ = mo + CWARPS * 8 * DH;                          // [CWARPS][8]
         float* ml = mm_ + CWARPS * 8;                               // [CWARPS][8]
         float* mb = ml + CWARPS * 8;                                // [CWARPS][8][G]
-        if (r == 0 && (HT == 8 || j < 2)) {
+        if (r == 0 && (!COLS || j < 2)) {
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
                 const int h = 2 * hp + k;
@@ -496,11 +500,11 @@ partial_kernel_tb(Problem P, float* __restrict__ part_o, float* __restrict__ par
                 for (int g = 0; g < G; ++g) mb[(warp * 8 + h) * G + g] = bsum[g][k];
             }
         }
-        if (HT == 8 || j < 2) {
+        if (!COLS || j < 2) {
 #pragma unroll
             for (int i = 0; i < MT; ++i) {
-                const int g = i / MTG, mm = i % MTG;
-                const int d = 64 * g + 8 * r + 2 * mm;    // row r; row r + 8 is d + 1
+                const int bb = i / MTB, mm = i % MTB;
+                const int d = BD * bb + VRUN * r + 2 * mm;    // row r; row r + 8 is d + 1
                 const int c0 = 2 * j, c1 = 2 * j + 1;
                 mo[(warp * 8 + c0) * DH + d] = oacc[i][0];
                 mo[(warp * 8 + c1) * DH + d] = oacc[i][1];

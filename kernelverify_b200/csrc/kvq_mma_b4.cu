@@ -1,7 +1,7 @@
 // Register-fragment tensor-core partial kernels (fp16 steps, head_dim 128):
 // for 4-bit caches the transposed-score kernel (group 64) and the original
 // one (groups 32 and 128); for 2-, 3-, 6- and 8-bit caches the byte-code
-// kernel (group 64).
+// kernel (groups 32, 64, 128; at groups 32 and 128 in its 8-column head form).
 #include <atomic>
 
 #include "kvq_launch.h"
@@ -16,7 +16,7 @@ constexpr int kMaxDevices = 64;
 template <int HT, int GROUP, int PARTS, int BITS>
 constexpr auto mma4_kernel() {
     if constexpr (BITS != 4)
-        return mma4::partial_kernel_tb<HT, PARTS, BITS>;
+        return mma4::partial_kernel_tb<HT, PARTS, BITS, GROUP>;
     else if constexpr (GROUP == 64)
         return mma4::partial_kernel_t<HT, PARTS>;
     else
@@ -72,15 +72,25 @@ static int mma4_occupancy() {
     return n;
 }
 
+template <int BITS>
+static int byte_occupancy_w(int ht, int group) {
+    if (group == 64) return ht == 4 ? mma4_occupancy<4, 64, BITS>() : mma4_occupancy<8, 64, BITS>();
+    return group == 32 ? mma4_occupancy<8, 32, BITS>() : mma4_occupancy<8, 128, BITS>();
+}
+
+static int byte_occupancy(int ht, int group, int bits) {
+    switch (bits) {
+        case 2: return byte_occupancy_w<2>(ht, group);
+        case 3: return byte_occupancy_w<3>(ht, group);
+        case 6: return byte_occupancy_w<6>(ht, group);
+        default: return byte_occupancy_w<8>(ht, group);
+    }
+}
+
 int mma4_ctas_per_sm(int ht, int group, int bits) {
     int n = 0;
     if (bits != 4) {
-        switch (bits) {
-            case 2: n = ht == 4 ? mma4_occupancy<4, 64, 2>() : mma4_occupancy<8, 64, 2>(); break;
-            case 3: n = ht == 4 ? mma4_occupancy<4, 64, 3>() : mma4_occupancy<8, 64, 3>(); break;
-            case 6: n = ht == 4 ? mma4_occupancy<4, 64, 6>() : mma4_occupancy<8, 64, 6>(); break;
-            default: n = ht == 4 ? mma4_occupancy<4, 64, 8>() : mma4_occupancy<8, 64, 8>(); break;
-        }
+        n = byte_occupancy(ht, group, bits);
     } else if (ht == 4)
         n = group == 32 ? mma4_occupancy<4, 32, 4>() : group == 64 ? mma4_occupancy<4, 64, 4>() : mma4_occupancy<4, 128, 4>();
     else
@@ -111,20 +121,32 @@ int sm_count() {
     return n;
 }
 
+// The byte-code kernel: at group 64 in its (group, head)-column form for up
+// to 4 query heads per cache head; at groups 32 and 128 always in the
+// 8-head-column form (a head tile of 4 has the same single tile when at most
+// 4 query heads share a cache head, which is when the planner picks 4).
+template <int PARTS, int BITS>
+static cudaError_t launch_byte(const Problem& P, int ht, int group, float* o, float* m, float* l,
+                               cudaStream_t stream) {
+    if (group == 64)
+        return ht == 4 ? mma4_one<4, 64, PARTS, BITS>(P, o, m, l, stream)
+                       : mma4_one<8, 64, PARTS, BITS>(P, o, m, l, stream);
+    if (ht == 4 && P.r > 4) return cudaErrorInvalidValue;
+    if (group == 32) return mma4_one<8, 32, PARTS, BITS>(P, o, m, l, stream);
+    if (group == 128) return mma4_one<8, 128, PARTS, BITS>(P, o, m, l, stream);
+    return cudaErrorInvalidValue;
+}
+
 template <int PARTS>
 static cudaError_t launch_parts(const Problem& P, int ht, int group, int bits, float* o, float* m,
                                 float* l, cudaStream_t stream) {
     if (bits != 4) {
-        if (group != 64 || (ht != 4 && ht != 8)) return cudaErrorInvalidValue;
+        if (ht != 4 && ht != 8) return cudaErrorInvalidValue;
         switch (bits) {
-            case 2: return ht == 4 ? mma4_one<4, 64, PARTS, 2>(P, o, m, l, stream)
-                                   : mma4_one<8, 64, PARTS, 2>(P, o, m, l, stream);
-            case 3: return ht == 4 ? mma4_one<4, 64, PARTS, 3>(P, o, m, l, stream)
-                                   : mma4_one<8, 64, PARTS, 3>(P, o, m, l, stream);
-            case 6: return ht == 4 ? mma4_one<4, 64, PARTS, 6>(P, o, m, l, stream)
-                                   : mma4_one<8, 64, PARTS, 6>(P, o, m, l, stream);
-            case 8: return ht == 4 ? mma4_one<4, 64, PARTS, 8>(P, o, m, l, stream)
-                                   : mma4_one<8, 64, PARTS, 8>(P, o, m, l, stream);
+            case 2: return launch_byte<PARTS, 2>(P, ht, group, o, m, l, stream);
+            case 3: return launch_byte<PARTS, 3>(P, ht, group, o, m, l, stream);
+            case 6: return launch_byte<PARTS, 6>(P, ht, group, o, m, l, stream);
+            case 8: return launch_byte<PARTS, 8>(P, ht, group, o, m, l, stream);
         }
         return cudaErrorInvalidValue;
     }

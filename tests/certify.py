@@ -42,8 +42,14 @@ SEEDS = ("gate: np.random.default_rng(t + bits) per shape in make_case(), q and 
 
 
 def _kernel_for(bits, dh, r, t_stride) -> str:
-    tc = bits == 4 and dh == 128 and r <= 8 and t_stride % 8 == 0
-    return "tensor-core (mma.sync, register fragments)" if tc else "CUDA-core"
+    """The kernel the library plans for an fp16 case of this shape (see
+    kvq_plan_kernel): the register-fragment tensor-core kernels at head_dim
+    128, at most 8 query heads per cache head and 8-row-aligned geometry."""
+    tc = dh == 128 and r <= 8 and t_stride % 8 == 0
+    if not tc:
+        return "CUDA-core"
+    return ("tensor-core (mma.sync, register fragments)" if bits == 4 else
+            "tensor-core (mma.sync, byte codes)")
 
 
 def _evidence(label, verdict, out, kernel) -> C.CaseEvidence:

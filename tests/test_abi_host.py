@@ -170,17 +170,16 @@ def test_cache_append_rejects_bad_destinations(lib, over, needle):
 
 
 def test_plan_kernel_names_the_kernel_without_a_device(lib):
-    """Aligned fp16 DH-128 geometry with 4-bit codes at any group, or any
-    width at group 64, plans the tensor-core kernels; a t_stride that is not a
-    multiple of 8, other widths at groups 32/128, or more than 8 query heads
-    per cache head the CUDA-core one; invalid arguments a negative status."""
+    """Aligned fp16 DH-128 geometry plans the tensor-core kernels at every
+    width and group; a t_stride that is not a multiple of 8, head_dim 64, fp32
+    or more than 8 query heads per cache head the CUDA-core one; invalid
+    arguments a negative status."""
     TC, CC = _native.KVQ_KERNEL_TENSOR_CORE, _native.KVQ_KERNEL_CUDA_CORE
-    assert lib.kvq_plan_kernel(ctypes.byref(_args())) == TC
-    for bits in (2, 3, 6, 8):
-        assert lib.kvq_plan_kernel(ctypes.byref(_args(bits=bits))) == TC
-        assert lib.kvq_plan_kernel(ctypes.byref(_args(bits=bits, group_size=32))) == CC
-        assert lib.kvq_plan_kernel(ctypes.byref(_args(bits=bits, group_size=128))) == CC
-    assert lib.kvq_plan_kernel(ctypes.byref(_args(group_size=128))) == TC
+    for bits in (2, 3, 4, 6, 8):
+        for group in (32, 64, 128):
+            assert lib.kvq_plan_kernel(ctypes.byref(_args(bits=bits, group_size=group))) == TC
+    assert lib.kvq_plan_kernel(ctypes.byref(_args(head_dim=64))) == CC
+    assert lib.kvq_plan_kernel(ctypes.byref(_args(dtype=1))) == CC
     assert lib.kvq_plan_kernel(ctypes.byref(_args(t_stride=130))) == CC
     assert lib.kvq_plan_kernel(ctypes.byref(_args(n_heads=32, n_kv_heads=2))) == CC
     assert lib.kvq_plan_kernel(ctypes.byref(_args(bits=5))) == _native.KVQ_ERR_INVALID
