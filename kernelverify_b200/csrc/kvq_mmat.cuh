@@ -156,9 +156,11 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
                 if (lane == 0) mbar_arrive(&empty[slot]);
                 continue;
             }
-            // fp32 scales and biases of the block (see partial_kernel)
+            // fp32 scales and biases of the block (see partial_kernel); at 4
+            // heads a lane needs one position's, which it reads from the stage
+            // directly (below)
             float* scr = reinterpret_cast<float*>(smem + Lay::SCR + warp * Lay::SCR_WARP);
-            {
+            if constexpr (HT != 4) {
                 const __half* kss = reinterpret_cast<const __half*>(st + Lay::KS) + blk * 16 * G;
                 const __half* kbs = reinterpret_cast<const __half*>(st + Lay::KB) + blk * 16 * G;
                 const __half* vss = reinterpret_cast<const __half*>(st + Lay::VS) + blk * 16 * G;
@@ -202,6 +204,21 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
                     }
                 }
             }
+            // at 4 heads the V code words are read now, so their shared-memory
+            // latency hides behind the score epilogue and the softmax
+            uint32_t vwq[G][4];
+            if constexpr (HT == 4) {
+                const int p0h = blk * 16 + j;
+                const unsigned char* vrowh = st + Lay::VC;
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const int boff = g * (GROUP / 2) + r * VBYTES;
+                    vwq[g][0] = *reinterpret_cast<const uint32_t*>(vrowh + (p0h) * ROWB + boff);
+                    vwq[g][1] = *reinterpret_cast<const uint32_t*>(vrowh + (p0h + 4) * ROWB + boff);
+                    vwq[g][2] = *reinterpret_cast<const uint32_t*>(vrowh + (p0h + 8) * ROWB + boff);
+                    vwq[g][3] = *reinterpret_cast<const uint32_t*>(vrowh + (p0h + 12) * ROWB + boff);
+                }
+            }
             // score epilogue: sc[k] (HT = 4) is head 2hp+k at the lane's kept
             // row; sc[2rr + k] (HT = 8) head 2hp+k at row r + 8rr
             float sc[NSC];
@@ -215,11 +232,14 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
                 const float x00 = half ? r0 : acc[0][0], x01 = half ? r1 : acc[0][1];   // group 0
                 const float x10 = half ? acc[0][2] : r0, x11 = half ? acc[0][3] : r1;   // group 1
                 const int lp = kr0 + 8 * half;
-                float kf[2 * G];
-                load_f<2 * G>(kscr + lp * 2 * G, kf);
                 const bool live = blk * 16 + lp < nvalid;
-                const float a0 = fmaf(kf[0], x00, fmaf(kf[1], x10, fmaf(kf[2], qs[0][0], kf[3] * qs[1][0])));
-                const float a1 = fmaf(kf[0], x01, fmaf(kf[1], x11, fmaf(kf[2], qs[0][1], kf[3] * qs[1][1])));
+                // the position's k scales and biases straight from the stage (a
+                // dead position's may be any bits: its score is replaced below)
+                const int prow = blk * 16 + lp;
+                const float2 ks2 = __half22float2(*reinterpret_cast<const __half2*>(st + Lay::KS + prow * 2 * G));
+                const float2 kb2 = __half22float2(*reinterpret_cast<const __half2*>(st + Lay::KB + prow * 2 * G));
+                const float a0 = scale2 * fmaf(ks2.x, x00, fmaf(ks2.y, x10, fmaf(kb2.x, qs[0][0], kb2.y * qs[1][0])));
+                const float a1 = scale2 * fmaf(ks2.x, x01, fmaf(ks2.y, x11, fmaf(kb2.x, qs[0][1], kb2.y * qs[1][1])));
                 sc[0] = live ? a0 : -INFINITY;
                 sc[1] = live ? a1 : -INFINITY;
             } else {
@@ -282,7 +302,18 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
             if constexpr (HT == 4) {
                 const int lp = kr0 + 8 * half;
                 float vf[2 * G];
-                load_f<2 * G>(vscr + lp * 2 * G, vf);
+                {
+                    // v scales and biases - 128 v scales from the stage; zero at a
+                    // dead position, so its P' and bias term vanish
+                    const int prow = blk * 16 + lp;
+                    const bool vlive = prow < nvalid;
+                    float2 vs2 = __half22float2(*reinterpret_cast<const __half2*>(st + Lay::VS + prow * 2 * G));
+                    float2 vb2 = __half22float2(*reinterpret_cast<const __half2*>(st + Lay::VB + prow * 2 * G));
+                    vs2.x = vlive ? vs2.x : 0.0f; vs2.y = vlive ? vs2.y : 0.0f;
+                    vb2.x = vlive ? vb2.x : 0.0f; vb2.y = vlive ? vb2.y : 0.0f;
+                    vf[0] = vs2.x; vf[1] = vs2.y;
+                    vf[2] = fmaf(vs2.x, -128.0f, vb2.x); vf[3] = fmaf(vs2.y, -128.0f, vb2.y);
+                }
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
                     bsum[g][0] = fmaf(e[0], vf[G + g], bsum[g][0]);
@@ -347,10 +378,15 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 const int boff = g * (GROUP / 2) + r * VBYTES;
-                const uint32_t wA = *reinterpret_cast<const uint32_t*>(vrow + (p0) * ROWB + boff);
-                const uint32_t wB = *reinterpret_cast<const uint32_t*>(vrow + (p0 + 4) * ROWB + boff);
-                const uint32_t wC = *reinterpret_cast<const uint32_t*>(vrow + (p0 + 8) * ROWB + boff);
-                const uint32_t wD = *reinterpret_cast<const uint32_t*>(vrow + (p0 + 12) * ROWB + boff);
+                uint32_t wA, wB, wC, wD;
+                if constexpr (HT == 4) {
+                    wA = vwq[g][0]; wB = vwq[g][1]; wC = vwq[g][2]; wD = vwq[g][3];
+                } else {
+                    wA = *reinterpret_cast<const uint32_t*>(vrow + (p0) * ROWB + boff);
+                    wB = *reinterpret_cast<const uint32_t*>(vrow + (p0 + 4) * ROWB + boff);
+                    wC = *reinterpret_cast<const uint32_t*>(vrow + (p0 + 8) * ROWB + boff);
+                    wD = *reinterpret_cast<const uint32_t*>(vrow + (p0 + 12) * ROWB + boff);
+                }
                 uint32_t fa[MTG][4];
                 quad_bf16<0>(wA, wB, fa[0][0], fa[0][1], fa[1][0], fa[1][1]);
                 quad_bf16<0>(wC, wD, fa[0][2], fa[0][3], fa[1][2], fa[1][3]);
