@@ -415,12 +415,14 @@ def build(torch_module=None):
     return guarded
 
 
-def kernel_spec():
+def kernel_spec(ragged: bool = False):
     """The runner-door template (kernelverify/pack/kv_attention.py:292-352),
     for `kernelverify_b200.runners.CudaRunner`. `specialize()` fills `$T`,
     `$BITS`, `$DH` (and optionally `$GROUP`); the source names the library
     entry point and the instantiation it selects, the bindings keep the
-    reference's names and order."""
+    reference's names and order. ragged=True adds an int32 input `seq_lens`
+    [b_rows] after new_v: per-sequence logical lengths, each at most the
+    case's t_cached (one cache per sequence: params cache_batch_stride)."""
     from kernelverify_b200.runners import Binding, BindingKind, KernelSpec, LaunchSpec
 
     source = (
@@ -441,6 +443,7 @@ def kernel_spec():
                   Binding(BindingKind.INPUT, "v_biases"),
                   Binding(BindingKind.INPUT, "new_k"),
                   Binding(BindingKind.INPUT, "new_v"),
+                  *((Binding(BindingKind.INPUT, "seq_lens"),) if ragged else ()),
                   Binding(BindingKind.OUTPUT),
                   Binding(BindingKind.SCALAR, "n_heads", "uint32"),
                   Binding(BindingKind.SCALAR, "t_cached", "uint32"),

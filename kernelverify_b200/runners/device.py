@@ -347,13 +347,20 @@ class LibraryKernel(_Kernel):
             if have < nbytes:
                 raise LaunchError(f"input {name!r} holds {have} bytes; the case's geometry reads "
                                   f"{nbytes}")
+        seq_lens = None
+        if "seq_lens" in by_name:
+            buf, dt, shape = by_name["seq_lens"]
+            if dt != np.dtype(np.int32) or int(np.prod(shape)) < b_rows:
+                raise LaunchError(f"input 'seq_lens' must be int32 with at least b_rows={b_rows} "
+                                  f"entries")
+            seq_lens = buf
         obuf, odt, oshape = tensors[out_idx]
         if int(np.prod(oshape)) * odt.itemsize < b_rows * n_heads * dh * esz:
             raise LaunchError("the output is smaller than b_rows x n_heads x DH")
         a = _native.KvqArgs()
         for name in self.REQUIRED:
             setattr(a, name, by_name[name][0].data_ptr())
-        a.seq_lens = None
+        a.seq_lens = seq_lens.data_ptr() if seq_lens is not None else None
         a.b_rows, a.n_heads, a.n_kv_heads = b_rows, n_heads, n_kv
         a.t_cached, a.t_stride, a.head_dim = t_cached, t_stride, dh
         a.bits, a.group_size = bits, group

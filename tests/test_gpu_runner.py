@@ -183,3 +183,32 @@ def test_sequence_split_over_separate_shard_tensors(native):
                            torch.stack([p[2] for p in parts]), torch.float16).cpu().numpy()
     v = kv.verify_output(kv.gqa_tiled_inputs(q, kc, vc, nk, nv, 4), merged)
     assert v.ok, v
+
+
+def test_ragged_batch_through_the_runner(runner):
+    """The raw door's ragged form: one cache per sequence
+    (cache_batch_stride), per-sequence lengths in the int32 seq_lens input;
+    each sequence judged as its own case against the oracle."""
+    from kernelverify_b200.pack.kv_attention import kernel_spec
+    from tests.kvq_cases import judge_per_sequence, pack
+    rng = np.random.default_rng(61)
+    b, h, hkv, t_pad, dh, bits = 4, 16, 4, 640, 128, 8
+    lens = np.array([1, 300, 640, 77], dtype=np.int32)
+    q = (rng.standard_normal((b, h, dh)) * 0.6).astype(np.float16)
+    kc = rng.standard_normal((b, hkv, t_pad, dh)).astype(np.float16)
+    vc = rng.standard_normal((b, hkv, t_pad, dh)).astype(np.float16)
+    nk = rng.standard_normal((b, hkv, dh)).astype(np.float16)
+    nv = rng.standard_normal((b, hkv, dh)).astype(np.float16)
+    kw, ks, kb = pack(kc, bits)
+    vw, vs, vb = pack(vc, bits)
+    spec = specialize(kernel_spec(ragged=True), {"T": "half", "BITS": bits, "DH": dh})
+    case = RunCase(inputs={"q": q, "k_wq": kw, "k_scales": ks, "k_biases": kb, "v_wq": vw,
+                           "v_scales": vs, "v_biases": vb, "new_k": nk, "new_v": nv,
+                           "seq_lens": lens},
+                   params={"b_rows": b, "n_heads": h, "t_cached": t_pad, "n_kv_heads": hkv,
+                           "t_stride": t_pad, "cache_batch_stride": hkv * t_pad},
+                   output_shapes=[((b, h, dh), "float16")], label="ragged")
+    [[res]] = runner.run_candidate([(spec, [case])])
+    assert res.ok, (res.status, res.detail)
+    for v in judge_per_sequence(q, kc, vc, nk, nv, bits, res.outputs[0], lens):
+        assert v.ok, v

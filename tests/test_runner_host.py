@@ -151,3 +151,19 @@ def test_real_worker_without_a_gpu_reports_unsupported():
     r = CudaRunner(worker_env={"KVQ_FORCE_NO_GPU": "1"}, startup_timeout=120)
     [batch] = r.run_candidate([(spec(), [case()])])
     assert batch[0].status is RunStatus.UNSUPPORTED
+
+
+def test_ragged_kernel_spec_adds_seq_lens_after_new_v():
+    """The raw door keeps the reference's bindings in order; the ragged form
+    inserts one int32 input, seq_lens, before the output."""
+    from kernelverify_b200.pack.kv_attention import kernel_spec
+    from kernelverify_b200.runners import BindingKind, specialize
+    plain = specialize(kernel_spec(), {"T": "half", "BITS": 4, "DH": 128})
+    ragged = specialize(kernel_spec(ragged=True), {"T": "half", "BITS": 4, "DH": 128})
+    names = lambda spec: [b.name for b in spec.bindings if b.kind is BindingKind.INPUT]
+    assert names(plain) == ["q", "k_wq", "k_scales", "k_biases", "v_wq", "v_scales", "v_biases",
+                            "new_k", "new_v"]
+    assert names(ragged) == names(plain) + ["seq_lens"]
+    assert ragged.output_count() == plain.output_count() == 1
+    scalars = lambda spec: [b.name for b in spec.bindings if b.kind is BindingKind.SCALAR]
+    assert scalars(ragged) == scalars(plain) == ["n_heads", "t_cached", "n_kv_heads", "t_stride"]
