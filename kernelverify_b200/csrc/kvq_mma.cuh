@@ -65,8 +65,10 @@ struct Layout {
     static constexpr int STAGE = VB + TP * G * 2;         // bytes per stage
     static_assert(STAGE % 128 == 0, "stage size");
     // ring depth: 6- and 8-bit stages are 1.5-2x the bytes, so fewer of them
-    // keep three CTAs' rings on an SM with about the same bytes in flight
-    static constexpr int NST = BITS >= 6 ? (STAGES * 2 + 2) / 3 : STAGES;
+    // keep three CTAs' rings on an SM with about the same bytes in flight (8-bit
+    // at group 32, whose scale runs are the longest, one stage fewer again)
+    static constexpr int NST = BITS >= 6 ? (STAGES * 2 + 2) / 3 - (BITS == 8 && G == 4 ? 1 : 0)
+                                         : STAGES;
     static constexpr int RING = STAGE * NST;
     // per consumer warp: fp32 [16][G] k_scale, k_bias, v_scale, v_bias - 128 v_scale
     // of the warp's 16-position block
