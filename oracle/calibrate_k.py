@@ -57,6 +57,13 @@ Gates:
   G3 MEMBERSHIP: leave-one-member-out K_anchored per member is reported as a
      necessity diagnostic; it never fails the ensemble.
 
+Diagnostic (added after the decision, outside this rule: it informs and
+decides nothing). `device_form` emulates the arithmetic of the library's
+tensor-core kernels -- factored scores, a base-2 lazy online softmax over
+16-position blocks, the combine's weights as three (or, the fast precision,
+two) bf16 parts against codes offset by 128 -- and the report gives its
+largest K demand and err / tol per dtype.
+
 Decision. If G1 holds, K = 4.0 stands as calibrated, and the report also
 names the smallest grid K that is sound on all three draws and whether it
 keeps detection (if it does, 4.0 is loose by that factor and detection is
@@ -270,6 +277,91 @@ HELD_OUT = {
     "blocked-16": blocked16,
 }
 
+# ---------------------------------------------------------------------------
+# diagnostic, outside the pre-registered population: the arithmetic form of
+# the library's tensor-core kernels, emulated in numpy
+# ---------------------------------------------------------------------------
+def _bf16_trunc(x: np.ndarray) -> np.ndarray:
+    return (x.astype(np.float32).view(np.uint32) & np.uint32(0xFFFF0000)).view(np.float32)
+
+
+def _bf16_rn(x: np.ndarray) -> np.ndarray:
+    u = x.astype(np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def device_form(inputs, parts: int = 3, block: int = 16, slack: float = 8.0) -> np.ndarray:
+    """The tensor-core kernels' arithmetic (fp32 throughout, exact products):
+    per-group factored scores scaled by log2(e)/sqrt(DH) after the group sum,
+    a base-2 online softmax over blocks of 16 positions whose reference point
+    moves only past `slack`, the combine's weights P' = p * v_scale carried as
+    `parts` bf16 parts (truncations, the last rounded to nearest) against
+    codes offset by 128 with the offset taken out through the bias term, the
+    step's own entry merged at the end. The hardware's summation order inside
+    an MMA is not modelled."""
+    bits, g = int(inputs["bits"][0]), kv.group_of(inputs)
+    q = inputs["q"].astype(np.float32)
+    bsz, h, dh = q.shape
+    t = inputs["k_cache"].shape[1]
+    groups = dh // g
+
+    def art(cache):
+        codes, sc, bi = canonical_quantize(cache.reshape(h * t, dh), bits, g)
+        return (codes.astype(np.float32).reshape(h, t, groups, g),
+                sc.astype(np.float32).reshape(h, t, groups),
+                bi.astype(np.float32).reshape(h, t, groups))
+
+    kc, ks, kb = art(inputs["k_cache"])
+    vc, vs, vb = art(inputs["v_cache"])
+    scale2 = np.float32(1.0 / math.sqrt(float(dh)) * 1.4426950408889634)
+    qg = q.reshape(bsz, h, groups, g)
+    x = np.einsum("bhgi,htgi->bhtg", qg, kc).astype(np.float32)
+    qs = qg.sum(axis=-1, dtype=np.float32)
+    s = ((x * ks[None] + qs[:, :, None, :] * kb[None]).sum(axis=-1, dtype=np.float32)
+         * scale2).astype(np.float32)
+    vb_fold = (vb - np.float32(128.0) * vs).astype(np.float32)       # bias - 128 scale
+    codes_v = (vc + np.float32(128.0)).astype(np.float32)             # exact bf16 128 + c
+    m = np.full((bsz, h), -np.inf, np.float32)
+    lsum = np.zeros((bsz, h), np.float32)
+    o = np.zeros((bsz, h, dh), np.float32)
+    for t0 in range(0, t, block):
+        sb = s[:, :, t0:t0 + block]
+        bm = sb.max(axis=-1)
+        move = bm > m + np.float32(slack)
+        new_m = np.where(move, bm, m).astype(np.float32)
+        alpha = np.where(np.isinf(m), np.float32(0.0), np.exp2(m - new_m)).astype(np.float32)
+        o = (o * alpha[..., None]).astype(np.float32)
+        lsum = (lsum * alpha).astype(np.float32)
+        m = new_m
+        e = np.exp2(sb - m[..., None]).astype(np.float32)               # [B, H, tb]
+        lsum = (lsum + e.sum(axis=-1, dtype=np.float32)).astype(np.float32)
+        p_v = (e[..., None] * vs[None, :, t0:t0 + block]).astype(np.float32)   # [B, H, tb, G]
+        rest, pieces = p_v, []
+        for k in range(parts):
+            piece = _bf16_rn(rest) if k == parts - 1 else _bf16_trunc(rest)
+            pieces.append(piece)
+            rest = (rest - piece).astype(np.float32)
+        cv = codes_v[:, t0:t0 + block]                                  # [H, tb, G, g]
+        for piece in pieces:
+            o = (o + np.einsum("bhtg,htgi->bhgi", piece, cv).reshape(bsz, h, dh)).astype(np.float32)
+        bias = np.einsum("bht,htg->bhg", e, vb_fold[:, t0:t0 + block]).astype(np.float32)
+        o = (o + np.repeat(bias, g, axis=-1)).astype(np.float32)
+    s_new = (np.sum(q * inputs["new_k"].astype(np.float32), axis=-1) * scale2).astype(np.float32)
+    mm = np.maximum(m, s_new)
+    w_old = np.where(np.isinf(m), np.float32(0.0), np.exp2(m - mm)).astype(np.float32)
+    w_new = np.exp2(s_new - mm).astype(np.float32)
+    o = (o * w_old[..., None] + w_new[..., None] * inputs["new_v"].astype(np.float32)).astype(np.float32)
+    lsum = (lsum * w_old + w_new).astype(np.float32)
+    return (o / lsum[..., None]).astype(inputs["q"].dtype)
+
+
+DIAGNOSTIC = {
+    "device-form-3-part": lambda x: device_form(x, 3),
+    "device-form-2-part": lambda x: device_form(x, 2),
+}
+
+
 # Evaluation classes of the held-out population: what changes the rounding
 # sequence, not merely its order. The membership repair promotes one member of
 # an offending class into the floor and scores the class's other members.
@@ -310,6 +402,7 @@ def measure(spec: Spec) -> dict:
     members = {name: kv.max_abs_error(kv.kv_member(x, **kw), ref)
                for name, kw in kv.KV_MEMBERS.items()}
     held = {name: kv.max_abs_error(fn(x), ref) for name, fn in HELD_OUT.items()}
+    diag = {name: kv.max_abs_error(fn(x), ref) for name, fn in DIAGNOSTIC.items()}
     fault_err = {}
     if spec.draw == "calibration" and spec.mode in battery.IID_MODES:
         for params in faults.KV_FAULTS:
@@ -318,7 +411,7 @@ def measure(spec: Spec) -> dict:
                 kv.max_abs_error(out, ref) if np.all(np.isfinite(out)) else math.inf)
     return {"draw": spec.draw, "dims": dict(spec.dims), "dtype": spec.dtype, "mode": spec.mode,
             "seed": spec.seed, "group": spec.group, "base": base, "members": members,
-            "held_out": held, "faults": fault_err}
+            "held_out": held, "diagnostic": diag, "faults": fault_err}
 
 
 def k_required(base: float, floor_e: float, floor_c: float) -> float:
@@ -446,6 +539,20 @@ def summarize(rows: list) -> dict:
         out["repair"] = {"offending_classes": offending, "promoted_to_floor": promoted,
                          "still_held_out_in_class": same_class, "k_required": rep,
                          "sound_at_shipped_K": all(v <= K_SHIPPED for v in rep.values())}
+    # diagnostic: the tensor-core arithmetic form, per dtype (outside the
+    # rule: it informs, it decides nothing)
+    diag = {}
+    for r in rows:
+        fe = max(r["members"].values())
+        tol = max(r["base"], K_SHIPPED * fe)
+        for name, err in r.get("diagnostic", {}).items():
+            d = diag.setdefault(name, {}).setdefault(r["dtype"], {"k_required": 0.0,
+                                                                   "err_over_tol": 0.0,
+                                                                   "cases": 0})
+            d["k_required"] = max(d["k_required"], k_required(r["base"], fe, err))
+            d["err_over_tol"] = max(d["err_over_tol"], err / tol if tol > 0 else math.inf)
+            d["cases"] += 1
+    out["diagnostic"] = diag
     # decision
     need = max(out["k_required"].values())
     sound_grid = [k for k in K_GRID if k >= need]
@@ -516,6 +623,16 @@ def render(summary: dict) -> str:
                   "- largest K required after the repair: " + ", ".join(
                       f"{d} {k:.3g}" for d, k in rep["k_required"].items()),
                   f"- sound at the shipped K: {rep['sound_at_shipped_K']}"]
+    if summary.get("diagnostic"):
+        lines += ["", "Diagnostic, outside the pre-registered population: the arithmetic form of",
+                  "the library's tensor-core kernels, emulated in numpy (`device_form`; the",
+                  "kernels serve fp16 steps only, fp32 rows are for information):", "",
+                  "| form | dtype | cases | largest K required | largest err / tol at the shipped K |",
+                  "|---|---|---|---|---|"]
+        for name, by_dt in summary["diagnostic"].items():
+            for dt, d in sorted(by_dt.items()):
+                lines.append(f"| {name} | {dt} | {d['cases']} | {d['k_required']:.3g} | "
+                             f"{d['err_over_tol']:.3g} |")
     lines += ["", "Leave-one-member-out largest K required (calibration draw):", ""]
     for m, k in summary["G3_leave_one_member_out"].items():
         lines.append(f"- `{m}`: {k:.3g}")

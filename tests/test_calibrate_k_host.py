@@ -69,3 +69,17 @@ def test_a_wrong_implementation_is_exhibited(monkeypatch):
     summary = ck.summarize([ck.measure(s) for s in specs])
     assert summary["k_required_by_impl"]["planted-fp16-scores"] > ck.K_SHIPPED
     assert not summary["G1_sound_at_shipped_K"]
+
+
+def test_device_form_fits_fp16_steps_only():
+    """The emulated tensor-core arithmetic sits well inside the tolerance of
+    fp16 steps (the only steps those kernels serve) in both precisions, and
+    outside it at fp32 -- why fp32 caches run the CUDA-core kernel."""
+    for bits, group in ((4, 64), (8, 64), (3, 32)):
+        x16 = _case(bits, "float16", group=group)
+        ref, tol = kv.reference_and_tolerance(x16, "float16")
+        for parts in (3, 2):
+            assert kv.max_abs_error(ck.device_form(x16, parts), ref) <= 0.5 * tol, (bits, parts)
+    x32 = _case(2, "float32", group=128)
+    ref, tol = kv.reference_and_tolerance(x32, "float32")
+    assert kv.max_abs_error(ck.device_form(x32, 3), ref) > tol
