@@ -76,9 +76,11 @@ def should_dispatch(t: int) -> bool:
 
 
 def launch_config(b: int, h: int, n_kv_heads: int | None = None, t: int = 0):
-    """(grid, block) of the partial kernel for B=b, H=h at length t, as the
-    library plans it: grid (T splits, cache heads x head tiles, b), 256
-    threads. Informational -- the library plans its own launch."""
+    """(grid, block) of the CUDA-core partial kernel for B=b, H=h at length
+    t: grid (T splits, cache heads x head tiles, b), 256 threads.
+    Informational only -- the library plans its own launch, and the
+    tensor-core kernels (`plan_kernel` names which one runs) size their T
+    splits by whole waves of resident CTAs instead."""
     hkv = n_kv_heads or h
     r = h // hkv
     ht = 1 if r == 1 else (4 if r <= 4 else 8)
@@ -88,6 +90,33 @@ def launch_config(b: int, h: int, n_kv_heads: int | None = None, t: int = 0):
     chunk = max(THREADS_PER_CTA, -(-chunk // THREADS_PER_CTA) * THREADS_PER_CTA)
     splits = max(1, -(-t // chunk)) if t else 1
     return (splits, hkv * tiles, b), (THREADS_PER_CTA, 1, 1)
+
+
+def _check_buffers(device, *entries) -> None:
+    """Tensors the library reads or writes through their raw addresses alone,
+    as (name, tensor, shape, dtype) entries: each must have exactly this
+    shape and dtype and be contiguous (all checked first), then live on
+    `device` -- or the kernel would index memory the tensor does not own."""
+    for name, ten, shape, dtype in entries:
+        if tuple(ten.shape) != tuple(shape):
+            raise ValueError(f"{name} has shape {tuple(ten.shape)}, expected {tuple(shape)}")
+        if ten.dtype != dtype:
+            raise ValueError(f"{name} is {ten.dtype}, expected {dtype}")
+        if not ten.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    torch = _torch()
+    device = torch.device(device)
+    if device.type == "cuda" and device.index is None and torch.cuda.is_available():
+        device = torch.device("cuda", torch.cuda.current_device())
+    for name, ten, _, _ in entries:
+        if not ten.is_cuda or ten.device != device:
+            raise ValueError(f"{name} must be a CUDA tensor on {device}")
+
+
+def _check_words(name, ten) -> None:
+    torch = _torch()
+    if ten.dtype not in (torch.int32, torch.uint32):
+        raise ValueError(f"{name}: packed words must be int32/uint32 tensors, got {ten.dtype}")
 
 
 def _args(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *, bits,
@@ -143,8 +172,7 @@ def _args(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *
         t_cached = t_stride
     require_capacity(int(t_cached), t_stride)
     if seq_lens is not None:
-        if seq_lens.dtype != torch.int32 or tuple(seq_lens.shape) != (b,) or not seq_lens.is_cuda:
-            raise ValueError("seq_lens must be a CUDA int32 tensor [B]")
+        _check_buffers(q.device, ("seq_lens", seq_lens, (b,), torch.int32))
     a = KvqArgs()
     a.q, a.k_wq, a.k_scales, a.k_biases = (q.data_ptr(), k_wq.data_ptr(), k_scales.data_ptr(),
                                            k_biases.data_ptr())
@@ -215,8 +243,8 @@ def decode(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, 
     lib = _native.lib()
     if out is None:
         out = torch.empty_like(q)
-    elif tuple(out.shape) != tuple(q.shape) or out.dtype != q.dtype or not out.is_contiguous():
-        raise ValueError("out must be a contiguous tensor shaped and typed like q")
+    else:
+        _check_buffers(q.device, ("out", out, q.shape, q.dtype))
     need = lib.kvq_workspace_bytes(a)
     buf, have = _workspace(q.device, need, workspace)
     s = stream if stream is not None else torch.cuda.current_stream(q.device)
@@ -242,6 +270,9 @@ def decode_partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k,
         part_m = torch.empty((b, h), dtype=torch.float32, device=q.device)
     if part_l is None:
         part_l = torch.empty((b, h), dtype=torch.float32, device=q.device)
+    _check_buffers(q.device, ("part_o", part_o, (b, h, dh), torch.float32),
+                   ("part_m", part_m, (b, h), torch.float32),
+                   ("part_l", part_l, (b, h), torch.float32))
     need = lib.kvq_workspace_bytes(a)
     buf, have = _workspace(q.device, need, workspace)
     s = stream if stream is not None else torch.cuda.current_stream(q.device)
@@ -256,10 +287,20 @@ def lse_merge(part_o, part_m, part_l, out_dtype, out=None, stream=None):
     """Merge stacked partials part_o [P, B, H, DH], part_m/part_l [P, B, H]
     into out [B, H, DH] (the sequence-split merge)."""
     torch = _torch()
+    if part_o.dim() != 4:
+        raise ValueError(f"part_o must be [P, B, H, DH], got {tuple(part_o.shape)}")
     n, b, h, dh = part_o.shape
+    dev = part_o.device
+    _dtype_code(out_dtype)
+    bufs = [("part_o", part_o, (n, b, h, dh), torch.float32),
+            ("part_m", part_m, (n, b, h), torch.float32),
+            ("part_l", part_l, (n, b, h), torch.float32)]
+    if out is not None:
+        bufs.append(("out", out, (b, h, dh), out_dtype))
+    _check_buffers(dev, *bufs)
     if out is None:
-        out = torch.empty((b, h, dh), dtype=out_dtype, device=part_o.device)
-    s = stream if stream is not None else torch.cuda.current_stream(part_o.device)
+        out = torch.empty((b, h, dh), dtype=out_dtype, device=dev)
+    s = stream if stream is not None else torch.cuda.current_stream(dev)
     lib = _native.lib()
     _native.check(lib.kvq_lse_merge(part_o.data_ptr(), part_m.data_ptr(), part_l.data_ptr(), n,
                                     b * h, dh, _dtype_code(out_dtype), out.data_ptr(),
@@ -294,8 +335,11 @@ def lse_merge_records(records, b_rows: int, n_heads: int, head_dim: int, out_dty
     if (records.dim() != 2 or records.shape[1] != record_floats(rows, head_dim)
             or records.dtype != torch.float32 or not records.is_contiguous()):
         raise ValueError(f"records must be contiguous fp32 [P, {record_floats(rows, head_dim)}]")
+    _dtype_code(out_dtype)
     if out is None:
         out = torch.empty((b_rows, n_heads, head_dim), dtype=out_dtype, device=records.device)
+    else:
+        _check_buffers(records.device, ("out", out, (b_rows, n_heads, head_dim), out_dtype))
     s = stream if stream is not None else torch.cuda.current_stream(records.device)
     _native.check(_native.lib().kvq_lse_merge_records(records.data_ptr(), records.shape[0], rows,
                                                       head_dim, _dtype_code(out_dtype),
@@ -340,6 +384,7 @@ def cache_append(w, words, scales, biases, bits: int, *, position: int = 0, posi
         raise ValueError(f"cache leads with {tuple(words.shape[:-2])}; w is [{b}, {hkv}, ...]")
     t_stride = words.shape[-2]
     groups = scales.shape[-1]
+    _check_words("words", words)
     if groups == 0 or dh % groups or words.shape[-1] * 32 != dh * bits:
         raise ValueError(f"cache rows do not hold {dh} codes of {bits} bits")
     for name, ten in (("words", words), ("scales", scales), ("biases", biases)):
@@ -369,8 +414,19 @@ def quantize_cache(cache, bits: int, group_size: int = 64):
 def dequant(words, scales, biases, bits: int, stream=None):
     """fp32 dequantized values of a packed artefact, same leading shape."""
     torch = _torch()
+    if (words.dim() < 1 or words.shape[-1] == 0 or bits not in SUPPORTED_BITS
+            or words.shape[-1] * 32 % bits):
+        raise ValueError(f"words {tuple(words.shape)} at {bits} bits is not a packed artefact")
+    _check_words("words", words)
     groups = scales.shape[-1]
     dh = words.shape[-1] * 32 // bits
+    if groups == 0 or dh % groups:
+        raise ValueError(f"scales carry {groups} groups per row, which does not divide {dh}")
+    _dtype_code(scales.dtype)
+    lead = tuple(words.shape[:-1])
+    _check_buffers(words.device, ("words", words, words.shape, words.dtype),
+                   ("scales", scales, lead + (groups,), scales.dtype),
+                   ("biases", biases, lead + (groups,), scales.dtype))
     rows = words.numel() // words.shape[-1]
     out = torch.empty(tuple(words.shape[:-1]) + (dh,), dtype=torch.float32, device=words.device)
     s = stream if stream is not None else torch.cuda.current_stream(words.device)

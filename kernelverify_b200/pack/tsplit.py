@@ -98,7 +98,9 @@ class PeerExchange:
         """All ranks' records of `parity` merged into out [rows, head_dim]."""
         import torch
         from kernelverify_b200 import _native
-        from kernelverify_b200.pack.kv_attention import _dtype_code
+        from kernelverify_b200.pack.kv_attention import _check_buffers, _dtype_code
+        _dtype_code(out.dtype)
+        _check_buffers(self.device, ("out", out, (self.rows, self.head_dim), out.dtype))
         s = stream if stream is not None else torch.cuda.current_stream(out.device)
         _native.check_peer(_native.lib().kvq_peer_merge(
             self._array, self.world, self.rank, parity, self.rows, self.head_dim,
