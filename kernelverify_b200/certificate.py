@@ -102,10 +102,16 @@ class CaseEvidence:
     tol: float
     output_sha256: str
     kernel: str             # which device kernel served the case
+    ref_max: float = 0.0    # max|fp64 reference| of the judged case (0: not recorded)
 
     @property
     def margin(self) -> float:
         return self.err / self.tol if self.tol > 0 else float("inf")
+
+    @property
+    def max_rel(self) -> float | None:
+        """max-abs error relative to max|ref|, when the magnitude was recorded."""
+        return self.err / self.ref_max if self.ref_max > 0 else None
 
 
 @dataclass
@@ -190,6 +196,8 @@ class Certificate:
                             "runs, so fingerprints and margins describe this run only",
                 "cases": [{"label": c.label, "kernel": c.kernel, "output_sha256": c.output_sha256,
                            "err": c.err, "tol": c.tol, "margin_err_over_tol": round(c.margin, 6),
+                           **({"ref_max_abs": c.ref_max, "max_rel_err": c.max_rel}
+                              if c.max_rel is not None else {}),
                            "passed": c.passed} for c in self.cases],
             },
         }

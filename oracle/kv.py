@@ -146,9 +146,16 @@ class Verdict:
     ok: bool
     err: float
     tol: float
+    ref_max: float = 0.0     # max|ref|: err / ref_max is the max-rel error
+
+    @property
+    def rel(self) -> float:
+        """max |candidate - ref| / max|ref| (0 when the reference is all zero)."""
+        return self.err / self.ref_max if self.ref_max > 0 else 0.0
 
     def __str__(self) -> str:
-        return f"err {self.err:9.3e}  tol {self.tol:9.3e}  {'pass' if self.ok else 'FAIL'}"
+        return (f"err {self.err:9.3e}  rel {self.rel:9.3e}  tol {self.tol:9.3e}  "
+                f"{'pass' if self.ok else 'FAIL'}")
 
 
 def kv_inputs(q, k_cache, v_cache, new_k, new_v, bits: int, group_size: int = 64) -> dict:
@@ -169,7 +176,8 @@ def reference_and_tolerance(inputs: dict, dtype: str = "float16"):
 def judge(candidate, ref: np.ndarray, tol: float) -> Verdict:
     """Max-abs error at fp64 against tol (kernelverify/pack/verify.py:108-111)."""
     err = max_abs_error(candidate, ref)
-    return Verdict(ok=err <= tol, err=err, tol=tol)
+    ref_max = float(np.max(np.abs(ref))) if np.size(ref) else 0.0
+    return Verdict(ok=err <= tol, err=err, tol=tol, ref_max=ref_max)
 
 
 def verify_output(inputs: dict, candidate, dtype: str = "float16") -> Verdict:

@@ -56,19 +56,19 @@ def _evidence(label, verdict, out, kernel) -> C.CaseEvidence:
     return C.CaseEvidence(label=label, passed=bool(verdict.ok), err=float(verdict.err),
                           tol=float(verdict.tol),
                           output_sha256=hashlib.sha256(np.ascontiguousarray(out).tobytes()).hexdigest(),
-                          kernel=kernel)
+                          kernel=kernel, ref_max=float(verdict.ref_max))
 
 
-def run_protocol(bits: int, dh: int) -> list:
-    evidence = []
+def protocol_cases(bits: int, dh: int):
+    """The protocol's cases in order: (label, kind, (q, k_cache, v_cache,
+    new_k, new_v), kernel); kind "shared" is one cache for the batch (judged
+    as one case), "per-sequence" one cache per sequence (judged per
+    sequence). Host-only: seeded numpy inputs."""
     for (b, h, t, d) in cases.VERIFY_SHAPES:
         if d != dh:
             continue
-        q, kc, vc, nk, nv = cases.make_case(b, h, t, d, seed=t + bits)
-        out = run_decode(q, kc, vc, nk, nv, bits)
-        v = judge_gqa(q, kc, vc, nk, nv, bits, out)
-        evidence.append(_evidence(f"gate B={b} H={h} T={t} DH={d} {bits}-bit", v, out,
-                                  _kernel_for(bits, d, 1, t)))
+        yield (f"gate B={b} H={h} T={t} DH={d} {bits}-bit", "shared",
+               cases.make_case(b, h, t, d, seed=t + bits), _kernel_for(bits, d, 1, t))
     # grouped queries, per-sequence caches
     rng = np.random.default_rng(9000 + bits)
     b, h, hkv, t = 2, 32, 8, 1024
@@ -77,18 +77,24 @@ def run_protocol(bits: int, dh: int) -> list:
     vc = rng.standard_normal((b, hkv, t, dh)).astype(np.float16)
     nk = rng.standard_normal((b, hkv, dh)).astype(np.float16)
     nv = rng.standard_normal((b, hkv, dh)).astype(np.float16)
-    out = run_decode(q, kc, vc, nk, nv, bits)
-    verdicts = judge_per_sequence(q, kc, vc, nk, nv, bits, out)
-    worst = max(verdicts, key=lambda v: v.err / v.tol)
-    evidence.append(_evidence(f"grouped B=2 H=32 HKV=8 T=1024 DH={dh} {bits}-bit per-sequence",
-                              type(worst)(all(v.ok for v in verdicts), worst.err, worst.tol), out,
-                              _kernel_for(bits, dh, 4, t)))
+    yield (f"grouped B=2 H=32 HKV=8 T=1024 DH={dh} {bits}-bit per-sequence", "per-sequence",
+           (q, kc, vc, nk, nv), _kernel_for(bits, dh, 4, t))
     # past the reference's capacity
-    q, kc, vc, nk, nv = cases.make_case(1, 4, 5000, dh, seed=7000 + bits)
-    out = run_decode(q, kc, vc, nk, nv, bits)
-    v = judge_gqa(q, kc, vc, nk, nv, bits, out)
-    evidence.append(_evidence(f"long B=1 H=4 T=5000 DH={dh} {bits}-bit", v, out,
-                              _kernel_for(bits, dh, 1, 5000)))
+    yield (f"long B=1 H=4 T=5000 DH={dh} {bits}-bit", "shared",
+           cases.make_case(1, 4, 5000, dh, seed=7000 + bits), _kernel_for(bits, dh, 1, 5000))
+
+
+def run_protocol(bits: int, dh: int) -> list:
+    evidence = []
+    for label, kind, (q, kc, vc, nk, nv), kernel in protocol_cases(bits, dh):
+        out = run_decode(q, kc, vc, nk, nv, bits)
+        if kind == "shared":
+            v = judge_gqa(q, kc, vc, nk, nv, bits, out)
+        else:
+            verdicts = judge_per_sequence(q, kc, vc, nk, nv, bits, out)
+            worst = max(verdicts, key=lambda x: x.err / x.tol)
+            v = type(worst)(all(x.ok for x in verdicts), worst.err, worst.tol, worst.ref_max)
+        evidence.append(_evidence(label, v, out, kernel))
     return evidence
 
 

@@ -67,3 +67,21 @@ def test_committed_certificates_are_complete_and_honest():
         assert {c["clause"] for c in doc["attestation"]["clauses"]} >= {"C1", "C4", "C5"}
         assert "B200" in doc["validity"]["binding_on"]["chip_generation"]
         assert (root / f"{name}.md").exists()
+
+
+def test_case_evidence_states_max_abs_and_max_rel():
+    """A case judged with its reference magnitude carries max-rel beside
+    max-abs in the advisory block; one without it carries max-abs only."""
+    cert = _cert(cases=[C.CaseEvidence("a", True, 6e-5, 6e-4, "00", "tensor-core", ref_max=0.15),
+                        C.CaseEvidence("b", True, 2e-5, 1e-3, "11", "CUDA-core")])
+    a, b = json.loads(cert.dumps())["advisory"]["cases"]
+    assert a["err"] == 6e-5 and abs(a["max_rel_err"] - 4e-4) < 1e-12 and a["ref_max_abs"] == 0.15
+    assert "max_rel_err" not in b
+
+
+def test_verdicts_carry_the_reference_magnitude():
+    import numpy as np
+    from oracle import kv
+    ref = np.array([[0.5, -2.0]])
+    v = kv.judge(ref + 1e-3, ref, 1e-2)
+    assert v.ok and v.ref_max == 2.0 and abs(v.rel - 5e-4) < 1e-12

@@ -20,5 +20,7 @@ def test_emit_two_specializations(native, tmp_path):
     assert doc["protocol_bound"]["all_passed"] and doc["protocol_bound"]["cases_run"] == 4
     assert "B200" in doc["validity"]["binding_on"]["chip_generation"]
     kernels = {c["kernel"] for c in doc["advisory"]["cases"]}
+    # max-abs and max-rel versus fp64 on fp16 outputs, both stated per case
+    assert all(0 < c["max_rel_err"] < 2.0 ** -11 for c in doc["advisory"]["cases"])
     assert any("tensor-core" in k for k in kernels)
     assert (tmp_path / "MANIFEST.md").exists()
