@@ -222,10 +222,16 @@ class Workspace:
 _default_ws: dict = {}
 
 
-def _workspace(device, nbytes, ws: Workspace | None):
+def _workspace(device, nbytes, ws: Workspace | None, stream):
+    """The scratch for one call on `stream`. Without a caller's workspace each
+    stream has its own default one, so calls in flight on different streams
+    never share partials; a buffer is allocated on the stream that uses it,
+    so the caching allocator orders its reuse after that stream's work."""
+    torch = _torch()
     if ws is None:
-        ws = _default_ws.setdefault((device.type, device.index), Workspace())
-    return ws.get(nbytes, device)
+        ws = _default_ws.setdefault((device.type, device.index, stream.cuda_stream), Workspace())
+    with torch.cuda.stream(stream):
+        return ws.get(nbytes, device)
 
 
 def decode(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *, bits,
@@ -246,8 +252,8 @@ def decode(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, 
     else:
         _check_buffers(q.device, ("out", out, q.shape, q.dtype))
     need = lib.kvq_workspace_bytes(a)
-    buf, have = _workspace(q.device, need, workspace)
     s = stream if stream is not None else torch.cuda.current_stream(q.device)
+    buf, have = _workspace(q.device, need, workspace, s)
     _native.check(lib.kvq_decode(a, out.data_ptr(), buf.data_ptr() if buf is not None else None,
                                  have, s.cuda_stream))
     return out
@@ -274,8 +280,8 @@ def decode_partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k,
                    ("part_m", part_m, (b, h), torch.float32),
                    ("part_l", part_l, (b, h), torch.float32))
     need = lib.kvq_workspace_bytes(a)
-    buf, have = _workspace(q.device, need, workspace)
     s = stream if stream is not None else torch.cuda.current_stream(q.device)
+    buf, have = _workspace(q.device, need, workspace, s)
     _native.check(lib.kvq_decode_partial(a, part_o.data_ptr(), part_m.data_ptr(),
                                          part_l.data_ptr(),
                                          buf.data_ptr() if buf is not None else None, have,
