@@ -210,12 +210,22 @@ class Workspace:
     def __init__(self):
         self._buf = None
 
-    def get(self, nbytes: int, device):
-        torch = _torch()
+    def get(self, nbytes: int, device, stream=None):
+        """(buffer, bytes) of at least `nbytes`; a new buffer is allocated on
+        `stream` (default: the current one), so the caching allocator orders
+        the old buffer's reuse after that stream's work."""
         if nbytes == 0:
             return None, 0
-        if self._buf is None or self._buf.numel() < nbytes or self._buf.device != device:
-            self._buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        buf = self._buf
+        if buf is None or buf.numel() < nbytes or buf.device != device:
+            torch = _torch()
+            self._buf = None
+            if stream is None:
+                self._buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            else:
+                with torch.cuda.stream(stream):
+                    self._buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8,
+                                            device=device)
         return self._buf, self._buf.numel()
 
 
@@ -225,13 +235,13 @@ _default_ws: dict = {}
 def _workspace(device, nbytes, ws: Workspace | None, stream):
     """The scratch for one call on `stream`. Without a caller's workspace each
     stream has its own default one, so calls in flight on different streams
-    never share partials; a buffer is allocated on the stream that uses it,
-    so the caching allocator orders its reuse after that stream's work."""
-    torch = _torch()
+    never share partials; a buffer is allocated on the stream that uses it."""
     if ws is None:
-        ws = _default_ws.setdefault((device.type, device.index, stream.cuda_stream), Workspace())
-    with torch.cuda.stream(stream):
-        return ws.get(nbytes, device)
+        key = (device.type, device.index, stream.cuda_stream)
+        ws = _default_ws.get(key)
+        if ws is None:
+            ws = _default_ws[key] = Workspace()
+    return ws.get(nbytes, device, stream)
 
 
 def decode(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *, bits,
