@@ -31,6 +31,8 @@ def main():
     if "--probe" in sys.argv:
         emit({"event": "done"})
         return
+    if "--stream" in sys.argv:
+        return stream()
     req = json.loads(sys.stdin.read())
     for s, entry in enumerate(req["specs"]):
         spec = KernelSpec.from_json(entry["spec"])
@@ -54,6 +56,42 @@ def main():
             emit({"event": "case", "spec": s, "index": i, "result": RunResult(
                 status=RunStatus.OK, outputs=outs, timing=Timing((1e-6,), (2e-6,), 1),
                 label=case.label).to_json()})
+    emit({"event": "done"})
+
+
+# stream mode: the spec's name sets the timings -- "slow" twice "fast"'s, and
+# "noisy" spreads 2x on every second dispatch; case labels "hang" and "crash"
+# behave as in batch mode, "fail" reports a launch error
+TIMES = {"fast": 1e-6, "slow": 2e-6, "noisy": 1e-6}
+
+
+def stream():
+    header = json.loads(sys.stdin.readline())
+    spec = KernelSpec.from_json(header["spec"])
+    if spec.name == "die-compiling":
+        os._exit(5)
+    emit({"event": "compiled", "spec": 0, "compile_options": {"math_mode": header["math_mode"]}})
+    base = TIMES.get(spec.name, 1e-6)
+    dispatches = 0
+    for line in sys.stdin:
+        msg = json.loads(line)
+        if msg.get("end"):
+            break
+        case = RunCase.from_json(msg["case"])
+        if case.label == "hang":
+            time.sleep(60)
+        if case.label == "crash":
+            os._exit(7)
+        dispatches += 1
+        if case.label == "fail":
+            result = RunResult(status=RunStatus.LAUNCH_ERROR, detail="launch failed",
+                               label=case.label)
+        else:
+            spread = 2.0 if spec.name == "noisy" and dispatches % 2 == 0 else 1.05
+            result = RunResult(status=RunStatus.OK, outputs=[],
+                               timing=Timing((base, base * spread, base), (base,), 1),
+                               label=case.label)
+        emit({"event": "case", "spec": 0, "index": msg["index"], "result": result.to_json()})
     emit({"event": "done"})
 
 

@@ -212,3 +212,30 @@ def test_ragged_batch_through_the_runner(runner):
     assert res.ok, (res.status, res.detail)
     for v in judge_per_sequence(q, kc, vc, nk, nv, bits, res.outputs[0], lens):
         assert v.ok, v
+
+
+def test_interleaved_compare_of_a_kernel_with_itself(runner):
+    """Two live stream-mode workers on one B200, the same library
+    specialisation in both arms: every round completes and each accepted
+    round's speedup sits near 1 (the comparison's ok depends on device
+    noise, so it is reported, not asserted)."""
+    from kernelverify_b200.pack.kv_attention import kernel_spec
+    from kernelverify_b200.runners.compare import compare
+    spec = specialize(kernel_spec(), {"T": "half", "BITS": 4, "DH": 128})
+    b, h, hkv, t, dh = 4, 32, 8, 4096, 128
+    q, kc, vc, nk, nv = cases.make_case(b, h, t, dh, seed=3)
+    kc, vc, nk, nv = kc[:hkv], vc[:hkv], nk[:, :hkv], nv[:, :hkv]
+    kw, ks, kb = quant.quantize_cache(kc, 4)
+    vw, vs, vb = quant.quantize_cache(vc, 4)
+    case = RunCase(inputs={"q": q, "k_wq": kw, "k_scales": ks, "k_biases": kb, "v_wq": vw,
+                           "v_scales": vs, "v_biases": vb, "new_k": nk, "new_v": nv},
+                   params={"b_rows": b, "n_heads": h, "t_cached": t, "n_kv_heads": hkv,
+                           "t_stride": t},
+                   output_shapes=[((b, h, dh), "float16")], label="gqa-4")
+    rep = compare(spec, spec, [case], rounds=3, repeats=5, runner=runner)
+    assert not rep.failure, rep.failure
+    samples = rep.cases[0].samples
+    assert len(samples) == 3 and all(s.ref_best > 0 and s.cand_best > 0 for s in samples)
+    for s in rep.cases[0].accepted:
+        assert 0.5 < s.speedup < 2.0, rep.summary()
+    print(rep.summary())
