@@ -336,8 +336,6 @@ def run_ours(args) -> dict | None:
             decoder.step(q, kw, ks, kb, vw, vs, vb, nk, nv, bits=cfg["bits"], t_local=t_rows,
                          out=out)
 
-    # kernels of ours per step: partial + merge (config 2); partial, its local
-    # merge when split, and the cross-rank merge (config 5)
     # our kernels per step: the split stage and the merge of its splits;
     # config 5 adds the merge of the ranks' records
     launches_per_step = 2 + (1 if args.config == 5 else 0)
@@ -482,7 +480,7 @@ def run_ours(args) -> dict | None:
                    "l2": f"inputs larger than L2: {n_sets} cache sets of {local_kv / 1e6:.1f} MB rotated",
                    "kv_bytes_per_step": step_kv,
                    "parallelism": f"dp{world}" if args.config == 2 else f"tsplit{world}-{args.transport}"},
-        "hbm_frac_step": round(value / world / peak, 4) if args.config == 2 else round(value / world / peak, 4),
+        "hbm_frac_step": round(value / world / peak, 4),   # per GPU, of the measured peak
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "peak_kind": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
