@@ -8,7 +8,6 @@ finiteness checks) on every case, fp16 and fp32, every input mode
 
 from __future__ import annotations
 
-import numpy as np
 import pytest
 
 from oracle import battery, kv

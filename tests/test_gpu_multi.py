@@ -8,7 +8,6 @@ from __future__ import annotations
 import os
 import socket
 
-import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu

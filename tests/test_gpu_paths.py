@@ -13,7 +13,7 @@ import os
 import numpy as np
 import pytest
 
-from oracle import cases, kv
+from oracle import cases
 from tests.kvq_cases import judge_gqa, judge_per_sequence, pack, run_decode, to_dev
 
 pytestmark = pytest.mark.gpu

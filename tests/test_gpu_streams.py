@@ -5,7 +5,6 @@ what each returns alone."""
 
 from __future__ import annotations
 
-import numpy as np
 import pytest
 
 from oracle import cases
