@@ -4,9 +4,9 @@ reference's recorded battery verdicts -- the control passes, each of the
 seven faults is detected exactly where the reference's numpy port is -- so a
 machine without a GPU checks the source's arithmetic. No device call is made.
 
-A stride through the 400 cases keeps the CPU suite to seconds; the GPU test
-walks all 400 on the device (the host build reproduces all 400 x 8 verdicts
-as well: 176/259/259/132/372/339/366 detections, every control passing)."""
+A stride through the 400 cases checks in-process; one test walks all 400 x 8
+verdicts over a spawned pool (176/259/259/132/372/339/366 detections, every
+control passing); the GPU test runs the device build against the host build."""
 
 from __future__ import annotations
 
@@ -73,3 +73,36 @@ def test_arguments_outside_the_seam_kernel_are_refused(over):
                                       a["n_heads"], a["n_kv_heads"], a["t_cached"],
                                       a["head_dim"], a["bits"], a["group"], ctypes.c_void_p())
     assert rc == -1
+
+
+def _case_verdicts(index: int):
+    """(control verdict, {fault: detected}) of the seam source's host build on
+    one battery case (run in a spawned worker)."""
+    case = battery.case_space()[index]
+    inputs = battery.case_inputs(case)
+    ref = kv.kv_reference(inputs)
+    tol = kv.kv_tolerance(case.dtype, inputs, ref)
+    control = battery.corpus_oracle_passes(seams.run_host(inputs, {}), ref, tol)
+    detected = {faults.fault_name(p): not battery.corpus_oracle_passes(seams.run_host(inputs, p),
+                                                                       ref, tol)
+                for p in faults.KV_FAULTS}
+    return index, control, detected
+
+
+def test_host_build_reproduces_every_recorded_verdict(bg):
+    """All 400 cases x (control + 7 faults), spread over the host's cores:
+    every verdict equals the reference's recorded one, so the detection
+    counts are 176/259/259/132/372/339/366 of 400."""
+    import multiprocessing as mp
+    import os
+    seams.build()
+    with mp.get_context("spawn").Pool(min(8, os.cpu_count() or 1)) as pool:
+        rows = pool.map(_case_verdicts, range(400), chunksize=10)
+    counts = {name: 0 for name in bg["counts"]}
+    for index, control, detected in rows:
+        rec = bg["cases"][index]
+        assert control == rec["control"], index
+        assert detected == rec["detected"], index
+        for name, d in detected.items():
+            counts[name] += d
+    assert counts == bg["counts"]
