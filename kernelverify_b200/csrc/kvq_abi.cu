@@ -73,17 +73,21 @@ size_t align_up(size_t n) { return (n + kAlign - 1) / kAlign * kAlign; }
 constexpr uint64_t kTargetCtas = 148 * 4 * 2;
 constexpr uint32_t kMaxSplits = 4096;
 
-enum KernelKind { KERNEL_GENERIC = 0, KERNEL_MMA4 = 1, KERNEL_UMMA4 = 2 };
+enum KernelKind { KERNEL_GENERIC = 0, KERNEL_MMA4 = 1, KERNEL_UMMA4 = 2, KERNEL_TMEM4 = 3 };
 
-// KVQ_KERNEL=generic forces the CUDA-core kernel, KVQ_KERNEL=umma the tcgen05
-// kernel where it applies (fp16, 4-bit, head_dim 128, group 64); unset, each
-// call takes the fastest eligible kernel, the register-fragment tensor-core
-// kernel for the tensor-core formats (A/B checks of the paths use the switch).
+// KVQ_KERNEL=generic forces the CUDA-core kernel, KVQ_KERNEL=mma the
+// register-fragment tensor-core kernels, KVQ_KERNEL=umma the single-role
+// tcgen05 kernel, KVQ_KERNEL=tmem the warp-specialised tensor-memory kernel
+// (the last two where they apply: fp16, 4-bit, head_dim 128, group 64).
+// Unset, each call takes the fastest eligible kernel (A/B checks of the paths
+// use the switch).
 int kernel_override() {
     const char* v = getenv("KVQ_KERNEL");
     if (v == nullptr) return -1;
     if (strcmp(v, "generic") == 0) return KERNEL_GENERIC;
+    if (strcmp(v, "mma") == 0) return KERNEL_MMA4;
     if (strcmp(v, "umma") == 0) return KERNEL_UMMA4;
+    if (strcmp(v, "tmem") == 0) return KERNEL_TMEM4;
     return -1;
 }
 
@@ -134,10 +138,42 @@ void mma4_splits(uint64_t span, uint64_t units, int ctas_per_sm, uint32_t* chunk
     *splits_out = (uint32_t)best_splits;
 }
 
+// Split plan of the persistent tensor-memory kernel: one CTA per SM walks
+// work items of `chunk` positions (whole 128-position tiles), item i of a CTA
+// being its (blockIdx + i * grid)-th. Of the split counts, take the one whose
+// busiest CTA streams the fewest tiles (a small per-item cost breaks ties
+// toward fewer, longer items, which also keeps the merge short).
+void tmem4_splits(uint64_t span, uint64_t units, uint32_t* chunk_out, uint32_t* splits_out,
+                  uint32_t* grid_out) {
+    const uint64_t tile = (uint64_t)kvq::tmem4_tile_positions();
+    const uint64_t sms = (uint64_t)kvq::sm_count();
+    const uint64_t tiles = span ? (span + tile - 1) / tile : 1;
+    uint64_t best_chunk = tiles, best_splits = 1;
+    double best_cost = 1e300;
+    for (uint64_t s = 1; s <= tiles && s <= kMaxSplits; ++s) {
+        const uint64_t chunk = (tiles + s - 1) / s;
+        const uint64_t splits = (tiles + chunk - 1) / chunk;
+        if (splits != s) continue;
+        const uint64_t items = units * splits;
+        const uint64_t per_cta = (items + sms - 1) / sms;
+        const double cost = (double)per_cta * ((double)chunk + 0.25);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best_chunk = chunk;
+            best_splits = splits;
+        }
+    }
+    const uint64_t items = units * best_splits;
+    *chunk_out = (uint32_t)(best_chunk * tile);
+    *splits_out = (uint32_t)best_splits;
+    *grid_out = (uint32_t)(items < sms ? items : sms);
+}
+
 struct Plan {
     kvq::Problem P;
     int kernel;
     int ht;
+    uint32_t grid;      // persistent CTAs (tensor-memory kernel)
     uint32_t rows;      // b_rows * n_heads
     size_t part_bytes;  // one fp32 [n_splits, rows, DH] block
     size_t ml_bytes;    // one fp32 [n_splits, rows] block
@@ -185,10 +221,13 @@ int plan(const kvq_args* a, Plan* pl) {
                         a->cache_batch_stride % 8 == 0 && a->t_begin % 8 == 0;
     const bool tc = a->dtype == KVQ_F16 && a->head_dim == 128 && P.r <= 8 && tma_ok;
     const int forced = kernel_override();
+    const bool g64b4 = a->group_size == 64 && a->bits == 4;
     if (!tc || forced == KERNEL_GENERIC)
         pl->kernel = KERNEL_GENERIC;
-    else if (a->group_size == 64 && a->bits == 4 && forced == KERNEL_UMMA4)
+    else if (g64b4 && forced == KERNEL_UMMA4)
         pl->kernel = KERNEL_UMMA4;
+    else if (g64b4 && forced == KERNEL_TMEM4)
+        pl->kernel = KERNEL_TMEM4;
     else
         pl->kernel = KERNEL_MMA4;
     if (pl->kernel != KERNEL_GENERIC)
@@ -202,6 +241,13 @@ int plan(const kvq_args* a, Plan* pl) {
     const uint64_t span = end > a->t_begin ? end - a->t_begin : 0;
     const uint64_t units = (uint64_t)a->b_rows * a->n_kv_heads * P.head_tiles;
     pl->rows = a->b_rows * a->n_heads;
+    pl->grid = 0;
+    if (pl->kernel == KERNEL_TMEM4) {
+        tmem4_splits(span, units, &P.chunk, &P.n_splits, &pl->grid);
+        pl->part_bytes = align_up((size_t)P.n_splits * pl->rows * a->head_dim * sizeof(float));
+        pl->ml_bytes = align_up((size_t)P.n_splits * pl->rows * sizeof(float));
+        return KVQ_OK;
+    }
     if (pl->kernel != KERNEL_GENERIC) {
         if (pl->kernel == KERNEL_UMMA4)
             // 128-position tiles; the CTA's fixed work (TMEM, the q operand, the
@@ -232,6 +278,7 @@ int plan(const kvq_args* a, Plan* pl) {
 
 cudaError_t launch_partial_any(const Plan& pl, uint32_t bits, uint32_t dtype, uint32_t dh,
                                float* o, float* m, float* l, cudaStream_t s) {
+    if (pl.kernel == KERNEL_TMEM4) return kvq::launch_tmem4(pl.P, pl.ht, pl.grid, o, m, l, s);
     if (pl.kernel == KERNEL_UMMA4) return kvq::launch_umma4(pl.P, pl.ht, o, m, l, s);
     if (pl.kernel == KERNEL_MMA4)
         return kvq::launch_mma4(pl.P, pl.ht, pl.P.group_size, (int)bits, fast_precision() ? 2 : 3,
@@ -444,7 +491,8 @@ int kvq_plan_kernel(const kvq_args* a) {
     if (rc) return rc;
     switch (pl.kernel) {
         case KERNEL_MMA4: return KVQ_KERNEL_TENSOR_CORE;
-        case KERNEL_UMMA4: return KVQ_KERNEL_TCGEN05;
+        case KERNEL_UMMA4:
+        case KERNEL_TMEM4: return KVQ_KERNEL_TCGEN05;
         default: return KVQ_KERNEL_CUDA_CORE;
     }
 }

@@ -50,6 +50,14 @@ cudaError_t launch_umma4(const Problem& P, int ht, float* part_o, float* part_m,
                          cudaStream_t stream);
 int umma4_ctas_per_sm(int ht);
 
+// The warp-specialised tensor-memory kernel (fp16, 4-bit, head_dim 128,
+// group 64, ht in {4, 8}): `grid` persistent CTAs, one per SM at most, walk the
+// Problem's b_rows x n_kv_heads x head_tiles x n_splits work items.
+cudaError_t launch_tmem4(const Problem& P, int ht, uint32_t grid, float* part_o, float* part_m,
+                         float* part_l, cudaStream_t stream);
+// Positions per tile of that kernel (its split chunks are multiples of it).
+int tmem4_tile_positions();
+
 // Resident tensor-core CTAs per SM for (ht, group) on the current device,
 // and the device's SM count (both cached per device; fixed fallbacks when the
 // device cannot be queried).

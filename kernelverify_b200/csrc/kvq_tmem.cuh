@@ -1,0 +1,782 @@
+// Warp-specialised, persistent 5th-generation tensor-core decode kernel with
+// both MMA A operands in tensor memory, for fp16 steps over 4-bit caches,
+// head_dim 128, group 64, up to 8 query heads per cache head.
+//
+// One CTA per SM walks a list of work items -- (batch row, cache head, head
+// tile, T split), consecutive items of a CTA gridDim.x apart -- through one
+// continuous pipeline of 128-position tiles. Fourteen warps, four roles:
+//
+//   warp 0      producer: cp.async.bulk (1-D TMA) of each tile's K codes, V
+//               codes and the four fp16 scale/bias runs into an NST-deep
+//               ring, completion counted by mbarrier transaction bytes.
+//   warp 1      MMA issuer (one thread): per tile the score MMAs
+//                 S[pos, n] = sum_k Kc[pos, k] * Qg[k, n]      (A: TMEM, B: smem)
+//               and, one tile behind, the combine MMAs
+//                 O[d, n'] = sum_pos Vc[d, pos] * P'[pos, n']  (A: TMEM, B: smem)
+//               every one a tcgen05.mma kind::f16 with M = 128, committed
+//               to mbarriers that release the operands and signal results.
+//   warps 2-5   K unpack: each warp's 16-byte reads of the raw K rows (four
+//               lanes per row, conflict-free) become exact fp16 values
+//               1024 + code, stored into tensor memory with 16x256b stores so
+//               that TMEM lane = position, the score MMA's A layout. Also
+//               the per-item Qg operand (each head's q restricted to one
+//               quantisation group, n = group * 8 + head).
+//   warps 6-9   V unpack: ldmatrix.trans reads 8x8 tiles of 16-bit code
+//               pairs across positions; each register becomes exact bf16
+//               128 + code of one dim at two positions, stored into tensor
+//               memory so that TMEM lane = dim, the combine's A layout.
+//   warps 10-13 softmax: thread = position of the tile (TMEM lane). It reads
+//               its scores, applies the factored dequant
+//                 score[h] = sum_g ks_g (S_gh - 1024 Qsum_gh) + kb_g Qsum_gh,
+//               the lazy online softmax (the reference point moves only when a
+//               score exceeds it by 2^8, decided by a warpgroup vote), and
+//               writes P' = p * v_scale as three bf16 parts (binary32-class,
+//               |error| <= 2^-23 |P'|) into the shared-memory B operand; the
+//               V-side bias term sum_pos p (b - 128 s) is summed in
+//               registers. The same thread then owns one dim of O: it reads
+//               that row of each tile's O from tensor memory (fresh per tile)
+//               and accumulates it in registers with the tile's rescale.
+//
+// Every operand hand-off is an mbarrier with bounded waits; tensor memory
+// (512 columns) is allocated once per CTA and always freed. Precision: K-side
+// products fp16 x fp16 are exact, accumulated in fp32 (with the 1024 offset,
+// taken out per group through Qsum); V-side P' parts against exact bf16
+// codes; fp16 outputs.
+#pragma once
+
+#include "kvq_umma.cuh"
+
+namespace kvq {
+namespace tmem4 {
+
+using mma4::and_or;
+using mma4::bulk_g2s;
+using mma4::evict_first_policy;
+using mma4::ex2;
+using mma4::mbar_arrive;
+using mma4::mbar_expect_tx;
+using mma4::mbar_init;
+using mma4::mbar_wait;
+using mma4::named_sync;
+using mma4::s_addr;
+using mma4::split3;
+using umma::consumers_any;
+using umma::fence_async_smem;
+using umma::idesc;
+using umma::sdesc;
+using umma::tc_fence_after;
+using umma::tc_fence_before;
+using umma::tmem_alloc;
+using umma::tmem_dealloc;
+using umma::tmem_ld16;
+using umma::tmem_relinquish;
+using umma::tmem_wait_ld;
+using umma::tmem_wait_st;
+using umma::umma_commit;
+
+constexpr int TP = 128;                 // positions per tile
+constexpr int DH = 128;
+constexpr int G = 2;                    // quantisation groups of 64 per row
+constexpr int ROWB = DH / 2;            // code bytes per row
+#ifndef KVQ_TMEM_STAGES
+#define KVQ_TMEM_STAGES 6
+#endif
+constexpr int NST = KVQ_TMEM_STAGES;    // raw ring depth
+constexpr int WARPS = 14;
+constexpr int THREADS = 32 * WARPS;
+constexpr int W_PROD = 0, W_MMA = 1, W_K = 2, W_V = 6, W_S = 10;
+constexpr int SM_BAR = 1;               // named barrier of the softmax warpgroup
+constexpr uint32_t TMEM_COLS = 512;
+
+template <int HT>
+struct Cfg {
+    static_assert(HT == 4 || HT == 8, "head tile");
+    static constexpr int GW = HT == 4 ? 16 : 32;       // O columns per group: (part, head) + pad
+    static constexpr int N_O = G * GW;                 // combine N
+    static constexpr int N_S = 16;                     // score N: group * 8 + head
+    // tensor memory columns (lane = position for AK and S, lane = dim for AV and O)
+    static constexpr uint32_t AK0 = 0;                 // [2][64]
+    static constexpr uint32_t AV0 = 128;               // [2][64]
+    static constexpr uint32_t S0 = 256;                // [2][16]
+    static constexpr uint32_t O0 = 288;                // [2][N_O]
+    static_assert(O0 + 2 * N_O <= TMEM_COLS, "tensor memory");
+    // shared memory
+    static constexpr int KC = 0;                       // raw stage: K codes [TP][64]
+    static constexpr int VC = KC + TP * ROWB;          //            V codes [TP][64]
+    static constexpr int KS = VC + TP * ROWB;          //            fp16 [TP][G] each
+    static constexpr int KB = KS + TP * G * 2;
+    static constexpr int VS = KB + TP * G * 2;
+    static constexpr int VB = VS + TP * G * 2;
+    static constexpr int STAGE = VB + TP * G * 2;
+    static constexpr int BP = NST * STAGE;             // P' [2]: bf16, MN-major core matrices
+    static constexpr int BP_LBO = (N_O / 8) * 128;     // bytes between 8-position row blocks
+    static constexpr int BP_BYTES = TP * N_O * 2;
+    static constexpr int BQ = BP + 2 * BP_BYTES;       // Qg [2]: fp16, K-major core matrices
+    static constexpr int BQ_BYTES = N_S * DH * 2;
+    static constexpr int BAR = BQ + 2 * BQ_BYTES;
+    // raw_full[NST], raw_empty[NST], then [2] each of ak_full, ak_empty,
+    // av_full, av_empty, s_full, s_empty, p_full, p_empty, o_full, o_empty, and
+    // one drain barrier
+    static constexpr int NBAR = 2 * NST + 20 + 1;
+    static constexpr int MISC = BAR + NBAR * 8;
+    static constexpr int TMEM_SLOT = MISC;             // uint32 TMEM base address
+    static constexpr int ERR = MISC + 4;               // int, any role's failed wait
+    static constexpr int SERR = MISC + 8;              // int, the softmax warpgroup's own
+    static constexpr int RED = MISC + 16;              // fp32 reduction scratch
+    static constexpr int RED_FLOATS = 4 * HT * (1 + G + 1 + 1) + HT;
+    static constexpr int BYTES = RED + RED_FLOATS * 4 + 16;
+    static_assert(STAGE % 128 == 0 && BP % 1024 == 0 && BQ % 128 == 0, "alignment");
+};
+
+template <int HT>
+constexpr size_t smem_bytes() { return Cfg<HT>::BYTES; }
+
+// ---- PTX wrappers ------------------------------------------------------------
+// 16 TMEM lanes x 256 bits, 8 repetitions along the columns: thread t holds,
+// per repetition n, lane (t/4) columns 8n + 2(t%4) + {0, 1} in v[4n], v[4n+1]
+// and lane (t/4) + 8, the same columns, in v[4n+2], v[4n+3].
+__device__ __forceinline__ void tmem_st_16x256b_x8(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.16x256b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+        "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+          "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+          "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+          "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+}
+// D[tmem] (+)= A[tmem] * B[smem descriptor]; kind::f16, one CTA
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t id,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(id), "r"(accumulate)
+        : "memory");
+}
+// four 8x8 b16 tiles, transposed: lanes 8i..8i+7 give tile i's row addresses;
+// thread t receives element (row 2(t%4), column t/4) in the low half and
+// (row 2(t%4)+1, column t/4) in the high half of x[i]
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t saddr, uint32_t (&x)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3])
+                 : "r"(saddr));
+}
+// fp16x2 (1024 + 16c) -> (1024 + c), exact
+__device__ __forceinline__ uint32_t h2_hi_to_lo(uint32_t x) {
+    __half2 v = __hfma2(*reinterpret_cast<__half2*>(&x), __half2(__half(0.0625f), __half(0.0625f)),
+                        __half2(__half(960.0f), __half(960.0f)));
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// K index k of the score MMA (16 per K-step, 2 per TMEM column) <-> head dim,
+// as the K unpack places codes: word i of a lane's 16-byte chunk j holds dims
+// 32j + 8i .. +7; its register m (m = 0..3) holds dims (m, m + 4) and goes to
+// repetition n = 2i + m/2, column 8n + 2j + m%2.
+__device__ __forceinline__ int kdim(int k) {
+    const int n = k >> 4, j = (k >> 2) & 3, c = (k >> 1) & 1, hf = k & 1;
+    return 32 * j + 8 * (n >> 1) + 2 * (n & 1) + c + 4 * hf;
+}
+// K index of the combine MMA (positions, 2 per TMEM column) of tile position
+// p, as the V unpack places them: repetition n = p/16 holds positions
+// 16n + 8c + 2j + {0, 1} in column 8n + 2j + c.
+__device__ __forceinline__ int vkpos(int p) {
+    const int n = p >> 4, x = p & 15, c = x >> 3, j = (x & 7) >> 1, hf = x & 1;
+    return 16 * n + 4 * j + 2 * c + hf;
+}
+// head dim of combine row (TMEM lane) L: lane 32q + 8s + r holds dim 32q + 4r + s
+__device__ __forceinline__ int vdim(int L) { return (L & ~31) + 4 * (L & 7) + ((L & 31) >> 3); }
+
+struct Item {
+    uint32_t b, hk, split, lo, hi, h0;
+    int nh, n_tiles;
+    bool with_new;
+    uint64_t rowbase;
+};
+
+template <int HT>
+__device__ __forceinline__ Item item_of(const Problem& P, uint32_t idx) {
+    Item it;
+    it.split = idx % P.n_splits;
+    uint32_t unit = idx / P.n_splits;
+    const uint32_t tile_h = unit % P.head_tiles;
+    unit /= P.head_tiles;
+    it.hk = unit % P.n_kv_heads;
+    it.b = unit / P.n_kv_heads;
+    it.h0 = it.hk * P.r + tile_h * HT;
+    it.nh = min(HT, (int)(P.r - tile_h * HT));
+    uint32_t len = P.t_cached;
+    if (P.seq_lens != nullptr) len = min((uint32_t)max(P.seq_lens[it.b], 0), P.t_cached);
+    const uint32_t end = min(P.t_end, len);
+    it.lo = P.t_begin + it.split * P.chunk;
+    it.hi = min(end, it.lo + P.chunk);
+    it.n_tiles = it.hi > it.lo ? (int)((it.hi - it.lo + TP - 1) / TP) : 0;
+    it.with_new = P.has_new_entry && it.split == P.n_splits - 1;
+    it.rowbase = (uint64_t)it.b * P.cache_batch_stride + (uint64_t)it.hk * P.t_stride;
+    return it;
+}
+
+// -----------------------------------------------------------------------------
+template <int HT>
+__global__ void __launch_bounds__(THREADS, 1)
+decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __restrict__ part_m,
+              float* __restrict__ part_l) {
+    using C = Cfg<HT>;
+    constexpr float L2E = 1.4426950408889634f;
+    constexpr float LN2 = 0.6931471805599453f;
+    constexpr uint32_t ID_S = idesc(false, false, false, C::N_S, 128);
+    constexpr uint32_t ID_V = idesc(true, false, true, C::N_O, 128);
+    const float scale2 = P.scale * L2E;   // scores in log2 units
+
+    extern __shared__ __align__(1024) unsigned char smem[];
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::BAR);
+    uint64_t* raw_full = bar;
+    uint64_t* raw_empty = bar + NST;
+    uint64_t* ak_full = bar + 2 * NST;
+    uint64_t* ak_empty = ak_full + 2;
+    uint64_t* av_full = ak_full + 4;
+    uint64_t* av_empty = ak_full + 6;
+    uint64_t* s_full = ak_full + 8;
+    uint64_t* s_empty = ak_full + 10;
+    uint64_t* p_full = ak_full + 12;
+    uint64_t* p_empty = ak_full + 14;
+    uint64_t* o_full = ak_full + 16;
+    uint64_t* o_empty = ak_full + 18;
+    uint64_t* drain = ak_full + 20;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::TMEM_SLOT);
+    volatile int* err = reinterpret_cast<volatile int*>(smem + C::ERR);
+    volatile int* serr = reinterpret_cast<volatile int*>(smem + C::SERR);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    if (tid == 0) {
+        for (int s = 0; s < NST; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], 12);          // every unpack and softmax warp
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ak_full[b], 4);
+            mbar_init(&ak_empty[b], 1);
+            mbar_init(&av_full[b], 4);
+            mbar_init(&av_empty[b], 1);
+            mbar_init(&s_full[b], 1);
+            mbar_init(&s_empty[b], 4);
+            mbar_init(&p_full[b], 4);
+            mbar_init(&p_empty[b], 1);
+            mbar_init(&o_full[b], 1);
+            mbar_init(&o_empty[b], 4);
+        }
+        mbar_init(drain, 1);
+        *err = 0;
+        *serr = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == W_MMA) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    // P' columns past the (group, part, head) ones stay zero for the kernel's life
+    for (int i = tid; i < 2 * C::BP_BYTES / 16; i += THREADS)
+        reinterpret_cast<uint4*>(smem + C::BP)[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == W_PROD) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            const uint64_t pol = evict_first_policy();
+            const unsigned char* kw = reinterpret_cast<const unsigned char*>(P.k_wq);
+            const unsigned char* vw = reinterpret_cast<const unsigned char*>(P.v_wq);
+            const unsigned char* ks = static_cast<const unsigned char*>(P.k_scales);
+            const unsigned char* kb = static_cast<const unsigned char*>(P.k_biases);
+            const unsigned char* vs = static_cast<const unsigned char*>(P.v_scales);
+            const unsigned char* vb = static_cast<const unsigned char*>(P.v_biases);
+            uint32_t gt = 0;
+            for (uint32_t idx = blockIdx.x; idx < n_items && !*err; idx += gridDim.x) {
+                const Item it = item_of<HT>(P, idx);
+                for (int i = 0; i < it.n_tiles; ++i, ++gt) {
+                    const uint32_t slot = gt % NST, round = gt / NST;
+                    if (gt >= NST && !mbar_wait(&raw_empty[slot], (round - 1) & 1)) {
+                        *err = 1;
+                        break;
+                    }
+                    const uint32_t t0 = it.lo + i * TP;
+                    const uint32_t n = min((uint32_t)TP, it.hi - t0);
+                    const uint32_t nr = (n + 7) & ~7u;
+                    const uint64_t row = it.rowbase + t0;
+                    unsigned char* st = smem + slot * C::STAGE;
+                    mbar_expect_tx(&raw_full[slot], nr * (2 * ROWB + 4 * G * 2));
+                    bulk_g2s(st + C::KC, kw + row * ROWB, nr * ROWB, &raw_full[slot], pol);
+                    bulk_g2s(st + C::VC, vw + row * ROWB, nr * ROWB, &raw_full[slot], pol);
+                    bulk_g2s(st + C::KS, ks + row * G * 2, nr * G * 2, &raw_full[slot], pol);
+                    bulk_g2s(st + C::KB, kb + row * G * 2, nr * G * 2, &raw_full[slot], pol);
+                    bulk_g2s(st + C::VS, vs + row * G * 2, nr * G * 2, &raw_full[slot], pol);
+                    bulk_g2s(st + C::VB, vb + row * G * 2, nr * G * 2, &raw_full[slot], pol);
+                }
+            }
+            // copies still in flight land before the CTA retires: wait (bounded)
+            // for every slot's last issued fill
+            const uint32_t issued = gt;
+            for (uint32_t s = 0; s < NST && s < issued; ++s) {
+                const uint32_t last = ((issued - 1 - s) / NST) * NST + s;
+                (void)mbar_wait(&raw_full[s], (last / NST) & 1);
+            }
+        }
+    } else if (warp == W_MMA) {
+        // ------------------------------ MMA issuer ----------------------------
+        if (lane == 0) {
+            const uint32_t bq0 = s_addr(smem + C::BQ), bp0 = s_addr(smem + C::BP);
+            uint32_t gt = 0, ni = 0;
+            int prev = -1;
+            bool ok = true;
+            auto combine = [&](uint32_t g) -> bool {
+                const uint32_t b = g & 1, ph = (g >> 1) & 1;
+                if (!mbar_wait(&av_full[b], ph) || !mbar_wait(&p_full[b], ph)) return false;
+                if (g >= 2 && !mbar_wait(&o_empty[b], ph ^ 1)) return false;
+                tc_fence_after();
+#pragma unroll
+                for (int s = 0; s < TP / 16; ++s)
+                    umma_ts(tmem + C::O0 + C::N_O * b, tmem + C::AV0 + 64 * b + 8 * s,
+                            sdesc(bp0 + b * C::BP_BYTES + s * 2 * C::BP_LBO, C::BP_LBO, 128), ID_V,
+                            s > 0 ? 1u : 0u);
+                umma_commit(&o_full[b]);
+                umma_commit(&av_empty[b]);
+                umma_commit(&p_empty[b]);
+                return true;
+            };
+            for (uint32_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+                const Item it = item_of<HT>(P, idx);
+                if (it.n_tiles == 0) continue;
+                const uint32_t bq = bq0 + (ni & 1) * C::BQ_BYTES;
+                for (int i = 0; i < it.n_tiles; ++i, ++gt) {
+                    const uint32_t b = gt & 1, ph = (gt >> 1) & 1;
+                    if (!mbar_wait(&ak_full[b], ph) || (gt >= 2 && !mbar_wait(&s_empty[b], ph ^ 1))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int s = 0; s < DH / 16; ++s)
+                        umma_ts(tmem + C::S0 + 16 * b, tmem + C::AK0 + 64 * b + 8 * s,
+                                sdesc(bq + s * 256, 128, 2048), ID_S, s > 0 ? 1u : 0u);
+                    umma_commit(&s_full[b]);
+                    umma_commit(&ak_empty[b]);
+                    if (prev >= 0 && !combine((uint32_t)prev)) {
+                        ok = false;
+                        break;
+                    }
+                    prev = (int)gt;
+                }
+                ++ni;
+            }
+            if (ok && prev >= 0 && !combine((uint32_t)prev)) ok = false;
+            if (!ok) *err = 1;
+            // every MMA issued has completed before tensor memory is freed
+            umma_commit(drain);
+            (void)mbar_wait(drain, 0);
+        }
+    } else if (warp < W_V) {
+        // ------------------------------ K unpack ------------------------------
+        const int q = warp & 3, r = lane >> 2, j = lane & 3;
+        const int tq = (warp - W_K) * 32 + lane;               // 0..127
+        uint32_t gt = 0, ni = 0;
+        bool ok = true;
+        for (uint32_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+            const Item it = item_of<HT>(P, idx);
+            if (it.n_tiles == 0) continue;
+            for (int i = 0; i < it.n_tiles; ++i, ++gt) {
+                const uint32_t slot = gt % NST, b = gt & 1;
+                if (!mbar_wait(&raw_full[slot], (gt / NST) & 1) ||
+                    (gt >= 2 && !mbar_wait(&ak_empty[b], ((gt >> 1) & 1) ^ 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (i == 0) {
+                    // Qg of this item: column n = g * 8 + h holds q[h] on group
+                    // g's dims and zero elsewhere, K-major core matrices
+                    const __half* qrow = static_cast<const __half*>(P.q) + ((size_t)it.b * P.n_heads + it.h0) * DH;
+                    unsigned char* bq = smem + C::BQ + (ni & 1) * C::BQ_BYTES;
+#pragma unroll
+                    for (int c2 = 0; c2 < 2; ++c2) {
+                        const int ci = tq + 128 * c2;                // 256 chunks of 8 fp16
+                        const int n = ci >> 4, c = ci & 15;
+                        const int g = n >> 3, h = n & 7;
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 8; e += 2) {
+                            const int d0 = kdim(8 * c + e), d1 = kdim(8 * c + e + 1);
+                            const __half x0 = (h < it.nh && d0 / 64 == g) ? qrow[h * DH + d0] : __half(0.0f);
+                            const __half x1 = (h < it.nh && d1 / 64 == g) ? qrow[h * DH + d1] : __half(0.0f);
+                            __half2 v = __halves2half2(x0, x1);
+                            w[e / 2] = *reinterpret_cast<uint32_t*>(&v);
+                        }
+                        *reinterpret_cast<uint4*>(bq + (n % 8) * 16 + (n / 8) * 2048 + c * 128) =
+                            make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    fence_async_smem();
+                }
+                const unsigned char* st = smem + slot * C::STAGE + C::KC;
+                uint32_t ra[32], rb[32];
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t (&dst)[32] = half ? rb : ra;
+#pragma unroll
+                    for (int rr = 0; rr < 2; ++rr) {
+                        const int p = 32 * q + 16 * half + 8 * rr + r;
+                        const uint4 w4 = *reinterpret_cast<const uint4*>(st + p * ROWB + 16 * j);
+                        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                        for (int wi = 0; wi < 4; ++wi) {
+                            const uint32_t w = ws[wi];
+                            const uint32_t w8 = w >> 8;
+                            const uint32_t m0 = and_or<0x000F000Fu, 0x64006400u>(w);
+                            const uint32_t m1 = h2_hi_to_lo(and_or<0x00F000F0u, 0x64006400u>(w));
+                            const uint32_t m2 = and_or<0x000F000Fu, 0x64006400u>(w8);
+                            const uint32_t m3 = h2_hi_to_lo(and_or<0x00F000F0u, 0x64006400u>(w8));
+                            // register m -> repetition 2wi + m/2, column offset m%2
+                            dst[4 * (2 * wi) + 2 * rr + 0] = m0;
+                            dst[4 * (2 * wi) + 2 * rr + 1] = m1;
+                            dst[4 * (2 * wi + 1) + 2 * rr + 0] = m2;
+                            dst[4 * (2 * wi + 1) + 2 * rr + 1] = m3;
+                        }
+                    }
+                }
+                const uint32_t col = tmem + C::AK0 + 64 * b;
+                tmem_st_16x256b_x8(col + ((uint32_t)(32 * q) << 16), ra);
+                tmem_st_16x256b_x8(col + ((uint32_t)(32 * q + 16) << 16), rb);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&ak_full[b]);
+                    mbar_arrive(&raw_empty[slot]);
+                }
+            }
+            ++ni;
+        }
+        if (!ok) *err = 1;
+    } else if (warp < W_S) {
+        // ------------------------------ V unpack ------------------------------
+        const int q = warp & 3;
+        uint32_t gt = 0;
+        bool ok = true;
+        for (uint32_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+            const Item it = item_of<HT>(P, idx);
+            for (int i = 0; i < it.n_tiles; ++i, ++gt) {
+                const uint32_t slot = gt % NST, b = gt & 1;
+                if (!mbar_wait(&raw_full[slot], (gt / NST) & 1) ||
+                    (gt >= 2 && !mbar_wait(&av_empty[b], ((gt >> 1) & 1) ^ 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // lane L gives the row address of tile L/8: repetition pair
+                // member L/16, rows 8 (L/8 % 2) .. + 7, this warp's 16 bytes
+                const uint32_t vbase = s_addr(smem + slot * C::STAGE + C::VC) + 16 * q;
+                uint32_t ua[32], ub[32];
+#pragma unroll
+                for (int pr = 0; pr < 4; ++pr) {
+                    const int pos = 16 * (2 * pr + (lane >> 4)) + 8 * ((lane >> 3) & 1) + (lane & 7);
+                    uint32_t x[4];
+                    ldsm_x4_trans(vbase + pos * ROWB, x);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int n = 2 * pr + (k >> 1), hh = k & 1;
+                        ua[4 * n + hh] = and_or<0x000F000Fu, 0x43004300u>(x[k]);
+                        ua[4 * n + 2 + hh] = and_or<0x000F000Fu, 0x43004300u>(x[k] >> 4);
+                        ub[4 * n + hh] = and_or<0x000F000Fu, 0x43004300u>(x[k] >> 8);
+                        ub[4 * n + 2 + hh] = and_or<0x000F000Fu, 0x43004300u>(x[k] >> 12);
+                    }
+                }
+                const uint32_t col = tmem + C::AV0 + 64 * b;
+                tmem_st_16x256b_x8(col + ((uint32_t)(32 * q) << 16), ua);
+                tmem_st_16x256b_x8(col + ((uint32_t)(32 * q + 16) << 16), ub);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&av_full[b]);
+                    mbar_arrive(&raw_empty[slot]);
+                }
+            }
+        }
+        if (!ok) *err = 1;
+    } else {
+        // ------------------------------ softmax -------------------------------
+        const int q = warp & 3;
+        const int p = 32 * q + lane;             // tile position = TMEM lane (scores)
+        const int d = vdim(32 * q + lane);       // head dim = TMEM lane (O)
+        const int gq = q >> 1;                   // group of that dim
+        const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
+        const int kp = vkpos(p);                 // this position's row of P'
+        float* red = reinterpret_cast<float*>(smem + C::RED);
+        float* red_l = red;                      // [4][HT]
+        float* red_b = red_l + 4 * HT;           // [4][G][HT]
+        float* red_q = red_b + 4 * G * HT;       // [4][HT]
+        float* red_m = red_q + 4 * HT;           // [4][HT]
+        float* snew = red_m + 4 * HT;            // [HT]
+        const size_t rows = (size_t)P.b_rows * P.n_heads;
+        uint32_t gt = 0;
+        bool bad = false;
+
+        for (uint32_t idx = blockIdx.x; idx < n_items; idx += gridDim.x) {
+            const Item it = item_of<HT>(P, idx);
+            const __half* qrow = static_cast<const __half*>(P.q) + ((size_t)it.b * P.n_heads + it.h0) * DH;
+            // per-group q sums of the item's heads
+            float qs[G][HT];
+            {
+#pragma unroll
+                for (int h = 0; h < HT; ++h) {
+                    float v = h < it.nh ? __half2float(qrow[h * DH + 32 * q + lane]) : 0.0f;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (lane == 0) red_q[q * HT + h] = v;
+                }
+                named_sync(SM_BAR, 128);
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+#pragma unroll
+                    for (int h = 0; h < HT; ++h) qs[g][h] = red_q[(2 * g) * HT + h] + red_q[(2 * g + 1) * HT + h];
+            }
+            float m_run[HT], l_part[HT], bsum[G][HT], o[HT], alpha_prev[HT];
+#pragma unroll
+            for (int h = 0; h < HT; ++h) {
+                m_run[h] = -INFINITY;
+                l_part[h] = 0.0f;
+                o[h] = 0.0f;
+                alpha_prev[h] = 1.0f;
+#pragma unroll
+                for (int g = 0; g < G; ++g) bsum[g][h] = 0.0f;
+            }
+            // O of tile g2 (this thread's dim and group) into the registers
+            auto accumulate = [&](uint32_t g2) {
+                const uint32_t b = g2 & 1;
+                const uint32_t col = tmem + C::O0 + C::N_O * b + C::GW * gq + lane_addr;
+                if constexpr (HT == 4) {
+                    uint32_t v[16];
+                    tmem_ld16(col, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int h = 0; h < HT; ++h)
+                        o[h] = fmaf(o[h], alpha_prev[h],
+                                    __uint_as_float(v[h]) + __uint_as_float(v[HT + h]) +
+                                        __uint_as_float(v[2 * HT + h]));
+                } else {
+                    uint32_t v[32];
+                    tmem_ld32(col, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int h = 0; h < HT; ++h)
+                        o[h] = fmaf(o[h], alpha_prev[h],
+                                    __uint_as_float(v[h]) + __uint_as_float(v[HT + h]) +
+                                        __uint_as_float(v[2 * HT + h]));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&o_empty[b]);
+            };
+
+            for (int i = 0; i < it.n_tiles && !bad; ++i, ++gt) {
+                const uint32_t slot = gt % NST, b = gt & 1, ph = (gt >> 1) & 1;
+                // every wait of the tile first, then one warpgroup vote on the
+                // outcome (so every thread takes the same branches)
+                bool okw = mbar_wait(&raw_full[slot], (gt / NST) & 1) && mbar_wait(&s_full[b], ph);
+                if (gt >= 2) okw = okw && mbar_wait(&p_empty[b], ph ^ 1);
+                if (i > 0) okw = okw && mbar_wait(&o_full[(gt - 1) & 1], ((gt - 1) >> 1) & 1);
+                if (!okw) *serr = 1;
+                tc_fence_after();
+                if (i > 0) accumulate(gt - 1);
+
+                // scores of position p
+                uint32_t xs[16];
+                tmem_ld16(tmem + C::S0 + 16 * b + lane_addr, xs);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_empty[b]);
+                const unsigned char* st = smem + slot * C::STAGE;
+                const int nvalid = (int)min((uint32_t)TP, it.hi - (it.lo + i * TP));
+                const bool live = p < nvalid;
+                const float2 ks2 = __half22float2(*reinterpret_cast<const __half2*>(st + C::KS + p * 4));
+                const float2 kb2 = __half22float2(*reinterpret_cast<const __half2*>(st + C::KB + p * 4));
+                const float2 vs2 = __half22float2(*reinterpret_cast<const __half2*>(st + C::VS + p * 4));
+                const float2 vb2 = __half22float2(*reinterpret_cast<const __half2*>(st + C::VB + p * 4));
+                const float ksc[G] = {ks2.x * scale2, ks2.y * scale2};
+                const float cq[G] = {fmaf(ksc[0], -1024.0f, kb2.x * scale2), fmaf(ksc[1], -1024.0f, kb2.y * scale2)};
+                float sc[HT];
+                bool grow = false;
+#pragma unroll
+                for (int h = 0; h < HT; ++h) {
+                    float a = 0.0f;
+#pragma unroll
+                    for (int g = 0; g < G; ++g)
+                        a = fmaf(ksc[g], __uint_as_float(xs[8 * g + h]), fmaf(cq[g], qs[g][h], a));
+                    sc[h] = live ? a : -INFINITY;
+                    grow |= sc[h] > m_run[h] + 8.0f;
+                }
+                // the stage's fp16 data is consumed
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&raw_empty[slot]);
+
+                const bool any_grow = consumers_any(grow);   // also a barrier: serr is uniform after it
+                if (*serr) {
+                    bad = true;
+                    break;
+                }
+                float alpha[HT];
+#pragma unroll
+                for (int h = 0; h < HT; ++h) alpha[h] = 1.0f;
+                if (any_grow) {
+#pragma unroll
+                    for (int h = 0; h < HT; ++h) {
+                        float v = sc[h];
+#pragma unroll
+                        for (int o2 = 16; o2 > 0; o2 >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o2));
+                        if (lane == 0) red_m[q * HT + h] = v;
+                    }
+                    named_sync(SM_BAR, 128);
+#pragma unroll
+                    for (int h = 0; h < HT; ++h) {
+                        const float v = fmaxf(fmaxf(red_m[h], red_m[HT + h]), fmaxf(red_m[2 * HT + h], red_m[3 * HT + h]));
+                        const float m_new = v > m_run[h] + 8.0f ? v : m_run[h];
+                        alpha[h] = ex2(m_run[h] - m_new);    // 0 on the item's first tile
+                        m_run[h] = m_new;
+                        l_part[h] *= alpha[h];
+#pragma unroll
+                        for (int g = 0; g < G; ++g) bsum[g][h] *= alpha[h];
+                    }
+                    named_sync(SM_BAR, 128);                 // red_m is read by everyone
+                }
+                float e[HT];
+#pragma unroll
+                for (int h = 0; h < HT; ++h) {
+                    e[h] = live ? ex2(sc[h] - m_run[h]) : 0.0f;
+                    l_part[h] += e[h];
+                }
+                // P' = p * v_scale in three bf16 parts, row kp of this tile's B
+                // operand: chunk (g, part) of HT columns; v bias - 128 v_scale
+                const float vsf[G] = {live ? vs2.x : 0.0f, live ? vs2.y : 0.0f};
+                const float vbf[G] = {live ? fmaf(vs2.x, -128.0f, vb2.x) : 0.0f,
+                                      live ? fmaf(vs2.y, -128.0f, vb2.y) : 0.0f};
+                unsigned char* prow = smem + C::BP + b * C::BP_BYTES + (kp % 8) * 16 + (kp / 8) * C::BP_LBO;
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    uint32_t hi[HT / 2], mid[HT / 2], lo[HT / 2];
+#pragma unroll
+                    for (int h = 0; h < HT; h += 2) {
+                        bsum[g][h] = fmaf(e[h], vbf[g], bsum[g][h]);
+                        bsum[g][h + 1] = fmaf(e[h + 1], vbf[g], bsum[g][h + 1]);
+                        const float2 v = __fmul2_rn(make_float2(e[h], e[h + 1]), make_float2(vsf[g], vsf[g]));
+                        split3(v.x, v.y, hi[h / 2], mid[h / 2], lo[h / 2]);
+                    }
+                    if constexpr (HT == 4) {
+                        // columns 16g + (hi 0..3, mid 4..7 | lo 8..11, zero 12..15)
+                        *reinterpret_cast<uint4*>(prow + (2 * g) * 128) = make_uint4(hi[0], hi[1], mid[0], mid[1]);
+                        *reinterpret_cast<uint4*>(prow + (2 * g + 1) * 128) = make_uint4(lo[0], lo[1], 0u, 0u);
+                    } else {
+                        // columns 32g + (hi 0..7 | mid 8..15 | lo 16..23 | zero 24..31)
+                        *reinterpret_cast<uint4*>(prow + (4 * g) * 128) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4*>(prow + (4 * g + 1) * 128) = make_uint4(mid[0], mid[1], mid[2], mid[3]);
+                        *reinterpret_cast<uint4*>(prow + (4 * g + 2) * 128) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    }
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[b]);
+#pragma unroll
+                for (int h = 0; h < HT; ++h) alpha_prev[h] = alpha[h];
+            }
+            // the item's last O tile
+            if (!bad && it.n_tiles > 0) {
+                const uint32_t last = gt - 1;
+                const bool okw = mbar_wait(&o_full[last & 1], (last >> 1) & 1);
+                if (!okw) *serr = 1;
+                tc_fence_after();
+                accumulate(last);
+                named_sync(SM_BAR, 128);
+                if (*serr) bad = true;
+            }
+
+            // ---- the item's partial: l and bias sums over the warpgroup ------
+#pragma unroll
+            for (int h = 0; h < HT; ++h) {
+                float v = l_part[h];
+#pragma unroll
+                for (int o2 = 16; o2 > 0; o2 >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o2);
+                if (lane == 0) red_l[q * HT + h] = v;
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float u = bsum[g][h];
+#pragma unroll
+                    for (int o2 = 16; o2 > 0; o2 >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o2);
+                    if (lane == 0) red_b[(q * G + g) * HT + h] = u;
+                }
+            }
+            if (it.with_new && q == 0) {
+                const __half* nk = static_cast<const __half*>(P.new_k) + ((size_t)it.b * P.n_kv_heads + it.hk) * DH;
+                for (int h = 0; h < it.nh; ++h) {
+                    float part = 0.0f;
+                    for (int dd = lane; dd < DH; dd += 32)
+                        part = fmaf(__half2float(qrow[h * DH + dd]), __half2float(nk[dd]), part);
+                    part = warp_sum(part);
+                    if (lane == 0) snew[h] = part * scale2;
+                }
+            }
+            named_sync(SM_BAR, 128);
+            const __half* nv = static_cast<const __half*>(P.new_v) + ((size_t)it.b * P.n_kv_heads + it.hk) * DH;
+            const float nvd = it.with_new ? __half2float(nv[d]) : 0.0f;
+            const bool poison = bad;
+#pragma unroll
+            for (int h = 0; h < HT; ++h) {
+                if (h >= it.nh) break;
+                const float l = red_l[h] + red_l[HT + h] + red_l[2 * HT + h] + red_l[3 * HT + h];
+                const float bs = red_b[(0 * G + gq) * HT + h] + red_b[(1 * G + gq) * HT + h] +
+                                 red_b[(2 * G + gq) * HT + h] + red_b[(3 * G + gq) * HT + h];
+                float ov = o[h] + bs, lv = l, M = m_run[h];
+                if (it.with_new) {
+                    const float sn = snew[h];
+                    const float Mx = fmaxf(M, sn);
+                    const float er = M == -INFINITY ? 0.0f : ex2(M - Mx);
+                    const float en = ex2(sn - Mx);
+                    ov = fmaf(nvd, en, ov * er);
+                    lv = fmaf(lv, er, en);
+                    M = Mx;
+                }
+                const size_t row = it.split * rows + (size_t)it.b * P.n_heads + it.h0 + h;
+                part_o[row * DH + d] = poison ? __int_as_float(0x7fc00000) : ov;
+                if (d == 0) {
+                    part_m[row] = poison ? __int_as_float(0x7fc00000) : M * LN2;   // natural-log units
+                    part_l[row] = poison ? __int_as_float(0x7fc00000) : lv;
+                }
+            }
+            named_sync(SM_BAR, 128);   // the reduction scratch is free again
+        }
+        if (bad) *err = 1;
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == W_MMA) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+}  // namespace tmem4
+}  // namespace kvq

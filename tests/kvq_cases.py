@@ -55,3 +55,31 @@ def judge_per_sequence(q, k_caches, v_caches, new_k, new_v, bits, out, lens=None
                                   new_k[b:b + 1], new_v[b:b + 1], bits, out[b:b + 1], group,
                                   dtype))
     return verdicts
+
+
+def judge_unit(payload):
+    """Verdicts of one (sequence, cache head) unit from its raw fp16 rows: q
+    [r, DH] of the unit's query heads, k/v rows [T, DH], new_k/new_v [DH], and
+    one or more candidate outputs [r, DH] ({tag: out}) judged against one
+    reference and tolerance. A module-level function so a spawned process
+    pool can run it (the oracle is CPU numpy; the judged units are
+    independent)."""
+    label, q, k_rows, v_rows, new_k, new_v, bits, group, outs = payload
+    inputs = kv.gqa_tiled_inputs(q[None], k_rows[None], v_rows[None], new_k[None, None],
+                                 new_v[None, None], bits, group)
+    ref, tol = kv.reference_and_tolerance(inputs)
+    return [(f"{tag}{label}", kv.judge(out[None], ref, tol)) for tag, out in outs.items()]
+
+
+def judge_units(payloads, processes: int | None = None):
+    """[(label, Verdict)] of every unit and candidate, judged in a spawned
+    pool (never forked: the caller has a CUDA context)."""
+    import multiprocessing as mp
+    import os
+    n = max(1, min(len(payloads), processes or os.cpu_count() or 1))
+    if n == 1:
+        res = [judge_unit(p) for p in payloads]
+    else:
+        with mp.get_context("spawn").Pool(n) as pool:
+            res = pool.map(judge_unit, payloads, chunksize=1)
+    return [v for unit in res for v in unit]
