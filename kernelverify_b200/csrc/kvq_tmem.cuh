@@ -57,6 +57,7 @@ using mma4::mbar_arrive;
 using mma4::mbar_expect_tx;
 using mma4::mbar_init;
 using mma4::mbar_wait;
+using mma4::mbar_try_wait;
 using mma4::named_sync;
 using mma4::s_addr;
 using mma4::split3;
@@ -82,9 +83,9 @@ constexpr int ROWB = DH / 2;            // code bytes per row
 #define KVQ_TMEM_STAGES 6
 #endif
 constexpr int NST = KVQ_TMEM_STAGES;    // raw ring depth
-constexpr int WARPS = 14;
+constexpr int WARPS = 15;
 constexpr int THREADS = 32 * WARPS;
-constexpr int W_PROD = 0, W_MMA = 1, W_K = 2, W_V = 6, W_S = 10;
+constexpr int W_PROD = 0, W_MMA = 1, W_K = 2, W_V = 6, W_S = 10, W_MMA_C = 14;
 constexpr int SM_BAR = 1;               // named barrier of the softmax warpgroup
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -99,7 +100,10 @@ struct Cfg {
     static constexpr uint32_t AV0 = 128;               // [2][64]
     static constexpr uint32_t S0 = 256;                // [2][16]
     static constexpr uint32_t O0 = 288;                // [2][N_O]
-    static_assert(O0 + 2 * N_O <= TMEM_COLS, "tensor memory");
+    // [2][8]: a position's fp16x2 k_scale, k_bias, v_scale, v_bias (columns
+    // 0..3), written beside its K operand so the softmax reads them with its scores
+    static constexpr uint32_t SC0 = O0 + 2 * N_O;
+    static_assert(SC0 + 16 <= TMEM_COLS, "tensor memory");
     // shared memory
     static constexpr int KC = 0;                       // raw stage: K codes [TP][64]
     static constexpr int VC = KC + TP * ROWB;          //            V codes [TP][64]
@@ -114,14 +118,13 @@ struct Cfg {
     static constexpr int BQ = BP + 2 * BP_BYTES;       // Qg [2]: fp16, K-major core matrices
     static constexpr int BQ_BYTES = N_S * DH * 2;
     static constexpr int BAR = BQ + 2 * BQ_BYTES;
-    // raw_full[NST], raw_empty[NST], then [2] each of ak_full, ak_empty,
-    // av_full, av_empty, s_full, s_empty, p_full, p_empty, o_full, o_empty, and
-    // one drain barrier
-    static constexpr int NBAR = 2 * NST + 20 + 1;
+    // raw_full[NST], raw_empty[NST], then [2] each of ak_full, av_full,
+    // s_full, s_empty, p_full, o_full, o_empty, and one drain barrier per issuer
+    static constexpr int NBAR = 2 * NST + 14 + 2;
     static constexpr int MISC = BAR + NBAR * 8;
     static constexpr int TMEM_SLOT = MISC;             // uint32 TMEM base address
     static constexpr int ERR = MISC + 4;               // int, any role's failed wait
-    static constexpr int SERR = MISC + 8;              // int, the softmax warpgroup's own
+    static constexpr int SERR = MISC + 8;              // int [2], the softmax warpgroup's own
     static constexpr int RED = MISC + 16;              // fp32 reduction scratch
     static constexpr int RED_FLOATS = 4 * HT * (1 + G + 1 + 1) + HT;
     static constexpr int BYTES = RED + RED_FLOATS * 4 + 16;
@@ -144,6 +147,28 @@ __device__ __forceinline__ void tmem_st_16x256b_x8(uint32_t taddr, const uint32_
         "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
         "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
+}
+__device__ __forceinline__ void tmem_st_16x256b_x1(uint32_t taddr, uint32_t v0, uint32_t v1, uint32_t v2,
+                                                   uint32_t v3) {
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x1.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v0),
+                 "r"(v1), "r"(v2), "r"(v3)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&v)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(taddr));
+}
+// Bounded waits on up to three mbarrier phases at once. Every phase is tested
+// before any is waited on: a test of a phase that completed long ago still
+// takes a shared-memory round trip, and independent tests overlap.
+__device__ __forceinline__ bool wait_all(uint64_t* b0, uint32_t p0, uint64_t* b1 = nullptr,
+                                         uint32_t p1 = 0, uint64_t* b2 = nullptr, uint32_t p2 = 0) {
+    const bool d0 = mma4::mbar_try_wait(b0, p0);
+    const bool d1 = b1 == nullptr || mma4::mbar_try_wait(b1, p1);
+    const bool d2 = b2 == nullptr || mma4::mbar_try_wait(b2, p2);
+    if (d0 && d1 && d2) return true;
+    return (d0 || mbar_wait(b0, p0)) && (d1 || mbar_wait(b1, p1)) && (d2 || mbar_wait(b2, p2));
 }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile(
@@ -244,43 +269,40 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::BAR);
     uint64_t* raw_full = bar;
     uint64_t* raw_empty = bar + NST;
+    // s_full[b] (scores of a tile done) also frees the tile's K operand and,
+    // one item later, its Qg buffer; o_full[b] (combine done) also frees the
+    // tile's V operand and its P' buffer
     uint64_t* ak_full = bar + 2 * NST;
-    uint64_t* ak_empty = ak_full + 2;
-    uint64_t* av_full = ak_full + 4;
-    uint64_t* av_empty = ak_full + 6;
-    uint64_t* s_full = ak_full + 8;
-    uint64_t* s_empty = ak_full + 10;
-    uint64_t* p_full = ak_full + 12;
-    uint64_t* p_empty = ak_full + 14;
-    uint64_t* o_full = ak_full + 16;
-    uint64_t* o_empty = ak_full + 18;
-    uint64_t* drain = ak_full + 20;
+    uint64_t* av_full = ak_full + 2;
+    uint64_t* s_full = ak_full + 4;
+    uint64_t* s_empty = ak_full + 6;
+    uint64_t* p_full = ak_full + 8;
+    uint64_t* o_full = ak_full + 10;
+    uint64_t* o_empty = ak_full + 12;
+    uint64_t* drain = ak_full + 14;       // [2]: one per MMA issuer
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::TMEM_SLOT);
     volatile int* err = reinterpret_cast<volatile int*>(smem + C::ERR);
-    volatile int* serr = reinterpret_cast<volatile int*>(smem + C::SERR);
+    volatile int* serr = reinterpret_cast<volatile int*>(smem + C::SERR);   // [2]
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     if (tid == 0) {
         for (int s = 0; s < NST; ++s) {
             mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], 12);          // every unpack and softmax warp
+            mbar_init(&raw_empty[s], 8);           // every K and V unpack warp
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ak_full[b], 4);
-            mbar_init(&ak_empty[b], 1);
             mbar_init(&av_full[b], 4);
-            mbar_init(&av_empty[b], 1);
             mbar_init(&s_full[b], 1);
             mbar_init(&s_empty[b], 4);
             mbar_init(&p_full[b], 4);
-            mbar_init(&p_empty[b], 1);
             mbar_init(&o_full[b], 1);
             mbar_init(&o_empty[b], 4);
+            mbar_init(&drain[b], 1);
         }
-        mbar_init(drain, 1);
         *err = 0;
-        *serr = 0;
+        serr[0] = serr[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == W_MMA) {
@@ -338,59 +360,66 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             }
         }
     } else if (warp == W_MMA) {
-        // ------------------------------ MMA issuer ----------------------------
+        // ------------------------- score MMA issuer ---------------------------
         if (lane == 0) {
-            const uint32_t bq0 = s_addr(smem + C::BQ), bp0 = s_addr(smem + C::BP);
+            const uint32_t bq0 = s_addr(smem + C::BQ);
             uint32_t gt = 0, ni = 0;
-            int prev = -1;
             bool ok = true;
-            auto combine = [&](uint32_t g) -> bool {
-                const uint32_t b = g & 1, ph = (g >> 1) & 1;
-                if (!mbar_wait(&av_full[b], ph) || !mbar_wait(&p_full[b], ph)) return false;
-                if (g >= 2 && !mbar_wait(&o_empty[b], ph ^ 1)) return false;
-                tc_fence_after();
-#pragma unroll
-                for (int s = 0; s < TP / 16; ++s)
-                    umma_ts(tmem + C::O0 + C::N_O * b, tmem + C::AV0 + 64 * b + 8 * s,
-                            sdesc(bp0 + b * C::BP_BYTES + s * 2 * C::BP_LBO, C::BP_LBO, 128), ID_V,
-                            s > 0 ? 1u : 0u);
-                umma_commit(&o_full[b]);
-                umma_commit(&av_empty[b]);
-                umma_commit(&p_empty[b]);
-                return true;
-            };
             for (uint32_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
                 const Item it = item_of<HT>(P, idx);
                 if (it.n_tiles == 0) continue;
-                const uint32_t bq = bq0 + (ni & 1) * C::BQ_BYTES;
+                // K-step s of the Qg operand starts 256 bytes (16 descriptor units) after s-1's
+                const uint64_t qdesc = sdesc(bq0 + (ni & 1) * C::BQ_BYTES, 128, 2048);
                 for (int i = 0; i < it.n_tiles; ++i, ++gt) {
                     const uint32_t b = gt & 1, ph = (gt >> 1) & 1;
-                    if (!mbar_wait(&ak_full[b], ph) || (gt >= 2 && !mbar_wait(&s_empty[b], ph ^ 1))) {
+                    if (!wait_all(&ak_full[b], ph, gt >= 2 ? &s_empty[b] : nullptr, ph ^ 1)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
+                    const uint32_t d = tmem + C::S0 + 16 * b, a = tmem + C::AK0 + 64 * b;
 #pragma unroll
-                    for (int s = 0; s < DH / 16; ++s)
-                        umma_ts(tmem + C::S0 + 16 * b, tmem + C::AK0 + 64 * b + 8 * s,
-                                sdesc(bq + s * 256, 128, 2048), ID_S, s > 0 ? 1u : 0u);
+                    for (int k = 0; k < DH / 16; ++k)
+                        umma_ts(d, a + 8 * k, qdesc + 16 * k, ID_S, k > 0 ? 1u : 0u);
                     umma_commit(&s_full[b]);
-                    umma_commit(&ak_empty[b]);
-                    if (prev >= 0 && !combine((uint32_t)prev)) {
-                        ok = false;
-                        break;
-                    }
-                    prev = (int)gt;
                 }
                 ++ni;
             }
-            if (ok && prev >= 0 && !combine((uint32_t)prev)) ok = false;
             if (!ok) *err = 1;
-            // every MMA issued has completed before tensor memory is freed
-            umma_commit(drain);
-            (void)mbar_wait(drain, 0);
+            // every MMA this thread issued has completed before tensor memory is freed
+            umma_commit(&drain[0]);
+            (void)mbar_wait(&drain[0], 0);
         }
-    } else if (warp < W_V) {
+    } else if (warp == W_MMA_C) {
+        // ------------------------ combine MMA issuer --------------------------
+        if (lane == 0) {
+            const uint32_t bp0 = s_addr(smem + C::BP);
+            uint32_t gt = 0;
+            bool ok = true;
+            for (uint32_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+                const Item it = item_of<HT>(P, idx);
+                for (int i = 0; i < it.n_tiles; ++i, ++gt) {
+                    const uint32_t b = gt & 1, ph = (gt >> 1) & 1;
+                    if (!wait_all(&av_full[b], ph, &p_full[b], ph, gt >= 2 ? &o_empty[b] : nullptr, ph ^ 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    // K-step s (16 positions) of P' starts two 8-position row blocks after s-1's
+                    const uint64_t pdesc = sdesc(bp0 + b * C::BP_BYTES, C::BP_LBO, 128);
+                    const uint32_t d = tmem + C::O0 + C::N_O * b, a = tmem + C::AV0 + 64 * b;
+#pragma unroll
+                    for (int k = 0; k < TP / 16; ++k)
+                        umma_ts(d, a + 8 * k, pdesc + (uint64_t)((2 * C::BP_LBO) >> 4) * k, ID_V,
+                                k > 0 ? 1u : 0u);
+                    umma_commit(&o_full[b]);
+                }
+            }
+            if (!ok) *err = 1;
+            umma_commit(&drain[1]);
+            (void)mbar_wait(&drain[1], 0);
+        }
+    } else if (warp >= W_K && warp < W_V) {
         // ------------------------------ K unpack ------------------------------
         const int q = warp & 3, r = lane >> 2, j = lane & 3;
         const int tq = (warp - W_K) * 32 + lane;               // 0..127
@@ -401,8 +430,10 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             if (it.n_tiles == 0) continue;
             for (int i = 0; i < it.n_tiles; ++i, ++gt) {
                 const uint32_t slot = gt % NST, b = gt & 1;
-                if (!mbar_wait(&raw_full[slot], (gt / NST) & 1) ||
-                    (gt >= 2 && !mbar_wait(&ak_empty[b], ((gt >> 1) & 1) ^ 1))) {
+                // s_empty of tile gt-2: its scores and scales are read (so its
+                // scores were computed: the K operand and, one item on, the Qg buffer are free)
+                if (!wait_all(&raw_full[slot], (gt / NST) & 1, gt >= 2 ? &s_empty[b] : nullptr,
+                              ((gt >> 1) & 1) ^ 1)) {
                     ok = false;
                     break;
                 }
@@ -460,6 +491,25 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 const uint32_t col = tmem + C::AK0 + 64 * b;
                 tmem_st_16x256b_x8(col + ((uint32_t)(32 * q) << 16), ra);
                 tmem_st_16x256b_x8(col + ((uint32_t)(32 * q + 16) << 16), rb);
+                // the rows' scale/bias pairs: lane j = 0 columns 0, 1 (k scale, k
+                // bias), j = 1 columns 2, 3 (v scale, v bias), j = 2, 3 unused
+                {
+                    const unsigned char* sb = smem + slot * C::STAGE + (j == 0 ? C::KS : C::VS);
+                    const int d2 = j == 0 ? C::KB - C::KS : C::VB - C::VS;
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const int p0 = 32 * q + 16 * half + r, p1 = p0 + 8;
+                        uint32_t a0 = 0u, a1 = 0u, b0 = 0u, b1 = 0u;
+                        if (j < 2) {
+                            a0 = *reinterpret_cast<const uint32_t*>(sb + p0 * 4);
+                            a1 = *reinterpret_cast<const uint32_t*>(sb + d2 + p0 * 4);
+                            b0 = *reinterpret_cast<const uint32_t*>(sb + p1 * 4);
+                            b1 = *reinterpret_cast<const uint32_t*>(sb + d2 + p1 * 4);
+                        }
+                        tmem_st_16x256b_x1(tmem + C::SC0 + 8 * b + ((uint32_t)(32 * q + 16 * half) << 16),
+                                           a0, a1, b0, b1);
+                    }
+                }
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
@@ -471,7 +521,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             ++ni;
         }
         if (!ok) *err = 1;
-    } else if (warp < W_S) {
+    } else if (warp >= W_V && warp < W_S) {
         // ------------------------------ V unpack ------------------------------
         const int q = warp & 3;
         uint32_t gt = 0;
@@ -480,8 +530,8 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             const Item it = item_of<HT>(P, idx);
             for (int i = 0; i < it.n_tiles; ++i, ++gt) {
                 const uint32_t slot = gt % NST, b = gt & 1;
-                if (!mbar_wait(&raw_full[slot], (gt / NST) & 1) ||
-                    (gt >= 2 && !mbar_wait(&av_empty[b], ((gt >> 1) & 1) ^ 1))) {
+                if (!wait_all(&raw_full[slot], (gt / NST) & 1, gt >= 2 ? &o_full[b] : nullptr,
+                              ((gt >> 1) & 1) ^ 1)) {
                     ok = false;
                     break;
                 }
@@ -517,7 +567,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             }
         }
         if (!ok) *err = 1;
-    } else {
+    } else if (warp >= W_S && warp < W_S + 4) {
         // ------------------------------ softmax -------------------------------
         const int q = warp & 3;
         const int p = 32 * q + lane;             // tile position = TMEM lane (scores)
@@ -533,6 +583,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
         float* snew = red_m + 4 * HT;            // [HT]
         const size_t rows = (size_t)P.b_rows * P.n_heads;
         uint32_t gt = 0;
+        uint32_t vc = 0;     // warpgroup checks so far: failures of check c go to serr[c % 2]
         bool bad = false;
 
         for (uint32_t idx = blockIdx.x; idx < n_items; idx += gridDim.x) {
@@ -554,18 +605,19 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
 #pragma unroll
                     for (int h = 0; h < HT; ++h) qs[g][h] = red_q[(2 * g) * HT + h] + red_q[(2 * g + 1) * HT + h];
             }
-            float m_run[HT], l_part[HT], bsum[G][HT], o[HT], alpha_prev[HT];
+            float m_run[HT], l_part[HT], bsum[G][HT], o[HT], alpha_p1[HT], alpha_p2[HT];
 #pragma unroll
             for (int h = 0; h < HT; ++h) {
                 m_run[h] = -INFINITY;
                 l_part[h] = 0.0f;
                 o[h] = 0.0f;
-                alpha_prev[h] = 1.0f;
+                alpha_p1[h] = alpha_p2[h] = 1.0f;
 #pragma unroll
                 for (int g = 0; g < G; ++g) bsum[g][h] = 0.0f;
             }
-            // O of tile g2 (this thread's dim and group) into the registers
-            auto accumulate = [&](uint32_t g2) {
+            // O of tile g2 (this thread's dim and group) into the registers:
+            // o = o * alpha + O_tile, alpha the reference-point move of that tile
+            auto accumulate = [&](uint32_t g2, const float (&alpha)[HT]) {
                 const uint32_t b = g2 & 1;
                 const uint32_t col = tmem + C::O0 + C::N_O * b + C::GW * gq + lane_addr;
                 if constexpr (HT == 4) {
@@ -574,7 +626,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                     tmem_wait_ld();
 #pragma unroll
                     for (int h = 0; h < HT; ++h)
-                        o[h] = fmaf(o[h], alpha_prev[h],
+                        o[h] = fmaf(o[h], alpha[h],
                                     __uint_as_float(v[h]) + __uint_as_float(v[HT + h]) +
                                         __uint_as_float(v[2 * HT + h]));
                 } else {
@@ -583,7 +635,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                     tmem_wait_ld();
 #pragma unroll
                     for (int h = 0; h < HT; ++h)
-                        o[h] = fmaf(o[h], alpha_prev[h],
+                        o[h] = fmaf(o[h], alpha[h],
                                     __uint_as_float(v[h]) + __uint_as_float(v[HT + h]) +
                                         __uint_as_float(v[2 * HT + h]));
                 }
@@ -593,30 +645,30 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             };
 
             for (int i = 0; i < it.n_tiles && !bad; ++i, ++gt) {
-                const uint32_t slot = gt % NST, b = gt & 1, ph = (gt >> 1) & 1;
+                const uint32_t b = gt & 1, ph = (gt >> 1) & 1;
                 // every wait of the tile first, then one warpgroup vote on the
-                // outcome (so every thread takes the same branches)
-                bool okw = mbar_wait(&raw_full[slot], (gt / NST) & 1) && mbar_wait(&s_full[b], ph);
-                if (gt >= 2) okw = okw && mbar_wait(&p_empty[b], ph ^ 1);
-                if (i > 0) okw = okw && mbar_wait(&o_full[(gt - 1) & 1], ((gt - 1) >> 1) & 1);
-                if (!okw) *serr = 1;
+                // outcome (so every thread takes the same branches). O is taken
+                // two tiles behind: tile i-2's combine ran during tile i-1.
+                // o_full of tile gt-2: its O is ready and this P' buffer is free
+                const bool okw = wait_all(&s_full[b], ph, gt >= 2 ? &o_full[b] : nullptr, ph ^ 1);
+                if (!okw) serr[vc & 1] = 1;
                 tc_fence_after();
-                if (i > 0) accumulate(gt - 1);
+                if (i >= 2) accumulate(gt - 2, alpha_p2);
 
-                // scores of position p
-                uint32_t xs[16];
+                // scores of position p, and its scales and biases
+                uint32_t xs[16], sv[4];
                 tmem_ld16(tmem + C::S0 + 16 * b + lane_addr, xs);
+                tmem_ld4(tmem + C::SC0 + 8 * b + lane_addr, sv);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&s_empty[b]);
-                const unsigned char* st = smem + slot * C::STAGE;
                 const int nvalid = (int)min((uint32_t)TP, it.hi - (it.lo + i * TP));
                 const bool live = p < nvalid;
-                const float2 ks2 = __half22float2(*reinterpret_cast<const __half2*>(st + C::KS + p * 4));
-                const float2 kb2 = __half22float2(*reinterpret_cast<const __half2*>(st + C::KB + p * 4));
-                const float2 vs2 = __half22float2(*reinterpret_cast<const __half2*>(st + C::VS + p * 4));
-                const float2 vb2 = __half22float2(*reinterpret_cast<const __half2*>(st + C::VB + p * 4));
+                const float2 ks2 = __half22float2(*reinterpret_cast<const __half2*>(&sv[0]));
+                const float2 kb2 = __half22float2(*reinterpret_cast<const __half2*>(&sv[1]));
+                const float2 vs2 = __half22float2(*reinterpret_cast<const __half2*>(&sv[2]));
+                const float2 vb2 = __half22float2(*reinterpret_cast<const __half2*>(&sv[3]));
                 const float ksc[G] = {ks2.x * scale2, ks2.y * scale2};
                 const float cq[G] = {fmaf(ksc[0], -1024.0f, kb2.x * scale2), fmaf(ksc[1], -1024.0f, kb2.y * scale2)};
                 float sc[HT];
@@ -630,15 +682,13 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                     sc[h] = live ? a : -INFINITY;
                     grow |= sc[h] > m_run[h] + 8.0f;
                 }
-                // the stage's fp16 data is consumed
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&raw_empty[slot]);
 
-                const bool any_grow = consumers_any(grow);   // also a barrier: serr is uniform after it
-                if (*serr) {
+                const bool any_grow = consumers_any(grow);   // a barrier: serr[vc] is settled
+                if (serr[vc & 1]) {
                     bad = true;
                     break;
                 }
+                ++vc;
                 float alpha[HT];
 #pragma unroll
                 for (int h = 0; h < HT; ++h) alpha[h] = 1.0f;
@@ -700,17 +750,23 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[b]);
 #pragma unroll
-                for (int h = 0; h < HT; ++h) alpha_prev[h] = alpha[h];
+                for (int h = 0; h < HT; ++h) {
+                    alpha_p2[h] = alpha_p1[h];
+                    alpha_p1[h] = alpha[h];
+                }
             }
-            // the item's last O tile
+            // the item's last two O tiles
             if (!bad && it.n_tiles > 0) {
                 const uint32_t last = gt - 1;
-                const bool okw = mbar_wait(&o_full[last & 1], (last >> 1) & 1);
-                if (!okw) *serr = 1;
+                bool okw = mbar_wait(&o_full[last & 1], (last >> 1) & 1);
+                if (it.n_tiles >= 2) okw = okw && mbar_wait(&o_full[(last - 1) & 1], ((last - 1) >> 1) & 1);
+                if (!okw) serr[vc & 1] = 1;
                 tc_fence_after();
-                accumulate(last);
+                if (it.n_tiles >= 2) accumulate(last - 1, alpha_p2);
+                accumulate(last, alpha_p1);
                 named_sync(SM_BAR, 128);
-                if (*serr) bad = true;
+                if (serr[vc & 1]) bad = true;
+                ++vc;
             }
 
             // ---- the item's partial: l and bias sums over the warpgroup ------
