@@ -233,7 +233,14 @@ class SequenceSplitDecoder:
 
     def step(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
              bits: int, t_local: int, out=None):
-        """out [B, H, DH] in q's dtype, identical on every rank."""
+        """out [B, H, DH] in q's dtype, identical on every rank. On a single
+        rank the split is the whole sequence: one kvq_decode."""
+        if self.world == 1:
+            from kernelverify_b200.pack import kv_attention as kva
+            res = kva.decode(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
+                             bits=bits, t_cached=t_local, out=out, workspace=self.workspace)
+            self.steps += 1
+            return res
         self.partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
                      bits=bits, t_local=t_local)
         res = self.finish(q.dtype, out=out)
@@ -252,6 +259,12 @@ class SequenceSplitDecoder:
         import torch
         self._dtype = q.dtype
         args = (q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v)
+        if self.world == 1:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                self.step(*args, bits=bits, t_local=t_local, out=out)
+            self.steps -= 1          # capture does not count as a step
+            return CapturedStep(self, (g,))
         if self.transport == "peer":
             graphs = []
             for parity in (0, 1):

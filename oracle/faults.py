@@ -31,12 +31,21 @@ def kv_attention(inputs, *, scores_dtype="float32", accum_dtype="float32",
                  new_entry_skipped=False, dhead_scale_dropped=False):
     """One decode step at fp32 over the canonical artefacts, with seams
     (kernelverify/reference/native_kernels.py:168-221)."""
-    q, new_k, new_v = inputs["q"], inputs["new_k"], inputs["new_v"]
     bits, g = int(inputs["bits"][0]), group_of(inputs)
-    dh = q.shape[-1]
     kd = cache_dequant(inputs["k_cache"], bits, g, scales_rotated if k_scales_rotated else None)
     vd = cache_dequant(inputs["v_cache"], bits, g, bias_dropped if v_bias_dropped else None)
+    return attend_dequantized(inputs["q"], kd, vd, inputs["new_k"], inputs["new_v"],
+                              scores_dtype=scores_dtype, accum_dtype=accum_dtype,
+                              new_entry_skipped=new_entry_skipped,
+                              dhead_scale_dropped=dhead_scale_dropped)
 
+
+def attend_dequantized(q, kd, vd, new_k, new_v, *, scores_dtype="float32", accum_dtype="float32",
+                       new_entry_skipped=False, dhead_scale_dropped=False):
+    """The port's attention arithmetic over already dequantized fp32 caches
+    kd/vd [H, T, DH] (kernelverify/reference/native_kernels.py:178-221): the
+    part of a step that remains once the artefacts are decoded."""
+    dh = q.shape[-1]
     qf = q.astype(np.float32)
     scale = 1.0 if dhead_scale_dropped else 1.0 / np.sqrt(np.float32(dh))
     scores = np.einsum("bhd,htd->bht", qf, kd) * scale

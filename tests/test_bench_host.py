@@ -28,4 +28,39 @@ def test_sweep_arguments():
     a = bench.parse_args(["--config", "3", "--bits", "6", "--group", "32"])
     assert (a.config, a.bits, a.group) == (3, 6, 32)
     assert bench.SWEEP_BITS == (2, 3, 4, 6, 8) and bench.SWEEP_GROUPS == (32, 64, 128)
-    assert bench.parse_args([]).config == 2
+    # the default is the metric's 1/2/4/8-GPU configuration, the sequence split
+    assert bench.parse_args([]).config == 5
+
+
+def test_cpu_shards_and_parity_unpack():
+    """The CPU baseline's shard of a unit, and the bench's library-independent
+    code unpack against the oracle's packer (every width, straddling codes)."""
+    import numpy as np
+    import torch
+    from oracle import quant
+    assert bench.cpu_shard_positions(bench.CONFIG5) == 8192
+    assert bench.cpu_shard_positions(bench.CONFIG2) == 512
+    rng = np.random.default_rng(3)
+    for bits in (2, 3, 4, 6, 8):
+        codes = rng.integers(0, 1 << bits, size=(5, 128))
+        words = quant.pack_codes(codes, bits)
+        got = bench._unpack_codes(torch.from_numpy(words.view(np.int32)), bits, 128)
+        assert np.array_equal(got.numpy().astype(np.int64), codes)
+
+
+def test_parity_unit_matches_the_oracle_reference():
+    """The bench's fp64 device reference, run on the CPU here, equals the
+    oracle's fp64 reference on the same packed rows."""
+    import numpy as np
+    import torch
+    from oracle import cases, kv, quant
+    q, kc, vc, nk, nv = cases.make_case(1, 4, 300, 128, seed=5)
+    kc, vc, nk, nv = kc[:1], vc[:1], nk[:, :1], nv[:, :1]
+    kw, ks, kb = quant.quantize_cache(kc, 4)
+    vw, vs, vb = quant.quantize_cache(vc, 4)
+    art = tuple(torch.from_numpy(np.ascontiguousarray(a.view(np.int32) if a.dtype == np.uint32 else a))[0]
+                for a in (kw, ks, kb, vw, vs, vb))
+    ref = kv.kv_reference(kv.gqa_tiled_inputs(q, kc, vc, nk, nv, 4))[0]
+    res = bench.parity_unit(torch.from_numpy(ref), torch.from_numpy(q[0]), torch.from_numpy(nk[0, 0]),
+                            torch.from_numpy(nv[0, 0]), art, 4)
+    assert res["ok"] and res["max_abs"] < 1e-12, res
