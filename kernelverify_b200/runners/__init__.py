@@ -8,7 +8,7 @@ candidate cannot take down with it. Importing this package touches no GPU;
 ask `CudaRunner().probe()` whether a device is present.
 """
 
-from kernelverify_b200.runners.cuda import BatchResult, CudaRunner
+from kernelverify_b200.runners.cuda import BatchResult, CompiledSession, CudaRunner, SessionError
 from kernelverify_b200.runners.result import DeviceInfo, RunResult, RunStatus, Timing
 from kernelverify_b200.runners.spec import (
     Binding,
@@ -21,6 +21,6 @@ from kernelverify_b200.runners.spec import (
 )
 from kernelverify_b200.runners.specialize import specialize
 
-__all__ = ["BatchResult", "Binding", "BindingKind", "CudaRunner", "DeviceInfo", "KernelSpec",
-           "LaunchMode", "LaunchSpec", "RunCase", "RunResult", "RunStatus", "SpecError",
-           "Timing", "specialize"]
+__all__ = ["BatchResult", "Binding", "BindingKind", "CompiledSession", "CudaRunner", "DeviceInfo",
+           "KernelSpec", "LaunchMode", "LaunchSpec", "RunCase", "RunResult", "RunStatus",
+           "SessionError", "SpecError", "Timing", "specialize"]

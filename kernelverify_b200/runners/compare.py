@@ -17,18 +17,18 @@ discipline --
 * an arm that hangs, dies or fails a case aborts the comparison with the
   arm's status in `failure`: a kernel that did not finish has no timing.
 
-Each worker runs in its own process group, as the batch runner's do, so a
-hung arm is killed with everything it started.
+Each arm is a `CompiledSession` (runners/cuda.py): a worker in its own
+process group, as the batch runner's are, so a hung arm is killed with
+everything it started.
 """
 
 from __future__ import annotations
 
-import json
+import contextlib
 import statistics
 from dataclasses import dataclass, field
 
-from kernelverify_b200.runners.cuda import CudaRunner, _drain, _EventStream, _tail
-from kernelverify_b200.runners.result import RunResult
+from kernelverify_b200.runners.cuda import CompiledSession, CudaRunner, SessionError
 from kernelverify_b200.runners.spec import KernelSpec, RunCase, SpecError
 
 DEFAULT_SPREAD_LIMIT = 1.5
@@ -102,81 +102,14 @@ class CompareReport:
         return "\n".join(lines)
 
 
-class ComparisonAborted(RuntimeError):
-    """An arm could not finish its half of the comparison."""
-
-
-class _LiveArm:
-    """A stream-mode worker holding one compiled spec across the rounds."""
-
-    def __init__(self, runner: CudaRunner, spec: KernelSpec, name: str, warmup: int,
-                 repeats: int):
-        self.name, self.runner = name, runner
-        self.proc = runner._spawn(["--stream"])
-        self.stderr: list = []
-        self.drain = _drain(self.proc.stderr, self.stderr)
-        self.events = _EventStream(self.proc.stdout)
-        try:
-            self._send({"spec": spec.to_json(), "warmup": warmup, "repeats": repeats,
-                        "math_mode": runner.math_mode})
-            self._await_compiled()
-        except BaseException:
-            runner._terminate(self.proc)
-            raise
-
-    def _send(self, payload: dict) -> None:
-        try:
-            self.proc.stdin.write(json.dumps(payload) + "\n")
-            self.proc.stdin.flush()
-        except (BrokenPipeError, ValueError, OSError) as error:
-            raise ComparisonAborted(self._died(f"while being sent work ({error})")) from None
-
-    def _next(self, budget: float, what: str) -> dict:
-        try:
-            event = self.events.next_event(budget)
-        except TimeoutError:
-            raise ComparisonAborted(f"arm {self.name}: timed out {what}") from None
-        if event is None:
-            raise ComparisonAborted(self._died(what))
-        if event.get("event") == "fatal":
-            r = RunResult.from_json(event["result"])
-            raise ComparisonAborted(f"arm {self.name}: {r.status.value}: {r.detail}")
-        return event
-
-    def _await_compiled(self) -> None:
-        while self._next(self.runner.startup_timeout, "before compiling").get("event") != "compiled":
-            pass
-
-    def time_case(self, case: RunCase, line: str) -> RunResult:
-        """Dispatch one case (its wire line is encoded once, outside the
-        rounds, so encoding never widens the gap between the two arms)."""
-        try:
-            self.proc.stdin.write(line)
-            self.proc.stdin.flush()
-        except (BrokenPipeError, ValueError, OSError):
-            raise ComparisonAborted(self._died(f"on case {case.label!r}")) from None
-        while True:
-            event = self._next(self.runner.case_timeout, f"on case {case.label!r}")
-            if event.get("event") != "case":
-                continue
-            result = RunResult.from_json(event["result"])
-            if not result.ok or result.timing is None:
-                raise ComparisonAborted(f"arm {self.name} failed case {case.label!r}: "
-                                        f"{result.status.value}: {result.detail}")
-            return result
-
-    def _died(self, when: str) -> str:
-        self.drain.join(timeout=0.5)
-        return f"arm {self.name}: the worker died {when}" + _tail("".join(self.stderr))
-
-    def close(self) -> None:
-        try:
-            self.proc.stdin.write(json.dumps({"end": True}) + "\n")
-            self.proc.stdin.flush()
-        except (BrokenPipeError, ValueError, OSError):
-            pass
-        self.runner._terminate(self.proc)
-        self.drain.join(timeout=1.0)
+def _round(arms, case: RunCase, line: str, round_index: int, spread_limit: float) -> RoundSample:
+    """One round of one case: the reference arm, then the candidate, back to
+    back on the same wire line; the round stands if the reference arm's own
+    repeats stayed within `spread_limit` of each other."""
+    ref, cand = (arm.time(case, line).timing for arm in arms)
+    return RoundSample(round_index=round_index, ref_best=ref.gpu_best, cand_best=cand.gpu_best,
+                       ref_spread=ref.gpu_spread, cand_spread=cand.gpu_spread,
+                       accepted=ref.gpu_spread <= spread_limit)
 
 
 def compare(spec_a: KernelSpec, spec_b: KernelSpec, cases, *, rounds: int = DEFAULT_ROUNDS,
@@ -190,35 +123,34 @@ def compare(spec_a: KernelSpec, spec_b: KernelSpec, cases, *, rounds: int = DEFA
     runner = runner or CudaRunner()
     cases = list(cases)
     report = CompareReport(spread_limit=spread_limit)
-    for spec, name in ((spec_a, "A"), (spec_b, "B")):
-        for c in cases:
-            try:
-                c.validate_against(spec)
-            except SpecError as error:
-                report.failure = f"arm {name}, case {c.label!r}: {error}"
-                return report
-    wire = [json.dumps({"index": i, "case": c.to_json()}) + "\n" for i, c in enumerate(cases)]
-    arms: list = []
+    bad = next(((name, c, err) for spec, name in ((spec_a, "A"), (spec_b, "B")) for c in cases
+                for err in [_mismatch(c, spec)] if err), None)
+    if bad is not None:
+        name, c, err = bad
+        report.failure = f"arm {name}, case {c.label!r}: {err}"
+        return report
+    lines = [CompiledSession.encode(i, c) for i, c in enumerate(cases)]
+    table = [CaseComparison(label=c.label or f"case {i}") for i, c in enumerate(cases)]
     try:
-        ref = _LiveArm(runner, spec_a, "A (reference)", warmup, repeats)
-        arms.append(ref)
-        cand = _LiveArm(runner, spec_b, "B (candidate)", warmup, repeats)
-        arms.append(cand)
-        out = [CaseComparison(label=c.label or f"case {i}") for i, c in enumerate(cases)]
-        for r in range(rounds):
-            for i, c in enumerate(cases):
-                a = ref.time_case(c, wire[i]).timing
-                b = cand.time_case(c, wire[i]).timing
-                out[i].samples.append(RoundSample(
-                    round_index=r, ref_best=a.gpu_best, cand_best=b.gpu_best,
-                    ref_spread=a.gpu_spread, cand_spread=b.gpu_spread,
-                    accepted=a.gpu_spread <= spread_limit))
-        report.cases = out
-    except ComparisonAborted as error:
+        with contextlib.ExitStack() as held:
+            arms = [held.enter_context(CompiledSession(runner, spec, warmup=warmup, repeats=repeats,
+                                                       name=name))
+                    for spec, name in ((spec_a, "A (reference)"), (spec_b, "B (candidate)"))]
+            for r in range(rounds):
+                for row, case, line in zip(table, cases, lines):
+                    row.samples.append(_round(arms, case, line, r, spread_limit))
+        report.cases = table
+    except SessionError as error:
         report.failure = str(error)
     except OSError as error:
         report.failure = f"a worker would not start: {error}"
-    finally:
-        for arm in arms:
-            arm.close()
     return report
+
+
+def _mismatch(case: RunCase, spec: KernelSpec) -> str:
+    """Why `case` cannot run on `spec` ('' when it can)."""
+    try:
+        case.validate_against(spec)
+    except SpecError as error:
+        return str(error)
+    return ""

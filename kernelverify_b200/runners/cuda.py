@@ -327,6 +327,100 @@ class CudaRunner:
                 pass
 
 
+class SessionError(RuntimeError):
+    """A compiled session could not serve a request: its worker went silent
+    past its budget, exited, reported a fatal status, or failed the case."""
+
+
+class CompiledSession:
+    """One kernel held compiled by an isolated worker in `--stream` mode, for
+    timing many cases against the same compiled code (an interleaved A/B
+    keeps one session per arm open for all its rounds).
+
+        with CompiledSession(runner, spec, warmup=1, repeats=3, name="A") as s:
+            result = s.time(case)
+
+    `time` returns the case's RunResult or raises SessionError; the worker's
+    process group ends on close() or leaving the `with` block, whatever state
+    it is in."""
+
+    def __init__(self, runner: CudaRunner, spec: KernelSpec, *, warmup: int, repeats: int,
+                 name: str = "session"):
+        self.runner, self.name = runner, name
+        self._stderr: list = []
+        self._proc = runner._spawn(["--stream"])
+        self._stderr_reader = _drain(self._proc.stderr, self._stderr)
+        self._events = _EventStream(self._proc.stdout)
+        try:
+            self._write(json.dumps({"spec": spec.to_json(), "warmup": warmup, "repeats": repeats,
+                                    "math_mode": runner.math_mode}) + "\n", "before compiling")
+            self._expect("compiled", runner.startup_timeout, "before compiling")
+        except BaseException:
+            self.close()
+            raise
+
+    @staticmethod
+    def encode(index: int, case: RunCase) -> str:
+        """The wire line of a case request (encode once, send many times)."""
+        return json.dumps({"index": index, "case": case.to_json()}) + "\n"
+
+    def time(self, case: RunCase, line: str | None = None) -> RunResult:
+        what = f"on case {case.label!r}"
+        self._write(line if line is not None else self.encode(0, case), what)
+        result = RunResult.from_json(self._expect("case", self.runner.case_timeout, what)["result"])
+        if not result.ok or result.timing is None:
+            raise SessionError(f"arm {self.name} failed case {case.label!r}: "
+                               f"{result.status.value}: {result.detail}")
+        return result
+
+    def close(self) -> None:
+        proc, self._proc = self._proc, None
+        if proc is None:
+            return
+        try:
+            proc.stdin.write(json.dumps({"end": True}) + "\n")
+            proc.stdin.flush()
+        except (BrokenPipeError, ValueError, OSError):
+            pass
+        self.runner._terminate(proc)
+        self._stderr_reader.join(timeout=1.0)
+
+    def __enter__(self) -> "CompiledSession":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    # -- the wire --------------------------------------------------------------
+    def _write(self, text: str, what: str) -> None:
+        try:
+            self._proc.stdin.write(text)
+            self._proc.stdin.flush()
+        except (BrokenPipeError, ValueError, OSError, AttributeError):
+            raise SessionError(self._exited(what)) from None
+
+    def _expect(self, kind: str, budget: float, what: str) -> dict:
+        """The next event of `kind`; every wait for an event is bounded by
+        `budget` seconds."""
+        while True:
+            try:
+                event = self._events.next_event(budget)
+            except TimeoutError:
+                raise SessionError(f"arm {self.name}: timed out {what}") from None
+            if event is None:
+                raise SessionError(self._exited(what))
+            tag = event.get("event")
+            if tag == "fatal":
+                failed = RunResult.from_json(event["result"])
+                raise SessionError(f"arm {self.name}: {failed.status.value}: {failed.detail}")
+            if tag == kind:
+                return event
+
+    def _exited(self, what: str) -> str:
+        self._stderr_reader.join(timeout=0.5)
+        return f"arm {self.name}: the worker died {what}" + _tail("".join(self._stderr))
+
+
 def spawn_isolated(python: str, module: str, args=(), env=None, **popen_kwargs) -> subprocess.Popen:
     """`python -m module *args` in its own session (so a hung kernel can be
     killed by process group), cwd and PYTHONPATH at the repo root, text pipes
