@@ -4,38 +4,39 @@
 //
 // One CTA per SM walks a list of work items -- (batch row, cache head, head
 // tile, T split), consecutive items of a CTA gridDim.x apart -- through one
-// continuous pipeline of 128-position tiles. Fourteen warps, four roles:
+// continuous pipeline of 128-position tiles. Twenty warps in five
+// warpgroups, registers re-split between them with setmaxnreg:
 //
-//   warp 0      producer: cp.async.bulk (1-D TMA) of each tile's K codes, V
-//               codes and the four fp16 scale/bias runs into an NST-deep
-//               ring, completion counted by mbarrier transaction bytes.
-//   warp 1      MMA issuer (one thread): per tile the score MMAs
-//                 S[pos, n] = sum_k Kc[pos, k] * Qg[k, n]      (A: TMEM, B: smem)
-//               and, one tile behind, the combine MMAs
-//                 O[d, n'] = sum_pos Vc[d, pos] * P'[pos, n']  (A: TMEM, B: smem)
-//               every one a tcgen05.mma kind::f16 with M = 128, committed
-//               to mbarriers that release the operands and signal results.
-//   warps 2-5   K unpack: each warp's 16-byte reads of the raw K rows (four
-//               lanes per row, conflict-free) become exact fp16 values
-//               1024 + code, stored into tensor memory with 16x256b stores so
-//               that TMEM lane = position, the score MMA's A layout. Also
-//               the per-item Qg operand (each head's q restricted to one
-//               quantisation group, n = group * 8 + head).
-//   warps 6-9   V unpack: ldmatrix.trans reads 8x8 tiles of 16-bit code
-//               pairs across positions; each register becomes exact bf16
-//               128 + code of one dim at two positions, stored into tensor
-//               memory so that TMEM lane = dim, the combine's A layout.
-//   warps 10-13 softmax: thread = position of the tile (TMEM lane). It reads
-//               its scores, applies the factored dequant
+//   warpgroup 0 (32 registers): warp 0 producer, cp.async.bulk (1-D TMA) of
+//               each tile's K codes, V codes and the four fp16 scale/bias runs
+//               into an NST-deep ring (mbarrier transaction bytes); warp 1 the
+//               score MMA issuer, S[pos, n] = sum_k Kc[pos, k] Qg[k, n] (A in
+//               tensor memory, B = Qg in shared memory); warp 2 the combine
+//               MMA issuer, O[d, n'] = sum_pos Vc[d, pos] P'[pos, n'] (A in
+//               tensor memory, B = P' in shared memory); one thread each, every
+//               MMA a tcgen05.mma kind::f16 with M = 128. Warp 3 idles.
+//   warpgroup 1 K unpack: 16-byte reads of the raw K rows (four lanes per
+//               row, conflict-free) become exact fp16 1024 + code, stored to
+//               tensor memory with 16x256b stores (TMEM lane = position), with
+//               each position's scale/bias pairs in four spare columns; per
+//               item also the Qg operand (each head's q restricted to one
+//               quantisation group, n = group * 8 + head) and its per-group
+//               q sums.
+//   warpgroup 2 V unpack: ldmatrix.trans reads 8x8 tiles of 16-bit code pairs
+//               across positions; each register becomes exact bf16 128 + code
+//               of one dim at two positions (TMEM lane = dim).
+//   warpgroups 3 and 4 (128 registers) softmax, even and odd tiles: thread =
+//               position (TMEM lane). It reads its scores and scales, applies
 //                 score[h] = sum_g ks_g (S_gh - 1024 Qsum_gh) + kb_g Qsum_gh,
 //               the lazy online softmax (the reference point moves only when a
 //               score exceeds it by 2^8, decided by a warpgroup vote), and
 //               writes P' = p * v_scale as three bf16 parts (binary32-class,
 //               |error| <= 2^-23 |P'|) into the shared-memory B operand; the
-//               V-side bias term sum_pos p (b - 128 s) is summed in
-//               registers. The same thread then owns one dim of O: it reads
-//               that row of each tile's O from tensor memory (fresh per tile)
-//               and accumulates it in registers with the tile's rescale.
+//               V-side bias term sum_pos p (b - 128 s) is summed in registers.
+//               The same thread owns one dim of O: it reads that row of each
+//               of its tiles' O from tensor memory and accumulates it in
+//               registers. Each warpgroup keeps its own (O, m, l) over its
+//               tiles; the two are merged by log-sum-exp at the item's end.
 //
 // Every operand hand-off is an mbarrier with bounded waits; tensor memory
 // (512 columns) is allocated once per CTA and always freed. Precision: K-side
@@ -83,10 +84,19 @@ constexpr int ROWB = DH / 2;            // code bytes per row
 #define KVQ_TMEM_STAGES 6
 #endif
 constexpr int NST = KVQ_TMEM_STAGES;    // raw ring depth
-constexpr int WARPS = 15;
+constexpr int WARPS = 20;
 constexpr int THREADS = 32 * WARPS;
-constexpr int W_PROD = 0, W_MMA = 1, W_K = 2, W_V = 6, W_S = 10, W_MMA_C = 14;
-constexpr int SM_BAR = 1;               // named barrier of the softmax warpgroup
+constexpr int W_PROD = 0, W_MMA = 1, W_MMA_C = 2, W_K = 4, W_V = 8, W_S = 12;   // W_S: two warpgroups
+// Registers per thread: the launch's (every warp) and, after setmaxnreg, the
+// single-thread roles' and the softmax warpgroups'. 4*32*REG_LOW +
+// 8*32*REG_LAUNCH + 8*32*REG_SOFTMAX must not exceed THREADS * REG_LAUNCH,
+// and the host refuses to launch a build whose register count is not
+// REG_LAUNCH (a re-split over budget would wait forever).
+constexpr int REG_LAUNCH = 96, REG_LOW = 32, REG_SOFTMAX = 128;
+static_assert(4 * 32 * REG_LOW + 8 * 32 * REG_LAUNCH + 8 * 32 * REG_SOFTMAX <= THREADS * REG_LAUNCH,
+              "register re-split over the launch budget");
+constexpr int XCH_BAR = 3;              // named barrier of both softmax warpgroups (256 threads)
+constexpr int QRING = 4;                // per-item q-sum slots
 constexpr uint32_t TMEM_COLS = 512;
 
 template <int HT>
@@ -112,23 +122,29 @@ struct Cfg {
     static constexpr int VS = KB + TP * G * 2;
     static constexpr int VB = VS + TP * G * 2;
     static constexpr int STAGE = VB + TP * G * 2;
-    static constexpr int BP = NST * STAGE;             // P' [2]: bf16, MN-major core matrices
+    static constexpr int BP = NST * STAGE;             // P' [4]: bf16, MN-major core matrices
     static constexpr int BP_LBO = (N_O / 8) * 128;     // bytes between 8-position row blocks
     static constexpr int BP_BYTES = TP * N_O * 2;
-    static constexpr int BQ = BP + 2 * BP_BYTES;       // Qg [2]: fp16, K-major core matrices
+    static constexpr int BQ = BP + 4 * BP_BYTES;       // Qg [2]: fp16, K-major core matrices
     static constexpr int BQ_BYTES = N_S * DH * 2;
-    static constexpr int BAR = BQ + 2 * BQ_BYTES;
+    static constexpr int QS = BQ + 2 * BQ_BYTES;       // fp32 [QRING][G][8] per-group q sums
+    static constexpr int XCH = QS + QRING * G * 8 * 4; // fp32 [2][(128 + 2) * HT]: odd -> even warpgroup
+    static constexpr int XCH_FLOATS = (128 + 2) * HT;
+    static constexpr int BAR = XCH + 2 * XCH_FLOATS * 4;
     // raw_full[NST], raw_empty[NST], then [2] each of ak_full, av_full,
-    // s_full, s_empty, p_full, o_full, o_empty, and one drain barrier per issuer
-    static constexpr int NBAR = 2 * NST + 14 + 2;
+    // s_full, s_empty, p_full, o_full, o_empty, one drain barrier per issuer,
+    // and q_full[QRING]
+    static constexpr int NBAR = 2 * NST + 14 + 2 + QRING;
     static constexpr int MISC = BAR + NBAR * 8;
     static constexpr int TMEM_SLOT = MISC;             // uint32 TMEM base address
     static constexpr int ERR = MISC + 4;               // int, any role's failed wait
-    static constexpr int SERR = MISC + 8;              // int [2], the softmax warpgroup's own
-    static constexpr int RED = MISC + 16;              // fp32 reduction scratch
-    static constexpr int RED_FLOATS = 4 * HT * (1 + G + 1 + 1) + HT;
-    static constexpr int BYTES = RED + RED_FLOATS * 4 + 16;
-    static_assert(STAGE % 128 == 0 && BP % 1024 == 0 && BQ % 128 == 0, "alignment");
+    static constexpr int STALL = MISC + 8;             // int, a stall was reported
+    static constexpr int FLAGS = MISC + 16;            // int [2 warpgroups][2][4]: tile votes
+    static constexpr int RED = MISC + 80;              // fp32 [2 warpgroups][RED_FLOATS]
+    static constexpr int RED_FLOATS = 4 * HT * (1 + G + 1) + HT;
+    static constexpr int BYTES = RED + 2 * RED_FLOATS * 4 + 16;
+    static_assert(STAGE % 128 == 0 && BP % 1024 == 0 && BQ % 128 == 0 && QS % 16 == 0 &&
+                  XCH % 16 == 0 && BAR % 8 == 0 && FLAGS % 16 == 0, "alignment");
 };
 
 template <int HT>
@@ -159,6 +175,32 @@ __device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&v)[4]) {
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
                  : "r"(taddr));
 }
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Every wait of this kernel gives up after WAIT_NS of device time.
+constexpr uint64_t WAIT_NS = 1000000000ull;
+__device__ __forceinline__ bool twait(uint64_t* bar, uint32_t parity) {
+    if (mma4::mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    do {
+        if (mma4::mbar_try_wait(bar, parity)) return true;
+    } while (global_ns() - t0 < WAIT_NS);
+    return false;
+}
+// The first wait to give up (over all CTAs of the launches since load)
+// records where: {site, tile, CTA, 1}; the kernel's partials are poisoned with
+// NaN either way.
+__device__ unsigned int g_stall[4];
+__device__ __forceinline__ void report_stall(int* first, int site, uint32_t tile) {
+    if (atomicCAS(first, 0, 1) == 0 && atomicCAS(&g_stall[3], 0u, 1u) == 0u) {
+        g_stall[0] = (unsigned)site;
+        g_stall[1] = tile;
+        g_stall[2] = blockIdx.x;
+    }
+}
 // Bounded waits on up to three mbarrier phases at once. Every phase is tested
 // before any is waited on: a test of a phase that completed long ago still
 // takes a shared-memory round trip, and independent tests overlap.
@@ -168,8 +210,13 @@ __device__ __forceinline__ bool wait_all(uint64_t* b0, uint32_t p0, uint64_t* b1
     const bool d1 = b1 == nullptr || mma4::mbar_try_wait(b1, p1);
     const bool d2 = b2 == nullptr || mma4::mbar_try_wait(b2, p2);
     if (d0 && d1 && d2) return true;
-    return (d0 || mbar_wait(b0, p0)) && (d1 || mbar_wait(b1, p1)) && (d2 || mbar_wait(b2, p2));
+    return (d0 || twait(b0, p0)) && (d1 || twait(b1, p1)) && (d2 || twait(b2, p2));
 }
+// per-warpgroup register re-split (every thread of the warpgroup executes it)
+template <int N>
+__device__ __forceinline__ void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
@@ -271,7 +318,8 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
     uint64_t* raw_empty = bar + NST;
     // s_full[b] (scores of a tile done) also frees the tile's K operand and,
     // one item later, its Qg buffer; o_full[b] (combine done) also frees the
-    // tile's V operand and its P' buffer
+    // tile's V operand and its P' buffer. Buffer b of S, P' and O belongs to
+    // softmax warpgroup b (tiles of parity b).
     uint64_t* ak_full = bar + 2 * NST;
     uint64_t* av_full = ak_full + 2;
     uint64_t* s_full = ak_full + 4;
@@ -280,11 +328,13 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
     uint64_t* o_full = ak_full + 10;
     uint64_t* o_empty = ak_full + 12;
     uint64_t* drain = ak_full + 14;       // [2]: one per MMA issuer
+    uint64_t* q_full = ak_full + 16;      // [QRING]: an item's q sums are written
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::TMEM_SLOT);
     volatile int* err = reinterpret_cast<volatile int*>(smem + C::ERR);
-    volatile int* serr = reinterpret_cast<volatile int*>(smem + C::SERR);   // [2]
+    int* stall = reinterpret_cast<int*>(smem + C::STALL);
+    const float* qsums = reinterpret_cast<const float*>(smem + C::QS);
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, wg = warp >> 2;
 
     if (tid == 0) {
         for (int s = 0; s < NST; ++s) {
@@ -301,16 +351,18 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             mbar_init(&o_empty[b], 4);
             mbar_init(&drain[b], 1);
         }
+        for (int s = 0; s < QRING; ++s) mbar_init(&q_full[s], 4);
         *err = 0;
-        serr[0] = serr[1] = 0;
+        *stall = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (tid < 16) reinterpret_cast<int*>(smem + C::FLAGS)[tid] = 0;
     if (warp == W_MMA) {
         tmem_alloc(tmem_slot, TMEM_COLS);
         tmem_relinquish();
     }
     // P' columns past the (group, part, head) ones stay zero for the kernel's life
-    for (int i = tid; i < 2 * C::BP_BYTES / 16; i += THREADS)
+    for (int i = tid; i < 4 * C::BP_BYTES / 16; i += THREADS)
         reinterpret_cast<uint4*>(smem + C::BP)[i] = make_uint4(0u, 0u, 0u, 0u);
     fence_async_smem();
     tc_fence_before();
@@ -318,9 +370,10 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == W_PROD) {
-        // ------------------------------ producer ------------------------------
-        if (lane == 0) {
+    if (wg == 0) {
+        regs_dec<REG_LOW>();
+        if (warp == W_PROD && lane == 0) {
+            // ------------------------------ producer --------------------------
             const uint64_t pol = evict_first_policy();
             const unsigned char* kw = reinterpret_cast<const unsigned char*>(P.k_wq);
             const unsigned char* vw = reinterpret_cast<const unsigned char*>(P.v_wq);
@@ -333,7 +386,8 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 const Item it = item_of<HT>(P, idx);
                 for (int i = 0; i < it.n_tiles; ++i, ++gt) {
                     const uint32_t slot = gt % NST, round = gt / NST;
-                    if (gt >= NST && !mbar_wait(&raw_empty[slot], (round - 1) & 1)) {
+                    if (gt >= NST && !twait(&raw_empty[slot], (round - 1) & 1)) {
+                        report_stall(stall, 1, gt);
                         *err = 1;
                         break;
                     }
@@ -356,23 +410,22 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             const uint32_t issued = gt;
             for (uint32_t s = 0; s < NST && s < issued; ++s) {
                 const uint32_t last = ((issued - 1 - s) / NST) * NST + s;
-                (void)mbar_wait(&raw_full[s], (last / NST) & 1);
+                if (!twait(&raw_full[s], (last / NST) & 1)) report_stall(stall, 2, last);
             }
-        }
-    } else if (warp == W_MMA) {
-        // ------------------------- score MMA issuer ---------------------------
-        if (lane == 0) {
+        } else if (warp == W_MMA && lane == 0) {
+            // ------------------------- score MMA issuer -----------------------
             const uint32_t bq0 = s_addr(smem + C::BQ);
             uint32_t gt = 0, ni = 0;
             bool ok = true;
             for (uint32_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
                 const Item it = item_of<HT>(P, idx);
                 if (it.n_tiles == 0) continue;
-                // K-step s of the Qg operand starts 256 bytes (16 descriptor units) after s-1's
+                // K-step k of the Qg operand starts 256 bytes (16 descriptor units) after k-1's
                 const uint64_t qdesc = sdesc(bq0 + (ni & 1) * C::BQ_BYTES, 128, 2048);
                 for (int i = 0; i < it.n_tiles; ++i, ++gt) {
                     const uint32_t b = gt & 1, ph = (gt >> 1) & 1;
                     if (!wait_all(&ak_full[b], ph, gt >= 2 ? &s_empty[b] : nullptr, ph ^ 1)) {
+                        report_stall(stall, 3, gt);
                         ok = false;
                         break;
                     }
@@ -388,11 +441,9 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             if (!ok) *err = 1;
             // every MMA this thread issued has completed before tensor memory is freed
             umma_commit(&drain[0]);
-            (void)mbar_wait(&drain[0], 0);
-        }
-    } else if (warp == W_MMA_C) {
-        // ------------------------ combine MMA issuer --------------------------
-        if (lane == 0) {
+            if (!twait(&drain[0], 0)) report_stall(stall, 4, gt);
+        } else if (warp == W_MMA_C && lane == 0) {
+            // ------------------------ combine MMA issuer ----------------------
             const uint32_t bp0 = s_addr(smem + C::BP);
             uint32_t gt = 0;
             bool ok = true;
@@ -401,12 +452,15 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 for (int i = 0; i < it.n_tiles; ++i, ++gt) {
                     const uint32_t b = gt & 1, ph = (gt >> 1) & 1;
                     if (!wait_all(&av_full[b], ph, &p_full[b], ph, gt >= 2 ? &o_empty[b] : nullptr, ph ^ 1)) {
+                        report_stall(stall, 5, gt);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    // K-step s (16 positions) of P' starts two 8-position row blocks after s-1's
-                    const uint64_t pdesc = sdesc(bp0 + b * C::BP_BYTES, C::BP_LBO, 128);
+                    // P' of tile gt: the pair of warpgroup b, alternate tiles of it; K-step
+                    // k (16 positions) starts two 8-position row blocks after k-1's
+                    const uint32_t pb = 2 * b + ph;
+                    const uint64_t pdesc = sdesc(bp0 + pb * C::BP_BYTES, C::BP_LBO, 128);
                     const uint32_t d = tmem + C::O0 + C::N_O * b, a = tmem + C::AV0 + 64 * b;
 #pragma unroll
                     for (int k = 0; k < TP / 16; ++k)
@@ -417,9 +471,9 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             }
             if (!ok) *err = 1;
             umma_commit(&drain[1]);
-            (void)mbar_wait(&drain[1], 0);
+            if (!twait(&drain[1], 0)) report_stall(stall, 6, gt);
         }
-    } else if (warp >= W_K && warp < W_V) {
+    } else if (wg == 1) {
         // ------------------------------ K unpack ------------------------------
         const int q = warp & 3, r = lane >> 2, j = lane & 3;
         const int tq = (warp - W_K) * 32 + lane;               // 0..127
@@ -434,6 +488,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 // scores were computed: the K operand and, one item on, the Qg buffer are free)
                 if (!wait_all(&raw_full[slot], (gt / NST) & 1, gt >= 2 ? &s_empty[b] : nullptr,
                               ((gt >> 1) & 1) ^ 1)) {
+                    report_stall(stall, 7, gt);
                     ok = false;
                     break;
                 }
@@ -461,12 +516,33 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                             make_uint4(w[0], w[1], w[2], w[3]);
                     }
                     fence_async_smem();
+                    // the per-group q sums: lane group of 8 sums 64 dims of (g, h)
+                    {
+                        const int h = tq >> 4, g = (tq >> 3) & 1, part = tq & 7;
+                        float v = 0.0f;
+                        if (h < it.nh) {
+                            const uint4 u = *reinterpret_cast<const uint4*>(qrow + h * DH + g * 64 + part * 8);
+                            const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&uw[k]));
+                                v += f.x + f.y;
+                            }
+                        }
+                        v += __shfl_xor_sync(0xffffffffu, v, 1);
+                        v += __shfl_xor_sync(0xffffffffu, v, 2);
+                        v += __shfl_xor_sync(0xffffffffu, v, 4);
+                        if (part == 0)
+                            reinterpret_cast<float*>(smem + C::QS)[((ni % QRING) * G + g) * 8 + h] = v;
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&q_full[ni % QRING]);
                 }
                 const unsigned char* st = smem + slot * C::STAGE + C::KC;
-                uint32_t ra[32], rb[32];
+                const uint32_t col = tmem + C::AK0 + 64 * b;
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
-                    uint32_t (&dst)[32] = half ? rb : ra;
+                    uint32_t dst[32];
 #pragma unroll
                     for (int rr = 0; rr < 2; ++rr) {
                         const int p = 32 * q + 16 * half + 8 * rr + r;
@@ -476,21 +552,15 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                         for (int wi = 0; wi < 4; ++wi) {
                             const uint32_t w = ws[wi];
                             const uint32_t w8 = w >> 8;
-                            const uint32_t m0 = and_or<0x000F000Fu, 0x64006400u>(w);
-                            const uint32_t m1 = h2_hi_to_lo(and_or<0x00F000F0u, 0x64006400u>(w));
-                            const uint32_t m2 = and_or<0x000F000Fu, 0x64006400u>(w8);
-                            const uint32_t m3 = h2_hi_to_lo(and_or<0x00F000F0u, 0x64006400u>(w8));
                             // register m -> repetition 2wi + m/2, column offset m%2
-                            dst[4 * (2 * wi) + 2 * rr + 0] = m0;
-                            dst[4 * (2 * wi) + 2 * rr + 1] = m1;
-                            dst[4 * (2 * wi + 1) + 2 * rr + 0] = m2;
-                            dst[4 * (2 * wi + 1) + 2 * rr + 1] = m3;
+                            dst[4 * (2 * wi) + 2 * rr + 0] = and_or<0x000F000Fu, 0x64006400u>(w);
+                            dst[4 * (2 * wi) + 2 * rr + 1] = h2_hi_to_lo(and_or<0x00F000F0u, 0x64006400u>(w));
+                            dst[4 * (2 * wi + 1) + 2 * rr + 0] = and_or<0x000F000Fu, 0x64006400u>(w8);
+                            dst[4 * (2 * wi + 1) + 2 * rr + 1] = h2_hi_to_lo(and_or<0x00F000F0u, 0x64006400u>(w8));
                         }
                     }
+                    tmem_st_16x256b_x8(col + ((uint32_t)(32 * q + 16 * half) << 16), dst);
                 }
-                const uint32_t col = tmem + C::AK0 + 64 * b;
-                tmem_st_16x256b_x8(col + ((uint32_t)(32 * q) << 16), ra);
-                tmem_st_16x256b_x8(col + ((uint32_t)(32 * q + 16) << 16), rb);
                 // the rows' scale/bias pairs: lane j = 0 columns 0, 1 (k scale, k
                 // bias), j = 1 columns 2, 3 (v scale, v bias), j = 2, 3 unused
                 {
@@ -521,7 +591,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             ++ni;
         }
         if (!ok) *err = 1;
-    } else if (warp >= W_V && warp < W_S) {
+    } else if (wg == 2) {
         // ------------------------------ V unpack ------------------------------
         const int q = warp & 3;
         uint32_t gt = 0;
@@ -532,6 +602,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 const uint32_t slot = gt % NST, b = gt & 1;
                 if (!wait_all(&raw_full[slot], (gt / NST) & 1, gt >= 2 ? &o_full[b] : nullptr,
                               ((gt >> 1) & 1) ^ 1)) {
+                    report_stall(stall, 8, gt);
                     ok = false;
                     break;
                 }
@@ -539,24 +610,28 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 // lane L gives the row address of tile L/8: repetition pair
                 // member L/16, rows 8 (L/8 % 2) .. + 7, this warp's 16 bytes
                 const uint32_t vbase = s_addr(smem + slot * C::STAGE + C::VC) + 16 * q;
-                uint32_t ua[32], ub[32];
+                uint32_t x[4][4];
 #pragma unroll
                 for (int pr = 0; pr < 4; ++pr) {
                     const int pos = 16 * (2 * pr + (lane >> 4)) + 8 * ((lane >> 3) & 1) + (lane & 7);
-                    uint32_t x[4];
-                    ldsm_x4_trans(vbase + pos * ROWB, x);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int n = 2 * pr + (k >> 1), hh = k & 1;
-                        ua[4 * n + hh] = and_or<0x000F000Fu, 0x43004300u>(x[k]);
-                        ua[4 * n + 2 + hh] = and_or<0x000F000Fu, 0x43004300u>(x[k] >> 4);
-                        ub[4 * n + hh] = and_or<0x000F000Fu, 0x43004300u>(x[k] >> 8);
-                        ub[4 * n + 2 + hh] = and_or<0x000F000Fu, 0x43004300u>(x[k] >> 12);
-                    }
+                    ldsm_x4_trans(vbase + pos * ROWB, x[pr]);
                 }
                 const uint32_t col = tmem + C::AV0 + 64 * b;
-                tmem_st_16x256b_x8(col + ((uint32_t)(32 * q) << 16), ua);
-                tmem_st_16x256b_x8(col + ((uint32_t)(32 * q + 16) << 16), ub);
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    // half 0: dims 4u, 4u+1 (lanes r, r+8); half 1: dims 4u+2, 4u+3
+                    uint32_t u[32];
+#pragma unroll
+                    for (int pr = 0; pr < 4; ++pr)
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const int n = 2 * pr + (k >> 1), hh = k & 1;
+                            const uint32_t xv = half ? x[pr][k] >> 8 : x[pr][k];
+                            u[4 * n + hh] = and_or<0x000F000Fu, 0x43004300u>(xv);
+                            u[4 * n + 2 + hh] = and_or<0x000F000Fu, 0x43004300u>(xv >> 4);
+                        }
+                    tmem_st_16x256b_x8(col + ((uint32_t)(32 * q + 16 * half) << 16), u);
+                }
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
@@ -567,58 +642,56 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             }
         }
         if (!ok) *err = 1;
-    } else if (warp >= W_S && warp < W_S + 4) {
+    } else {
         // ------------------------------ softmax -------------------------------
+        regs_inc<REG_SOFTMAX>();
+        const int sp = wg - 3;                   // this warpgroup takes tiles of parity sp
+        const int bar_id = 1 + sp;
         const int q = warp & 3;
         const int p = 32 * q + lane;             // tile position = TMEM lane (scores)
         const int d = vdim(32 * q + lane);       // head dim = TMEM lane (O)
         const int gq = q >> 1;                   // group of that dim
         const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
         const int kp = vkpos(p);                 // this position's row of P'
-        float* red = reinterpret_cast<float*>(smem + C::RED);
+        int* flags = reinterpret_cast<int*>(smem + C::FLAGS) + 8 * sp;      // [2][4]
+        float* red = reinterpret_cast<float*>(smem + C::RED) + sp * C::RED_FLOATS;
         float* red_l = red;                      // [4][HT]
         float* red_b = red_l + 4 * HT;           // [4][G][HT]
-        float* red_q = red_b + 4 * G * HT;       // [4][HT]
-        float* red_m = red_q + 4 * HT;           // [4][HT]
+        float* red_m = red_b + 4 * G * HT;       // [4][HT]
         float* snew = red_m + 4 * HT;            // [HT]
         const size_t rows = (size_t)P.b_rows * P.n_heads;
-        uint32_t gt = 0;
-        uint32_t vc = 0;     // warpgroup checks so far: failures of check c go to serr[c % 2]
+        const uint32_t b = (uint32_t)sp;         // S, P' and O buffer of this warpgroup
+        uint32_t gt = 0, ni = 0, xi = 0;
+        uint32_t vc = 0;     // votes so far: vote c's words live in flags[c % 2]
         bool bad = false;
 
-        for (uint32_t idx = blockIdx.x; idx < n_items; idx += gridDim.x) {
+        for (uint32_t idx = blockIdx.x; idx < n_items; idx += gridDim.x, ++xi) {
             const Item it = item_of<HT>(P, idx);
-            const __half* qrow = static_cast<const __half*>(P.q) + ((size_t)it.b * P.n_heads + it.h0) * DH;
-            // per-group q sums of the item's heads
             float qs[G][HT];
-            {
-#pragma unroll
-                for (int h = 0; h < HT; ++h) {
-                    float v = h < it.nh ? __half2float(qrow[h * DH + 32 * q + lane]) : 0.0f;
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                    if (lane == 0) red_q[q * HT + h] = v;
-                }
-                named_sync(SM_BAR, 128);
+            bool q_ok = true;        // voted on with this warpgroup's first tile of the item
+            if (it.n_tiles > 0) {
+                const uint32_t qslot = ni % QRING;
+                q_ok = bad || twait(&q_full[qslot], (ni / QRING) & 1);
+                if (!q_ok) report_stall(stall, 9, gt);
 #pragma unroll
                 for (int g = 0; g < G; ++g)
 #pragma unroll
-                    for (int h = 0; h < HT; ++h) qs[g][h] = red_q[(2 * g) * HT + h] + red_q[(2 * g + 1) * HT + h];
+                    for (int h = 0; h < HT; ++h) qs[g][h] = qsums[(qslot * G + g) * 8 + h];
             }
-            float m_run[HT], l_part[HT], bsum[G][HT], o[HT], alpha_p1[HT], alpha_p2[HT];
+            float m_run[HT], l_part[HT], bsum[G][HT], o[HT], alpha_p1[HT];
 #pragma unroll
             for (int h = 0; h < HT; ++h) {
                 m_run[h] = -INFINITY;
                 l_part[h] = 0.0f;
                 o[h] = 0.0f;
-                alpha_p1[h] = alpha_p2[h] = 1.0f;
+                alpha_p1[h] = 1.0f;
 #pragma unroll
                 for (int g = 0; g < G; ++g) bsum[g][h] = 0.0f;
             }
-            // O of tile g2 (this thread's dim and group) into the registers:
-            // o = o * alpha + O_tile, alpha the reference-point move of that tile
-            auto accumulate = [&](uint32_t g2, const float (&alpha)[HT]) {
-                const uint32_t b = g2 & 1;
+            // O of this warpgroup's tile (this thread's dim and group) into the
+            // registers: o = o * alpha + O_tile, alpha the reference-point move
+            // of that tile
+            auto accumulate = [&](const float (&alpha)[HT]) {
                 const uint32_t col = tmem + C::O0 + C::N_O * b + C::GW * gq + lane_addr;
                 if constexpr (HT == 4) {
                     uint32_t v[16];
@@ -644,16 +717,19 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 if (lane == 0) mbar_arrive(&o_empty[b]);
             };
 
-            for (int i = 0; i < it.n_tiles && !bad; ++i, ++gt) {
-                const uint32_t b = gt & 1, ph = (gt >> 1) & 1;
-                // every wait of the tile first, then one warpgroup vote on the
-                // outcome (so every thread takes the same branches). O is taken
-                // two tiles behind: tile i-2's combine ran during tile i-1.
-                // o_full of tile gt-2: its O is ready and this P' buffer is free
-                const bool okw = wait_all(&s_full[b], ph, gt >= 2 ? &o_full[b] : nullptr, ph ^ 1);
-                if (!okw) serr[vc & 1] = 1;
+            const uint32_t gt0 = gt;
+            int last_i = -1;
+            bool okw_o = q_ok;       // the previous tile's wait for its O (voted on with this tile)
+            for (int i = (int)((sp - gt0) & 1); i < it.n_tiles && !bad; i += 2) {
+                const uint32_t g_ = gt0 + i, ph = (g_ >> 1) & 1;
+                // the tile's wait first, then one warpgroup vote on the outcome
+                // (so every thread takes the same branches). This tile's P'
+                // buffer was last read by the combine of tile g_-4, whose O this
+                // warpgroup has already taken.
+                const bool okw_s = twait(&s_full[b], ph);
+                if (!okw_s) report_stall(stall, 10, g_);
+                const bool okw = okw_s && okw_o;
                 tc_fence_after();
-                if (i >= 2) accumulate(gt - 2, alpha_p2);
 
                 // scores of position p, and its scales and biases
                 uint32_t xs[16], sv[4];
@@ -682,17 +758,26 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                     sc[h] = live ? a : -INFINITY;
                     grow |= sc[h] > m_run[h] + 8.0f;
                 }
-
-                const bool any_grow = consumers_any(grow);   // a barrier: serr[vc] is settled
-                if (serr[vc & 1]) {
+                // the warpgroup's vote: per warp (bit 0) some score outgrew its
+                // reference point, (bit 1) a wait of the tile failed; every
+                // thread reads all four words after the barrier
+                {
+                    const uint32_t wv = (__any_sync(0xffffffffu, grow) ? 1u : 0u) |
+                                        (__any_sync(0xffffffffu, !okw) ? 2u : 0u);
+                    if (lane == 0) flags[(vc & 1) * 4 + q] = (int)wv;
+                }
+                named_sync(bar_id, 128);
+                const int4 fl = *reinterpret_cast<const int4*>(flags + (vc & 1) * 4);
+                const int fv = fl.x | fl.y | fl.z | fl.w;
+                ++vc;
+                if (fv & 2) {
                     bad = true;
                     break;
                 }
-                ++vc;
                 float alpha[HT];
 #pragma unroll
                 for (int h = 0; h < HT; ++h) alpha[h] = 1.0f;
-                if (any_grow) {
+                if (fv & 1) {
 #pragma unroll
                     for (int h = 0; h < HT; ++h) {
                         float v = sc[h];
@@ -700,18 +785,18 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                         for (int o2 = 16; o2 > 0; o2 >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o2));
                         if (lane == 0) red_m[q * HT + h] = v;
                     }
-                    named_sync(SM_BAR, 128);
+                    named_sync(bar_id, 128);
 #pragma unroll
                     for (int h = 0; h < HT; ++h) {
                         const float v = fmaxf(fmaxf(red_m[h], red_m[HT + h]), fmaxf(red_m[2 * HT + h], red_m[3 * HT + h]));
                         const float m_new = v > m_run[h] + 8.0f ? v : m_run[h];
-                        alpha[h] = ex2(m_run[h] - m_new);    // 0 on the item's first tile
+                        alpha[h] = ex2(m_run[h] - m_new);    // 0 on the warpgroup's first tile
                         m_run[h] = m_new;
                         l_part[h] *= alpha[h];
 #pragma unroll
                         for (int g = 0; g < G; ++g) bsum[g][h] *= alpha[h];
                     }
-                    named_sync(SM_BAR, 128);                 // red_m is read by everyone
+                    named_sync(bar_id, 128);                 // red_m is read by everyone
                 }
                 float e[HT];
 #pragma unroll
@@ -724,7 +809,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 const float vsf[G] = {live ? vs2.x : 0.0f, live ? vs2.y : 0.0f};
                 const float vbf[G] = {live ? fmaf(vs2.x, -128.0f, vb2.x) : 0.0f,
                                       live ? fmaf(vs2.y, -128.0f, vb2.y) : 0.0f};
-                unsigned char* prow = smem + C::BP + b * C::BP_BYTES + (kp % 8) * 16 + (kp / 8) * C::BP_LBO;
+                unsigned char* prow = smem + C::BP + (2 * b + ph) * C::BP_BYTES + (kp % 8) * 16 + (kp / 8) * C::BP_LBO;
 #pragma unroll
                 for (int g = 0; g < G; ++g) {
                     uint32_t hi[HT / 2], mid[HT / 2], lo[HT / 2];
@@ -747,29 +832,42 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                     }
                 }
                 fence_async_smem();
+                // the O of this warpgroup's previous tile in the item (its combine
+                // ran during this tile's work), rescaled by that tile's move. Taken
+                // before this tile's P' is published: that combine has then
+                // consumed the previous p_full phase, so p_full never runs two
+                // phases ahead of the combine issuer's wait (which would alias)
+                if (i >= 2) {
+                    okw_o = twait(&o_full[b], ph ^ 1);
+                    if (!okw_o) report_stall(stall, 11, g_);
+                    tc_fence_after();
+                    accumulate(alpha_p1);
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[b]);
 #pragma unroll
-                for (int h = 0; h < HT; ++h) {
-                    alpha_p2[h] = alpha_p1[h];
-                    alpha_p1[h] = alpha[h];
-                }
+                for (int h = 0; h < HT; ++h) alpha_p1[h] = alpha[h];
+                last_i = i;
             }
-            // the item's last two O tiles
-            if (!bad && it.n_tiles > 0) {
-                const uint32_t last = gt - 1;
-                bool okw = mbar_wait(&o_full[last & 1], (last >> 1) & 1);
-                if (it.n_tiles >= 2) okw = okw && mbar_wait(&o_full[(last - 1) & 1], ((last - 1) >> 1) & 1);
-                if (!okw) serr[vc & 1] = 1;
+            gt = gt0 + (uint32_t)it.n_tiles;
+            if (it.n_tiles > 0) ++ni;
+            // this warpgroup's last O tile of the item
+            if (!bad && last_i >= 0) {
+                const uint32_t last = gt0 + (uint32_t)last_i;
+                const bool okw_l = twait(&o_full[b], (last >> 1) & 1);
+                if (!okw_l) report_stall(stall, 12, last);
+                const bool okw = okw_l && okw_o;
                 tc_fence_after();
-                if (it.n_tiles >= 2) accumulate(last - 1, alpha_p2);
-                accumulate(last, alpha_p1);
-                named_sync(SM_BAR, 128);
-                if (serr[vc & 1]) bad = true;
+                accumulate(alpha_p1);
+                const int wv = __any_sync(0xffffffffu, !okw) ? 2 : 0;
+                if (lane == 0) flags[(vc & 1) * 4 + q] = wv;
+                named_sync(bar_id, 128);
+                const int4 fl = *reinterpret_cast<const int4*>(flags + (vc & 1) * 4);
                 ++vc;
+                if ((fl.x | fl.y | fl.z | fl.w) & 2) bad = true;
             }
 
-            // ---- the item's partial: l and bias sums over the warpgroup ------
+            // ---- the warpgroup's (O, m, l): l and bias sums over its threads --
 #pragma unroll
             for (int h = 0; h < HT; ++h) {
                 float v = l_part[h];
@@ -784,7 +882,8 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                     if (lane == 0) red_b[(q * G + g) * HT + h] = u;
                 }
             }
-            if (it.with_new && q == 0) {
+            const __half* qrow = static_cast<const __half*>(P.q) + ((size_t)it.b * P.n_heads + it.h0) * DH;
+            if (sp == 0 && it.with_new && q == 0) {
                 const __half* nk = static_cast<const __half*>(P.new_k) + ((size_t)it.b * P.n_kv_heads + it.hk) * DH;
                 for (int h = 0; h < it.nh; ++h) {
                     float part = 0.0f;
@@ -794,34 +893,58 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                     if (lane == 0) snew[h] = part * scale2;
                 }
             }
-            named_sync(SM_BAR, 128);
-            const __half* nv = static_cast<const __half*>(P.new_v) + ((size_t)it.b * P.n_kv_heads + it.hk) * DH;
-            const float nvd = it.with_new ? __half2float(nv[d]) : 0.0f;
-            const bool poison = bad;
+            named_sync(bar_id, 128);
+            float lw[HT], ow[HT];
 #pragma unroll
             for (int h = 0; h < HT; ++h) {
-                if (h >= it.nh) break;
-                const float l = red_l[h] + red_l[HT + h] + red_l[2 * HT + h] + red_l[3 * HT + h];
-                const float bs = red_b[(0 * G + gq) * HT + h] + red_b[(1 * G + gq) * HT + h] +
-                                 red_b[(2 * G + gq) * HT + h] + red_b[(3 * G + gq) * HT + h];
-                float ov = o[h] + bs, lv = l, M = m_run[h];
-                if (it.with_new) {
-                    const float sn = snew[h];
-                    const float Mx = fmaxf(M, sn);
-                    const float er = M == -INFINITY ? 0.0f : ex2(M - Mx);
-                    const float en = ex2(sn - Mx);
-                    ov = fmaf(nvd, en, ov * er);
-                    lv = fmaf(lv, er, en);
-                    M = Mx;
-                }
-                const size_t row = it.split * rows + (size_t)it.b * P.n_heads + it.h0 + h;
-                part_o[row * DH + d] = poison ? __int_as_float(0x7fc00000) : ov;
-                if (d == 0) {
-                    part_m[row] = poison ? __int_as_float(0x7fc00000) : M * LN2;   // natural-log units
-                    part_l[row] = poison ? __int_as_float(0x7fc00000) : lv;
+                lw[h] = red_l[h] + red_l[HT + h] + red_l[2 * HT + h] + red_l[3 * HT + h];
+                ow[h] = o[h] + red_b[(0 * G + gq) * HT + h] + red_b[(1 * G + gq) * HT + h] +
+                        red_b[(2 * G + gq) * HT + h] + red_b[(3 * G + gq) * HT + h];
+            }
+            // ---- the odd tiles' warpgroup hands its (O, m, l) to the even one --
+            float* xch = reinterpret_cast<float*>(smem + C::XCH) + (xi & 1) * C::XCH_FLOATS;
+            const int tq = 32 * q + lane;
+            if (sp == 1) {
+#pragma unroll
+                for (int h = 0; h < HT; ++h) xch[2 * HT + tq * HT + h] = ow[h];
+                if (tq == 0)
+#pragma unroll
+                    for (int h = 0; h < HT; ++h) {
+                        xch[h] = m_run[h];
+                        xch[HT + h] = lw[h];
+                    }
+            }
+            if (sp == 1 && bad) *err = 1;
+            named_sync(XCH_BAR, 256);
+            if (sp == 0) {
+                const bool poison = bad || *err != 0;
+                const __half* nv = static_cast<const __half*>(P.new_v) + ((size_t)it.b * P.n_kv_heads + it.hk) * DH;
+                const float nvd = it.with_new ? __half2float(nv[d]) : 0.0f;
+#pragma unroll
+                for (int h = 0; h < HT; ++h) {
+                    if (h >= it.nh) break;
+                    const float m1 = xch[h], l1 = xch[HT + h], o1 = xch[2 * HT + tq * HT + h];
+                    float M = fmaxf(m_run[h], m1);
+                    const float w0 = m_run[h] == -INFINITY ? 0.0f : ex2(m_run[h] - M);
+                    const float w1 = m1 == -INFINITY ? 0.0f : ex2(m1 - M);
+                    float ov = fmaf(ow[h], w0, o1 * w1), lv = fmaf(lw[h], w0, l1 * w1);
+                    if (it.with_new) {
+                        const float sn = snew[h];
+                        const float Mx = fmaxf(M, sn);
+                        const float er = M == -INFINITY ? 0.0f : ex2(M - Mx);
+                        const float en = ex2(sn - Mx);
+                        ov = fmaf(nvd, en, ov * er);
+                        lv = fmaf(lv, er, en);
+                        M = Mx;
+                    }
+                    const size_t row = it.split * rows + (size_t)it.b * P.n_heads + it.h0 + h;
+                    part_o[row * DH + d] = poison ? __int_as_float(0x7fc00000) : ov;
+                    if (d == 0) {
+                        part_m[row] = poison ? __int_as_float(0x7fc00000) : M * LN2;   // natural-log units
+                        part_l[row] = poison ? __int_as_float(0x7fc00000) : lv;
+                    }
                 }
             }
-            named_sync(SM_BAR, 128);   // the reduction scratch is free again
         }
         if (bad) *err = 1;
     }

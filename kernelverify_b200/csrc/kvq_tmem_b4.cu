@@ -23,6 +23,13 @@ cudaError_t tmem_prepare() {
     e = cudaFuncSetAttribute(tmem4::decode_kernel<HT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)tmem4::smem_bytes<HT>());
     if (e != cudaSuccess) return e;
+    // the warpgroups re-split the registers the CTA launched with: a build
+    // whose per-thread count differs would make the softmax warpgroups' request
+    // wait forever, so it is never launched
+    cudaFuncAttributes fa{};
+    e = cudaFuncGetAttributes(&fa, tmem4::decode_kernel<HT>);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != tmem4::REG_LAUNCH) return cudaErrorInvalidConfiguration;
     done.fetch_or(bit, std::memory_order_acq_rel);
     return cudaSuccess;
 }
