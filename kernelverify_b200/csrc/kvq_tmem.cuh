@@ -96,24 +96,30 @@ constexpr int REG_LAUNCH = 96, REG_LOW = 32, REG_SOFTMAX = 128;
 static_assert(4 * 32 * REG_LOW + 8 * 32 * REG_LAUNCH + 8 * 32 * REG_SOFTMAX <= THREADS * REG_LAUNCH,
               "register re-split over the launch budget");
 constexpr int XCH_BAR = 3;              // named barrier of both softmax warpgroups (256 threads)
+// Buffer depths: K operands (with their scale columns), V operands, score
+// accumulators, Qg operands. Score MMAs run up to NAK tiles behind the K unpack
+// and NS tiles ahead of the softmax reads, the V unpack NAV tiles ahead of the
+// combine MMAs; Qg buffer i is reused NBQ items later.
+constexpr int NAK = 2, NAV = 3, NS = 4, NBQ = 3;
 constexpr int QRING = 4;                // per-item q-sum slots
 constexpr uint32_t TMEM_COLS = 512;
 
 template <int HT>
 struct Cfg {
     static_assert(HT == 4 || HT == 8, "head tile");
-    static constexpr int GW = HT == 4 ? 16 : 32;       // O columns per group: (part, head) + pad
+    // O columns per group, (part, head): HT = 4 pads 12 to 16, HT = 8 uses 24
+    static constexpr int GW = HT == 4 ? 16 : 24;
     static constexpr int N_O = G * GW;                 // combine N
     static constexpr int N_S = 16;                     // score N: group * 8 + head
     // tensor memory columns (lane = position for AK and S, lane = dim for AV and O)
-    static constexpr uint32_t AK0 = 0;                 // [2][64]
-    static constexpr uint32_t AV0 = 128;               // [2][64]
-    static constexpr uint32_t S0 = 256;                // [2][16]
-    static constexpr uint32_t O0 = 288;                // [2][N_O]
+    static constexpr uint32_t AK0 = 0;                 // [NAK][64]
+    static constexpr uint32_t AV0 = 64 * NAK;          // [NAV][64]
+    static constexpr uint32_t S0 = AV0 + 64 * NAV;     // [NS][16]
+    static constexpr uint32_t O0 = S0 + 16 * NS;       // [2][N_O]
     // [2][8]: a position's fp16x2 k_scale, k_bias, v_scale, v_bias (columns
     // 0..3), written beside its K operand so the softmax reads them with its scores
-    static constexpr uint32_t SC0 = O0 + 2 * N_O;
-    static_assert(SC0 + 16 <= TMEM_COLS, "tensor memory");
+    static constexpr uint32_t SC0 = O0 + 2 * N_O;      // [NAK][8]
+    static_assert(SC0 + 8 * NAK <= TMEM_COLS, "tensor memory");
     // shared memory
     static constexpr int KC = 0;                       // raw stage: K codes [TP][64]
     static constexpr int VC = KC + TP * ROWB;          //            V codes [TP][64]
@@ -125,17 +131,17 @@ struct Cfg {
     static constexpr int BP = NST * STAGE;             // P' [4]: bf16, MN-major core matrices
     static constexpr int BP_LBO = (N_O / 8) * 128;     // bytes between 8-position row blocks
     static constexpr int BP_BYTES = TP * N_O * 2;
-    static constexpr int BQ = BP + 4 * BP_BYTES;       // Qg [2]: fp16, K-major core matrices
+    static constexpr int BQ = BP + 4 * BP_BYTES;       // Qg [NBQ]: fp16, K-major core matrices
     static constexpr int BQ_BYTES = N_S * DH * 2;
-    static constexpr int QS = BQ + 2 * BQ_BYTES;       // fp32 [QRING][G][8] per-group q sums
+    static constexpr int QS = BQ + NBQ * BQ_BYTES;     // fp32 [QRING][G][8] per-group q sums
     static constexpr int XCH = QS + QRING * G * 8 * 4; // fp32 [2][(128 + 2) * HT]: odd -> even warpgroup
     static constexpr int XCH_FLOATS = (128 + 2) * HT;
     static constexpr int BAR = XCH + 2 * XCH_FLOATS * 4;
-    // raw_full[NST], raw_empty[NST], then [2] each of ak_full, av_full,
-    // s_full, s_empty, p_full, o_full, o_empty, one drain barrier per issuer,
-    // and q_full[QRING]
-    static constexpr int NBAR = 2 * NST + 14 + 2 + QRING;
-    static constexpr int MISC = BAR + NBAR * 8;
+    // raw_full[NST], raw_empty[NST], ak_full[NAK], s_full[NS], s_empty[NS],
+    // av_full[NAV], av_empty[NAV], [2] each of p_full, o_full, o_empty, one
+    // drain barrier per issuer, and q_full[QRING]
+    static constexpr int NBAR = 2 * NST + NAK + 2 * NS + 2 * NAV + 6 + 2 + QRING;
+    static constexpr int MISC = BAR + (NBAR * 8 + 15) / 16 * 16;
     static constexpr int TMEM_SLOT = MISC;             // uint32 TMEM base address
     static constexpr int ERR = MISC + 4;               // int, any role's failed wait
     static constexpr int STALL = MISC + 8;             // int, a stall was reported
@@ -170,6 +176,12 @@ __device__ __forceinline__ void tmem_st_16x256b_x1(uint32_t taddr, uint32_t v0, 
                  "r"(v1), "r"(v2), "r"(v3)
                  : "memory");
 }
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                   "=r"(v[7])
+                 : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&v)[4]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
@@ -182,11 +194,32 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 // Every wait of this kernel gives up after WAIT_NS of device time.
 constexpr uint64_t WAIT_NS = 1000000000ull;
+// A test that may suspend the thread (up to `hint_ns`) until the phase
+// completes, so a waiting warp sleeps instead of re-issuing tests that take
+// issue slots from the warps doing work on the same scheduler.
+__device__ __forceinline__ bool try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(mma4::s_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+// Roles with slack (the producer, the K and V unpack run tiles ahead) sleep in
+// their waits; the softmax and the MMA issuers, on the critical path, poll.
+constexpr uint32_t SLEEP_HINT_NS = 1000000;
+template <bool SLEEP = false>
 __device__ __forceinline__ bool twait(uint64_t* bar, uint32_t parity) {
-    if (mma4::mbar_try_wait(bar, parity)) return true;
+    const auto test = [&]() {
+        return SLEEP ? try_wait_sleep(bar, parity, SLEEP_HINT_NS) : mma4::mbar_try_wait(bar, parity);
+    };
+    if (test()) return true;
     const uint64_t t0 = global_ns();
     do {
-        if (mma4::mbar_try_wait(bar, parity)) return true;
+        if (test()) return true;
     } while (global_ns() - t0 < WAIT_NS);
     return false;
 }
@@ -204,13 +237,14 @@ __device__ __forceinline__ void report_stall(int* first, int site, uint32_t tile
 // Bounded waits on up to three mbarrier phases at once. Every phase is tested
 // before any is waited on: a test of a phase that completed long ago still
 // takes a shared-memory round trip, and independent tests overlap.
+template <bool SLEEP = false>
 __device__ __forceinline__ bool wait_all(uint64_t* b0, uint32_t p0, uint64_t* b1 = nullptr,
                                          uint32_t p1 = 0, uint64_t* b2 = nullptr, uint32_t p2 = 0) {
     const bool d0 = mma4::mbar_try_wait(b0, p0);
     const bool d1 = b1 == nullptr || mma4::mbar_try_wait(b1, p1);
     const bool d2 = b2 == nullptr || mma4::mbar_try_wait(b2, p2);
     if (d0 && d1 && d2) return true;
-    return (d0 || twait(b0, p0)) && (d1 || twait(b1, p1)) && (d2 || twait(b2, p2));
+    return (d0 || twait<SLEEP>(b0, p0)) && (d1 || twait<SLEEP>(b1, p1)) && (d2 || twait<SLEEP>(b2, p2));
 }
 // per-warpgroup register re-split (every thread of the warpgroup executes it)
 template <int N>
@@ -316,19 +350,23 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::BAR);
     uint64_t* raw_full = bar;
     uint64_t* raw_empty = bar + NST;
-    // s_full[b] (scores of a tile done) also frees the tile's K operand and,
-    // one item later, its Qg buffer; o_full[b] (combine done) also frees the
-    // tile's V operand and its P' buffer. Buffer b of S, P' and O belongs to
-    // softmax warpgroup b (tiles of parity b).
-    uint64_t* ak_full = bar + 2 * NST;
-    uint64_t* av_full = ak_full + 2;
-    uint64_t* s_full = ak_full + 4;
-    uint64_t* s_empty = ak_full + 6;
-    uint64_t* p_full = ak_full + 8;
-    uint64_t* o_full = ak_full + 10;
-    uint64_t* o_empty = ak_full + 12;
-    uint64_t* drain = ak_full + 14;       // [2]: one per MMA issuer
-    uint64_t* q_full = ak_full + 16;      // [QRING]: an item's q sums are written
+    // Tile gt's K operand and scale columns are buffer gt % NAK, its scores
+    // gt % NS, its V operand gt % NAV, its P' pair and O buffer gt % 2
+    // (softmax warpgroup gt % 2 takes the tile). s_empty (the softmax read a
+    // tile's scores and scales, so its scores were computed) frees the tile's
+    // K operand and, NBQ - 1 items on, its Qg buffer; av_empty (combine done)
+    // frees its V operand, o_full (the same) its P' buffer and O for the
+    // softmax warpgroup that owns it.
+    uint64_t* ak_full = bar + 2 * NST;    // [NAK]
+    uint64_t* s_full = ak_full + NAK;     // [NS]
+    uint64_t* s_empty = s_full + NS;      // [NS]
+    uint64_t* av_full = s_empty + NS;     // [NAV]
+    uint64_t* av_empty = av_full + NAV;   // [NAV]: a tile's combine has read its V operand
+    uint64_t* p_full = av_empty + NAV;    // [2]
+    uint64_t* o_full = p_full + 2;
+    uint64_t* o_empty = p_full + 4;
+    uint64_t* drain = p_full + 6;         // [2]: one per MMA issuer
+    uint64_t* q_full = p_full + 8;        // [QRING]: an item's q sums are written
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::TMEM_SLOT);
     volatile int* err = reinterpret_cast<volatile int*>(smem + C::ERR);
     int* stall = reinterpret_cast<int*>(smem + C::STALL);
@@ -341,11 +379,16 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             mbar_init(&raw_full[s], 1);
             mbar_init(&raw_empty[s], 8);           // every K and V unpack warp
         }
+        for (int i = 0; i < NAK; ++i) mbar_init(&ak_full[i], 4);
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_empty[i], 4);
+        }
+        for (int i = 0; i < NAV; ++i) {
+            mbar_init(&av_full[i], 4);
+            mbar_init(&av_empty[i], 1);
+        }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&ak_full[b], 4);
-            mbar_init(&av_full[b], 4);
-            mbar_init(&s_full[b], 1);
-            mbar_init(&s_empty[b], 4);
             mbar_init(&p_full[b], 4);
             mbar_init(&o_full[b], 1);
             mbar_init(&o_empty[b], 4);
@@ -386,7 +429,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 const Item it = item_of<HT>(P, idx);
                 for (int i = 0; i < it.n_tiles; ++i, ++gt) {
                     const uint32_t slot = gt % NST, round = gt / NST;
-                    if (gt >= NST && !twait(&raw_empty[slot], (round - 1) & 1)) {
+                    if (gt >= NST && !twait<true>(&raw_empty[slot], (round - 1) & 1)) {
                         report_stall(stall, 1, gt);
                         *err = 1;
                         break;
@@ -421,20 +464,21 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 const Item it = item_of<HT>(P, idx);
                 if (it.n_tiles == 0) continue;
                 // K-step k of the Qg operand starts 256 bytes (16 descriptor units) after k-1's
-                const uint64_t qdesc = sdesc(bq0 + (ni & 1) * C::BQ_BYTES, 128, 2048);
+                const uint64_t qdesc = sdesc(bq0 + (ni % NBQ) * C::BQ_BYTES, 128, 2048);
                 for (int i = 0; i < it.n_tiles; ++i, ++gt) {
-                    const uint32_t b = gt & 1, ph = (gt >> 1) & 1;
-                    if (!wait_all(&ak_full[b], ph, gt >= 2 ? &s_empty[b] : nullptr, ph ^ 1)) {
+                    const uint32_t ka = gt % NAK, sb = gt % NS;
+                    if (!wait_all(&ak_full[ka], (gt / NAK) & 1, gt >= NS ? &s_empty[sb] : nullptr,
+                                  ((gt / NS) & 1) ^ 1)) {
                         report_stall(stall, 3, gt);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d = tmem + C::S0 + 16 * b, a = tmem + C::AK0 + 64 * b;
+                    const uint32_t d = tmem + C::S0 + 16 * sb, a = tmem + C::AK0 + 64 * ka;
 #pragma unroll
                     for (int k = 0; k < DH / 16; ++k)
                         umma_ts(d, a + 8 * k, qdesc + 16 * k, ID_S, k > 0 ? 1u : 0u);
-                    umma_commit(&s_full[b]);
+                    umma_commit(&s_full[sb]);
                 }
                 ++ni;
             }
@@ -450,8 +494,9 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             for (uint32_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
                 const Item it = item_of<HT>(P, idx);
                 for (int i = 0; i < it.n_tiles; ++i, ++gt) {
-                    const uint32_t b = gt & 1, ph = (gt >> 1) & 1;
-                    if (!wait_all(&av_full[b], ph, &p_full[b], ph, gt >= 2 ? &o_empty[b] : nullptr, ph ^ 1)) {
+                    const uint32_t b = gt & 1, ph = (gt >> 1) & 1, va = gt % NAV;
+                    if (!wait_all(&av_full[va], (gt / NAV) & 1, &p_full[b], ph,
+                                  gt >= 2 ? &o_empty[b] : nullptr, ph ^ 1)) {
                         report_stall(stall, 5, gt);
                         ok = false;
                         break;
@@ -461,12 +506,13 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                     // k (16 positions) starts two 8-position row blocks after k-1's
                     const uint32_t pb = 2 * b + ph;
                     const uint64_t pdesc = sdesc(bp0 + pb * C::BP_BYTES, C::BP_LBO, 128);
-                    const uint32_t d = tmem + C::O0 + C::N_O * b, a = tmem + C::AV0 + 64 * b;
+                    const uint32_t d = tmem + C::O0 + C::N_O * b, a = tmem + C::AV0 + 64 * va;
 #pragma unroll
                     for (int k = 0; k < TP / 16; ++k)
                         umma_ts(d, a + 8 * k, pdesc + (uint64_t)((2 * C::BP_LBO) >> 4) * k, ID_V,
                                 k > 0 ? 1u : 0u);
                     umma_commit(&o_full[b]);
+                    umma_commit(&av_empty[va]);
                 }
             }
             if (!ok) *err = 1;
@@ -483,11 +529,13 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
             const Item it = item_of<HT>(P, idx);
             if (it.n_tiles == 0) continue;
             for (int i = 0; i < it.n_tiles; ++i, ++gt) {
-                const uint32_t slot = gt % NST, b = gt & 1;
-                // s_empty of tile gt-2: its scores and scales are read (so its
-                // scores were computed: the K operand and, one item on, the Qg buffer are free)
-                if (!wait_all(&raw_full[slot], (gt / NST) & 1, gt >= 2 ? &s_empty[b] : nullptr,
-                              ((gt >> 1) & 1) ^ 1)) {
+                const uint32_t slot = gt % NST, ka = gt % NAK;
+                // s_empty of tile gt - NAK: its scores and scales are read, so its
+                // scores were computed: the K operand is free, and the Qg buffer
+                // of NBQ items ago (every item has at least one tile)
+                const uint32_t old = gt - NAK;
+                if (!wait_all<true>(&raw_full[slot], (gt / NST) & 1, gt >= NAK ? &s_empty[old % NS] : nullptr,
+                              (old / NS) & 1)) {
                     report_stall(stall, 7, gt);
                     ok = false;
                     break;
@@ -497,7 +545,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                     // Qg of this item: column n = g * 8 + h holds q[h] on group
                     // g's dims and zero elsewhere, K-major core matrices
                     const __half* qrow = static_cast<const __half*>(P.q) + ((size_t)it.b * P.n_heads + it.h0) * DH;
-                    unsigned char* bq = smem + C::BQ + (ni & 1) * C::BQ_BYTES;
+                    unsigned char* bq = smem + C::BQ + (ni % NBQ) * C::BQ_BYTES;
 #pragma unroll
                     for (int c2 = 0; c2 < 2; ++c2) {
                         const int ci = tq + 128 * c2;                // 256 chunks of 8 fp16
@@ -539,7 +587,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                     if (lane == 0) mbar_arrive(&q_full[ni % QRING]);
                 }
                 const unsigned char* st = smem + slot * C::STAGE + C::KC;
-                const uint32_t col = tmem + C::AK0 + 64 * b;
+                const uint32_t col = tmem + C::AK0 + 64 * ka;
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     uint32_t dst[32];
@@ -576,7 +624,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                             b0 = *reinterpret_cast<const uint32_t*>(sb + p1 * 4);
                             b1 = *reinterpret_cast<const uint32_t*>(sb + d2 + p1 * 4);
                         }
-                        tmem_st_16x256b_x1(tmem + C::SC0 + 8 * b + ((uint32_t)(32 * q + 16 * half) << 16),
+                        tmem_st_16x256b_x1(tmem + C::SC0 + 8 * ka + ((uint32_t)(32 * q + 16 * half) << 16),
                                            a0, a1, b0, b1);
                     }
                 }
@@ -584,7 +632,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(&ak_full[b]);
+                    mbar_arrive(&ak_full[ka]);
                     mbar_arrive(&raw_empty[slot]);
                 }
             }
@@ -599,9 +647,10 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
         for (uint32_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
             const Item it = item_of<HT>(P, idx);
             for (int i = 0; i < it.n_tiles; ++i, ++gt) {
-                const uint32_t slot = gt % NST, b = gt & 1;
-                if (!wait_all(&raw_full[slot], (gt / NST) & 1, gt >= 2 ? &o_full[b] : nullptr,
-                              ((gt >> 1) & 1) ^ 1)) {
+                const uint32_t slot = gt % NST, va = gt % NAV;
+                // av_empty of tile gt - NAV: its combine has read this V operand
+                if (!wait_all<true>(&raw_full[slot], (gt / NST) & 1, gt >= NAV ? &av_empty[va] : nullptr,
+                              ((gt / NAV) & 1) ^ 1)) {
                     report_stall(stall, 8, gt);
                     ok = false;
                     break;
@@ -616,7 +665,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                     const int pos = 16 * (2 * pr + (lane >> 4)) + 8 * ((lane >> 3) & 1) + (lane & 7);
                     ldsm_x4_trans(vbase + pos * ROWB, x[pr]);
                 }
-                const uint32_t col = tmem + C::AV0 + 64 * b;
+                const uint32_t col = tmem + C::AV0 + 64 * va;
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     // half 0: dims 4u, 4u+1 (lanes r, r+8); half 1: dims 4u+2, 4u+3
@@ -636,7 +685,7 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(&av_full[b]);
+                    mbar_arrive(&av_full[va]);
                     mbar_arrive(&raw_empty[slot]);
                 }
             }
@@ -703,8 +752,9 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                                     __uint_as_float(v[h]) + __uint_as_float(v[HT + h]) +
                                         __uint_as_float(v[2 * HT + h]));
                 } else {
-                    uint32_t v[32];
-                    tmem_ld32(col, v);
+                    uint32_t v[24];
+                    tmem_ld16(col, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+                    tmem_ld8(col + 16, *reinterpret_cast<uint32_t(*)[8]>(&v[16]));
                     tmem_wait_ld();
 #pragma unroll
                     for (int h = 0; h < HT; ++h)
@@ -726,19 +776,20 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                 // (so every thread takes the same branches). This tile's P'
                 // buffer was last read by the combine of tile g_-4, whose O this
                 // warpgroup has already taken.
-                const bool okw_s = twait(&s_full[b], ph);
+                const uint32_t sb = g_ % NS;
+                const bool okw_s = twait(&s_full[sb], (g_ / NS) & 1);
                 if (!okw_s) report_stall(stall, 10, g_);
                 const bool okw = okw_s && okw_o;
                 tc_fence_after();
 
                 // scores of position p, and its scales and biases
                 uint32_t xs[16], sv[4];
-                tmem_ld16(tmem + C::S0 + 16 * b + lane_addr, xs);
-                tmem_ld4(tmem + C::SC0 + 8 * b + lane_addr, sv);
+                tmem_ld16(tmem + C::S0 + 16 * sb + lane_addr, xs);
+                tmem_ld4(tmem + C::SC0 + 8 * (g_ % NAK) + lane_addr, sv);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&s_empty[b]);
+                if (lane == 0) mbar_arrive(&s_empty[sb]);
                 const int nvalid = (int)min((uint32_t)TP, it.hi - (it.lo + i * TP));
                 const bool live = p < nvalid;
                 const float2 ks2 = __half22float2(*reinterpret_cast<const __half2*>(&sv[0]));
@@ -825,10 +876,10 @@ decode_kernel(Problem P, uint32_t n_items, float* __restrict__ part_o, float* __
                         *reinterpret_cast<uint4*>(prow + (2 * g) * 128) = make_uint4(hi[0], hi[1], mid[0], mid[1]);
                         *reinterpret_cast<uint4*>(prow + (2 * g + 1) * 128) = make_uint4(lo[0], lo[1], 0u, 0u);
                     } else {
-                        // columns 32g + (hi 0..7 | mid 8..15 | lo 16..23 | zero 24..31)
-                        *reinterpret_cast<uint4*>(prow + (4 * g) * 128) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                        *reinterpret_cast<uint4*>(prow + (4 * g + 1) * 128) = make_uint4(mid[0], mid[1], mid[2], mid[3]);
-                        *reinterpret_cast<uint4*>(prow + (4 * g + 2) * 128) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        // columns 24g + (hi 0..7 | mid 8..15 | lo 16..23)
+                        *reinterpret_cast<uint4*>(prow + (3 * g) * 128) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4*>(prow + (3 * g + 1) * 128) = make_uint4(mid[0], mid[1], mid[2], mid[3]);
+                        *reinterpret_cast<uint4*>(prow + (3 * g + 2) * 128) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                     }
                 }
                 fence_async_smem();
