@@ -9,8 +9,11 @@
  *
  * Every entry point takes plain device pointers, sizes and a CUDA stream
  * handle (a cudaStream_t passed as void*; NULL is the legacy default stream).
- * The library never allocates device memory: scratch space ("workspace") is
- * passed in, sized by kvq_workspace_bytes(). Calls are asynchronous on the
+ * The decode entry points never allocate device memory: scratch space
+ * ("workspace") is passed in, sized by kvq_workspace_bytes(). The one
+ * allocation the library makes is the sequence-split exchange region of
+ * kvq_peer_alloc() (cudaMalloc: it must be IPC-shareable with the peer ranks),
+ * made once at setup and released by kvq_peer_free(). Calls are asynchronous on the
  * given stream, reentrant, and return KVQ_OK or a negative status; the
  * message of the calling thread's last failure is kvq_last_error().
  * Nothing here aborts or traps.
@@ -265,8 +268,10 @@ int kvq_cache_append(const void* w, uint32_t b_rows, uint32_t n_kv_heads, uint32
  * bytes on every GPU that loads the library, held until the process exits.
  * Calls whose split partials need more (kvq_workspace_bytes(a) above the
  * limit) fail with KVQ_ERR_INVALID; use kvq_decode with a workspace instead.
- * The first call on a device looks up the buffer's device address for that
- * device; make that first call before any stream capture. Every call on a
+ * Each call looks up the buffer's device address for the current device (so a
+ * call after a device reset finds it where the reloaded library put it); the
+ * first call on a device also loads the library's device code there, so make
+ * that first call before any stream capture. Every call on a
  * device shares the one buffer: calls that overlap on the GPU (two streams,
  * two host threads) race on it and must be serialized by the caller. Nothing
  * in the buffer needs to start at zero: each call writes every partial it

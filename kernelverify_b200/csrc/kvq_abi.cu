@@ -8,7 +8,6 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
-#include <mutex>
 #include <string>
 
 #include "kvq_b200.h"
@@ -316,26 +315,18 @@ int check_merge(uint32_t n_parts, uint32_t rows, uint32_t head_dim, uint32_t out
 // Scratch for kvq_decode_noalloc: a file-scope device buffer, present on every
 // device that loads this library. Host code may not use its name as a device
 // address (on the host it is a stand-in), so the device address is looked up
-// once per device with cudaGetSymbolAddress, with that device current.
+// with cudaGetSymbolAddress, with the calling device current. It is looked up
+// on every call rather than cached: after a device reset the library's device
+// code is loaded again and the buffer's address may change, and the lookup of
+// an already loaded symbol is a cheap host-side query.
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) unsigned char g_noalloc_scratch[KVQ_NOALLOC_SCRATCH_BYTES];
 
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {};
-
 int noalloc_scratch(void** out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    if (dev < 0 || dev >= 64) return fail(KVQ_ERR_UNSUPPORTED, "device index %d out of range", dev);
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_ptr[dev] == nullptr) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress of the built-in scratch");
-        g_noalloc_ptr[dev] = p;
-    }
-    *out = g_noalloc_ptr[dev];
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress of the built-in scratch");
+    *out = p;
     return KVQ_OK;
 }
 

@@ -10,8 +10,8 @@ import pytest
 
 from oracle import battery, calibrate_k as ck, device_members as dm, kv
 
-# The independent-draw case the harness exhibits (oracle/K_CALIBRATION.md):
-# factored-serial needs K = 4.38 over the shipped four members there.
+# The independent-draw case the calibration harness exhibits: factored-serial
+# needs K = 4.38 over the shipped four members there.
 EXHIBIT = battery.Case(tuple(sorted({"B": 4, "BITS": 8, "DH": 64, "H": 2, "T": 512}.items())),
                        "float32", "corpus uniform[-10,10]", ck.INDEPENDENT_SEED_BASE + 256)
 
