@@ -205,7 +205,9 @@ int kvq_peer_free(void* region);
 int kvq_peer_merge(void* const* regions, uint32_t world, uint32_t rank, uint32_t parity,
                    uint32_t rows, uint32_t head_dim, uint32_t out_dtype, void* out,
                    uint64_t timeout_us, void* stream);
-/* status word of a region: 0 ok, 1 a peer's flag did not arrive in time */
+/* status word of a region: 0 ok, 1 a peer's flag did not arrive in time, 2 a
+ * merge named a parity other than its step's (nothing was published; the
+ * rows are NaN) */
 int kvq_peer_status(const void* region, uint32_t* status, void* stream);
 /* the calling thread's last error from a kvq_peer_* call ("" when none) */
 const char* kvq_peer_last_error(void);

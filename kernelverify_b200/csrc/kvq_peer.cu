@@ -12,14 +12,20 @@
 // l), double-buffered by step parity.
 //
 // Step e (the region's counter + 1) on rank r: the local partial has written
-// record e & 1; block 0 of the merge kernel fences (system scope) and stores e
-// into every peer's flag slot r; every block waits until its own flags from
-// every peer are >= e (then reads each once with acquire semantics), merges
-// the records of parity e & 1, and the last block sets the counter to e. A
-// peer can only overwrite the record of parity e & 1 at step e + 2, after its
-// merge of step e + 1 saw this rank's flag e + 1, which this rank stores only
-// after its merge of step e has finished: the double buffer is never
-// overwritten while read.
+// record e & 1; every block of the merge kernel fences (system scope) and
+// stores e into every peer's flag slot r -- the same value from every block,
+// so no block's wait depends on another block of this launch being scheduled
+// -- then waits until its own flags from every peer are >= e (then reads each
+// once with acquire semantics), merges the records of parity e & 1, and the
+// last block sets the counter to e. A peer can only overwrite the record of
+// parity e & 1 at step e + 2, after its merge of step e + 1 saw this rank's
+// flag e + 1, which this rank stores only after its merge of step e has
+// finished: the double buffer is never overwritten while read.
+//
+// The caller names the parity its partial wrote; when that is not e & 1 (the
+// caller's step count and the region's disagree) the kernel publishes
+// nothing, so no peer merges a record from the wrong slot: the status word
+// becomes 2, the rows NaN, and the counter still advances.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -34,6 +40,7 @@ namespace peer {
 
 constexpr int MAX_RANKS = KVQ_PEER_MAX_RANKS;
 constexpr uint32_t CTRL_EPOCH = 0, CTRL_DONE = 4, CTRL_STATUS = 8, FLAGS = 64, RECORDS = 256;
+constexpr uint32_t STATUS_TIMEOUT = 1, STATUS_PARITY = 2;
 constexpr int THREADS = 128;
 
 struct Regions {
@@ -73,17 +80,18 @@ peer_merge_kernel(Regions regions, uint32_t world, uint32_t rank, uint32_t parit
     if (tid == 0) {
         const uint32_t e = *reinterpret_cast<volatile uint32_t*>(self + CTRL_EPOCH) + 1;
         s_epoch = e;
+        const bool parity_ok = parity == (e & 1u);
         // this rank's record for step e is complete (the kernels before this
-        // one wrote it): block 0 publishes it to every peer, one system-scope
-        // fence ahead of the flag stores
-        if (blockIdx.x == 0) {
+        // one wrote it): every block publishes it to every peer, one
+        // system-scope fence ahead of the flag stores
+        if (parity_ok) {
             __threadfence_system();
             for (uint32_t p = 0; p < world; ++p)
                 st_relaxed_sys(reinterpret_cast<uint32_t*>(regions.r[p] + FLAGS + 4 * rank), e);
         }
         // every peer's record for step e (relaxed polling, then one acquiring
         // read per flag), or give up after timeout_ns
-        bool ok = true;
+        bool ok = parity_ok;
         const uint64_t t0 = globaltimer();
         for (uint32_t p = 0; p < world && ok; ++p) {
             const uint32_t* flag = reinterpret_cast<const uint32_t*>(self + FLAGS + 4 * p);
@@ -98,7 +106,9 @@ peer_merge_kernel(Regions regions, uint32_t world, uint32_t rank, uint32_t parit
             if (ok) (void)ld_acquire_sys(flag);
         }
         s_bad = ok ? 0 : 1;
-        if (!ok) atomicExch(reinterpret_cast<unsigned int*>(self + CTRL_STATUS), 1u);
+        if (!ok)
+            atomicExch(reinterpret_cast<unsigned int*>(self + CTRL_STATUS),
+                       parity_ok ? STATUS_TIMEOUT : STATUS_PARITY);
     }
     __syncthreads();
 

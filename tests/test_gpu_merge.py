@@ -177,3 +177,51 @@ def test_peer_merge_wait_runs_out_and_reports(native):
         torch.cuda.synchronize()
         for r in regions:
             _native.check_peer(lib.kvq_peer_free(r))
+
+
+def test_peer_merge_with_the_wrong_parity_publishes_nothing(native):
+    """A merge told the parity its step does not have (a fresh region is at
+    step 1, parity 1; the call says 0): nothing is published, the status word
+    is 2, the rows are NaN, and the step counter still advances, so the next
+    call at the right parity (step 2, parity 0) merges normally."""
+    import ctypes
+    import torch
+    from kernelverify_b200 import _native
+    lib = _native.lib()
+    rows, dh = 4, 128
+    nbytes = lib.kvq_peer_region_bytes(rows, dh)
+    ptr = ctypes.c_void_p()
+    handle = (ctypes.c_char * _native.KVQ_PEER_HANDLE_BYTES)()
+    _native.check_peer(lib.kvq_peer_alloc(nbytes, ctypes.byref(ptr), handle))
+    region = ptr.value
+    s = torch.cuda.current_stream().cuda_stream
+    try:
+        arr = (ctypes.c_void_p * 1)(region)
+        out = torch.zeros((rows, dh), dtype=torch.float32, device="cuda")
+        _native.check_peer(lib.kvq_peer_merge(arr, 1, 0, 0, rows, dh, _native.KVQ_F32, out.data_ptr(),
+                                              200_000, s))
+        torch.cuda.synchronize()
+        st = ctypes.c_uint32()
+        _native.check_peer(lib.kvq_peer_status(region, ctypes.byref(st), s))
+        assert st.value == 2
+        assert torch.isnan(out).all()
+        # step 2 has parity 0: its record (O = 1, m = 0, l = 2 in every row)
+        # merges to 0.5 everywhere
+        base = region + lib.kvq_peer_record_offset(rows, dh, 0)
+
+        class _Rec:    # the record's device memory as a torch view
+            __cuda_array_interface__ = {"shape": (rows * (dh + 2),), "typestr": "<f4",
+                                        "data": (base, False), "version": 3, "strides": None}
+
+        rec = torch.as_tensor(_Rec(), device="cuda")
+        rec[: rows * dh] = 1.0
+        rec[rows * dh: rows * dh + rows] = 0.0
+        rec[rows * dh + rows:] = 2.0
+        torch.cuda.synchronize()
+        _native.check_peer(lib.kvq_peer_merge(arr, 1, 0, 0, rows, dh, _native.KVQ_F32, out.data_ptr(),
+                                              200_000, s))
+        torch.cuda.synchronize()
+        assert torch.equal(out, torch.full_like(out, 0.5))
+    finally:
+        torch.cuda.synchronize()
+        _native.check_peer(lib.kvq_peer_free(region))
