@@ -47,7 +47,8 @@ extern "C" {
 #define KVQ_OK 0
 #define KVQ_ERR_INVALID (-1)     /* bad shape, bits, group, dtype, alignment or size  */
 #define KVQ_ERR_LAUNCH (-2)      /* a CUDA launch or configuration error              */
-#define KVQ_ERR_UNSUPPORTED (-3) /* no device, or not an sm_100 device                */
+#define KVQ_ERR_UNSUPPORTED (-3) /* no device, or not an sm_100 device; for
+                                    kvq_tsplit_decode also a format it does not serve */
 
 /* element type of q, new_k, new_v, out, scales and biases */
 #define KVQ_F16 0
@@ -207,10 +208,45 @@ int kvq_peer_merge(void* const* regions, uint32_t world, uint32_t rank, uint32_t
                    uint64_t timeout_us, void* stream);
 /* status word of a region: 0 ok, 1 a peer's flag did not arrive in time, 2 a
  * merge named a parity other than its step's (nothing was published; the
- * rows are NaN) */
+ * rows are NaN), 3 (kvq_tsplit_decode's regions) a unit's partials did not
+ * all arrive in time */
 int kvq_peer_status(const void* region, uint32_t* status, void* stream);
 /* the calling thread's last error from a kvq_peer_* call ("" when none) */
 const char* kvq_peer_last_error(void);
+
+/*
+ * The sequence split as ONE kernel per rank per step (no reference
+ * counterpart; the reference has no multi-GPU path -- this is its single-GPU
+ * door kernelverify/pack/kv_attention.py:369-393 with the cached positions
+ * sharded by T range over `world` GPUs). a describes this rank's shard
+ * (t_begin 0, t_end = t_cached = the shard's positions; has_new_entry on one
+ * rank only). The split stage's CTAs write their partials into this rank's
+ * region; the last CTAs of each unit merge them, store each head row's record
+ * into every rank's region, read every rank's record of the row from their
+ * own region (bounded by timeout_us, 0 = 2 s) and write the merged rows into
+ * out [b_rows * n_heads, head_dim] (fp16), identical on every rank. Every
+ * exchanged word carries the step number, so no fence or flag is involved.
+ * world 1 is the whole sequence on one GPU, a single launch.
+ *
+ * Regions: one per rank, kvq_tsplit_region_bytes(b_rows * n_heads, head_dim,
+ * world) bytes (0 for a head_dim other than 128), allocated zeroed and mapped
+ * exactly as for kvq_peer_merge (kvq_peer_alloc / kvq_peer_open /
+ * kvq_peer_close / kvq_peer_free); region_bytes is that size. The step count
+ * lives in the region, so a CUDA graph of one call replays every later step;
+ * every rank must run every step. Status word (kvq_peer_status): 0 ok, 1 a
+ * peer's record did not arrive in time (rows NaN), 3 a unit's partials did
+ * not all arrive in time (rows NaN; the region's step counts are out of step,
+ * so it must be freed and allocated again). No workspace: the partials live in
+ * the region (at most 64 splits per row; the split plan is capped to fit).
+ * Returns KVQ_ERR_UNSUPPORTED for a format or size this form does not serve
+ * (kvq_tsplit_supported says which, without a device): it serves the
+ * tensor-core kernel's 4-bit group-64 format, and geometries whose merging
+ * CTAs leave room for the rest on the device.
+ */
+size_t kvq_tsplit_region_bytes(uint32_t rows, uint32_t head_dim, uint32_t world);
+int kvq_tsplit_supported(const kvq_args* a);
+int kvq_tsplit_decode(const kvq_args* a, void* const* regions, size_t region_bytes, uint32_t world,
+                      uint32_t rank, void* out, uint64_t timeout_us, void* stream);
 
 /*
  * fp32 dequantized values [rows, head_dim] of a packed artefact: scale * code

@@ -28,7 +28,8 @@ EXPORTS = ("kvq_workspace_bytes", "kvq_decode", "kvq_decode_partial", "kvq_split
            "kvq_dequant", "kvq_quantize", "kvq_cache_append", "kvq_supports", "kvq_plan_kernel", "kvq_last_error", "kvq_abi_version",
            "kvq_peer_region_bytes", "kvq_peer_record_offset", "kvq_peer_alloc", "kvq_peer_open",
            "kvq_peer_close", "kvq_peer_free", "kvq_peer_merge", "kvq_peer_status",
-           "kvq_peer_last_error")
+           "kvq_peer_last_error", "kvq_tsplit_region_bytes", "kvq_tsplit_supported",
+           "kvq_tsplit_decode")
 
 
 class NativeUnavailable(RuntimeError):
@@ -92,6 +93,9 @@ def _declare(lib) -> None:
         "kvq_peer_merge": (I, [P, U32, U32, U32, U32, U32, U32, P, U64, P]),
         "kvq_peer_status": (I, [P, ctypes.POINTER(ctypes.c_uint32), P]),
         "kvq_peer_last_error": (ctypes.c_char_p, []),
+        "kvq_tsplit_region_bytes": (SZ, [U32, U32, U32]),
+        "kvq_tsplit_supported": (I, [AP]),
+        "kvq_tsplit_decode": (I, [AP, P, SZ, U32, U32, P, U64, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

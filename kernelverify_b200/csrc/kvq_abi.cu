@@ -616,4 +616,81 @@ int kvq_cache_append(const void* w, uint32_t b_rows, uint32_t n_kv_heads, uint32
     return quantize_rows(w, rows, head_dim, bits, group_size, dtype, wq, scales, biases, dst, stream);
 }
 
+// ---------------------------------------------------------------------------
+// The one-kernel sequence split (kvq_fused.cuh)
+// ---------------------------------------------------------------------------
+static bool tsplit_plan_ok(const kvq_args* a, const Plan& pl) {
+    return pl.kernel == KERNEL_MMA4 && a->bits == 4 && a->group_size == 64;
+}
+
+size_t kvq_tsplit_region_bytes(uint32_t rows, uint32_t head_dim, uint32_t world) {
+    if (rows == 0 || head_dim != kvq::fused::DH || world == 0 || world > KVQ_PEER_MAX_RANKS) return 0;
+    return (size_t)kvq::fused::region_layout(rows, world).total;
+}
+
+int kvq_tsplit_supported(const kvq_args* a) {
+    std::string keep = g_error;
+    Plan pl;
+    const int ok = plan(a, &pl) == KVQ_OK && tsplit_plan_ok(a, pl);
+    g_error = keep;
+    return ok;
+}
+
+int kvq_tsplit_decode(const kvq_args* a, void* const* regions, size_t region_bytes, uint32_t world,
+                      uint32_t rank, void* out, uint64_t timeout_us, void* stream) {
+    g_error.clear();
+    Plan pl;
+    int rc = plan(a, &pl);
+    if (rc) return rc;
+    if (!tsplit_plan_ok(a, pl))
+        return fail(KVQ_ERR_UNSUPPORTED, "the one-kernel sequence split serves the tensor-core "
+                    "kernel's 4-bit group-64 format (fp16, head_dim 128, at most 8 query heads "
+                    "per cache head, 8-row-aligned geometry); use kvq_decode_partial and "
+                    "kvq_peer_merge");
+    if (!regions || !out) return fail(KVQ_ERR_INVALID, "regions or out is NULL");
+    if (world == 0 || world > KVQ_PEER_MAX_RANKS || rank >= world)
+        return fail(KVQ_ERR_INVALID, "world must be 1..%d and rank < world", KVQ_PEER_MAX_RANKS);
+    for (uint32_t p = 0; p < world; ++p)
+        if (!regions[p] || !aligned(regions[p], 256))
+            return fail(KVQ_ERR_INVALID, "region %u is NULL or not 256-byte aligned", p);
+    if (!aligned(out, 8)) return fail(KVQ_ERR_INVALID, "out must be 8-byte aligned");
+    const kvq::fused::Layout L = kvq::fused::region_layout(pl.rows, world);
+    if (region_bytes < L.total)
+        return fail(KVQ_ERR_INVALID, "regions of %zu bytes are smaller than the %llu this step "
+                    "needs (kvq_tsplit_region_bytes)", region_bytes, (unsigned long long)L.total);
+    // the partials live in the region's store: at most part_rows / rows splits
+    const uint64_t cap = L.part_rows / pl.rows;
+    if (pl.P.n_splits > cap) {
+        const uint32_t end = a->t_end < a->t_cached ? a->t_end : a->t_cached;
+        const uint64_t span = end > a->t_begin ? end - a->t_begin : 0;
+        const uint64_t stage = (uint64_t)kvq::mma4_stage_positions();
+        const uint64_t chunk = ((span + cap - 1) / cap + stage - 1) / stage * stage;
+        pl.P.chunk = (uint32_t)chunk;
+        pl.P.n_splits = (uint32_t)((span + chunk - 1) / chunk);
+    }
+    rc = device_ok();
+    if (rc) return rc;
+    // the merging CTAs wait for the rest of their unit: they must leave room
+    // on the device for every other CTA
+    const uint64_t units = (uint64_t)a->b_rows * a->n_kv_heads * pl.P.head_tiles;
+    const uint64_t kmax = 2ull * (uint32_t)pl.ht;   // merging CTAs per unit: two per head row
+    const uint64_t k = pl.P.n_splits < kmax ? pl.P.n_splits : kmax;
+    const uint64_t resident = (uint64_t)kvq::mma4_fused_ctas_per_sm(pl.ht) * kvq::sm_count();
+    if (units * k >= resident)
+        return fail(KVQ_ERR_UNSUPPORTED, "%llu units x %llu merging CTAs would fill the %llu "
+                    "resident CTAs; use kvq_decode_partial and kvq_peer_merge",
+                    (unsigned long long)units, (unsigned long long)k, (unsigned long long)resident);
+    kvq::fused::Fused F{};
+    for (uint32_t p = 0; p < world; ++p) F.region[p] = static_cast<unsigned char*>(regions[p]);
+    F.world = world;
+    F.rank = rank;
+    F.L = L;
+    F.timeout_ns = (timeout_us ? timeout_us : 2000000ull) * 1000ull;
+    F.out = static_cast<__half*>(out);
+    cudaError_t e = kvq::launch_mma4_fused(pl.P, pl.ht, fast_precision() ? 2 : 3, F,
+                                           static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "one-kernel sequence split launch");
+    return KVQ_OK;
+}
+
 }  // extern "C"

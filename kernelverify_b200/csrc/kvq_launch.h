@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include "kvq_common.cuh"
+#include "kvq_fused.cuh"
 
 namespace kvq {
 
@@ -32,6 +33,15 @@ cudaError_t launch_dequant(const uint32_t* wq, const void* scales, const void* b
 // precision)
 cudaError_t launch_mma4(const Problem& P, int ht, int group, int bits, int parts, float* part_o,
                         float* part_m, float* part_l, cudaStream_t stream);
+
+// The one-kernel sequence split (kvq_fused.cuh): the 4-bit group-64 split
+// stage with the merge, the exchange over the ranks' regions and the final
+// merge in its tail; its partials in the region's store, fp16 out through
+// F.out. ht in {4, 8}, parts 2 or 3. And its resident CTAs per SM (0 when the
+// device cannot be queried).
+cudaError_t launch_mma4_fused(const Problem& P, int ht, int parts, const fused::Fused& F,
+                              cudaStream_t stream);
+int mma4_fused_ctas_per_sm(int ht);
 
 // Merges of n_parts partials; part p's O block starts o_stride floats after
 // part p-1's, its m and l ml_stride floats after (stacked partials:

@@ -334,12 +334,18 @@ __device__ __forceinline__ void produce(const Problem& P, unsigned char* smem, u
 // sums) -- plus the step's own entry when `with_new`; written as (O, m in
 // natural-log units, l) rows of split `split`, NaN when `bad`. Every consumer
 // thread calls it after the merge area is complete.
-template <int HT, int GROUP>
+// TAGGED: the partial goes out as 8-byte words, the value's bits in the low
+// half and `tag` in the high half, row r of split s at
+// tagged[(s * rows + r) * (DH + 2)]: O [DH], then m, then l -- each word
+// stored whole (a relaxed 64-bit store), so a reader that finds the tag knows
+// that word is this step's without any fence (kvq_fused.cuh).
+template <int HT, int GROUP, bool TAGGED = false>
 __device__ __forceinline__ void finish_partial(const Problem& P, unsigned char* smem, int tid, int warp,
                                                int lane, uint32_t split, uint32_t b, uint32_t hk,
                                                uint32_t h0, int nh, bool with_new, float scale2,
                                                const int* err_flag, float* __restrict__ part_o,
-                                               float* __restrict__ part_m, float* __restrict__ part_l) {
+                                               float* __restrict__ part_m, float* __restrict__ part_l,
+                                               uint64_t* __restrict__ tagged = nullptr, uint32_t tag = 0) {
     constexpr int G = DH / GROUP;
     constexpr float LN2 = 0.6931471805599453f;
     const uint32_t H = P.n_heads;
@@ -384,10 +390,23 @@ __device__ __forceinline__ void finish_partial(const Problem& P, unsigned char* 
             l += e;
         }
         const size_t row = split * rows + (size_t)b * H + h0 + h;
-        part_o[row * DH + d] = bad ? __int_as_float(0x7fc00000) : o;
-        if (d == 0) {
-            part_m[row] = bad ? __int_as_float(0x7fc00000) : M * LN2;  // natural-log units
-            part_l[row] = bad ? __int_as_float(0x7fc00000) : l;
+        if constexpr (TAGGED) {
+            uint64_t* w = tagged + row * (DH + 2);
+            const uint64_t hi = (uint64_t)tag << 32;
+            const auto word = [&](float v) { return hi | __float_as_uint(bad ? __int_as_float(0x7fc00000) : v); };
+            // no compiler barrier: nothing else this thread does is ordered
+            // against these words (the tags carry their validity)
+            asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(w + d), "l"(word(o)));
+            if (d == 0) {
+                asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(w + DH), "l"(word(M * LN2)),
+                             "l"(word(l)));
+            }
+        } else {
+            part_o[row * DH + d] = bad ? __int_as_float(0x7fc00000) : o;
+            if (d == 0) {
+                part_m[row] = bad ? __int_as_float(0x7fc00000) : M * LN2;  // natural-log units
+                part_l[row] = bad ? __int_as_float(0x7fc00000) : l;
+            }
         }
     }
 }

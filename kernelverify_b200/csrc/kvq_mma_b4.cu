@@ -169,4 +169,53 @@ cudaError_t launch_mma4(const Problem& P, int ht, int group, int bits, int parts
                       : launch_parts<3>(P, ht, group, bits, o, m, l, stream);
 }
 
+// ---- the one-kernel sequence split (4-bit, group 64) ----------------------
+template <int HT, int PARTS>
+static cudaError_t fused_prepare() {
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev >= 0 && dev < kMaxDevices ? 1ull << dev : 0;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(mma4::partial_kernel_tf<HT, PARTS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)mma4::smem_bytes<64, 4>());
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(mma4::partial_kernel_tf<HT, PARTS>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+    return cudaSuccess;
+}
+
+template <int HT, int PARTS>
+static cudaError_t fused_one(const Problem& P, const fused::Fused& F, cudaStream_t stream) {
+    cudaError_t e = fused_prepare<HT, PARTS>();
+    if (e != cudaSuccess) return e;
+    dim3 grid(P.n_splits, P.n_kv_heads * P.head_tiles, P.b_rows);
+    mma4::partial_kernel_tf<HT, PARTS><<<grid, mma4::THREADS, mma4::smem_bytes<64, 4>(), stream>>>(P, F);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mma4_fused(const Problem& P, int ht, int parts, const fused::Fused& F,
+                              cudaStream_t stream) {
+    if (ht == 4) return parts == 2 ? fused_one<4, 2>(P, F, stream) : fused_one<4, 3>(P, F, stream);
+    if (ht == 8) return parts == 2 ? fused_one<8, 2>(P, F, stream) : fused_one<8, 3>(P, F, stream);
+    return cudaErrorInvalidValue;
+}
+
+int mma4_fused_ctas_per_sm(int ht) {
+    int n = 0;
+    cudaError_t e = ht == 4 ? fused_prepare<4, 3>() : fused_prepare<8, 3>();
+    if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &n, ht == 4 ? mma4::partial_kernel_tf<4, 3> : mma4::partial_kernel_tf<8, 3>, mma4::THREADS,
+            mma4::smem_bytes<64, 4>());
+    if (e != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
 }  // namespace kvq

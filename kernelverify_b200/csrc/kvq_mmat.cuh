@@ -18,6 +18,7 @@
 // lane (., j) -- the rows the combine's A fragments are built from.
 #pragma once
 
+#include "kvq_fused.cuh"
 #include "kvq_mma.cuh"
 
 namespace kvq {
@@ -31,10 +32,12 @@ __device__ __forceinline__ uint32_t transpose8x8(uint32_t x) {
     return y;
 }
 
-template <int HT, int PARTS>
-__global__ void __launch_bounds__(THREADS, KVQ_MMA_MINBLOCKS)
-partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part_m,
-                 float* __restrict__ part_l) {
+// The split stage's CTA: its split's partial into part_* [n_splits, rows(, DH)],
+// or with TAGGED as tagged words into `tagged` (finish_partial).
+template <int HT, int PARTS, bool TAGGED = false>
+__device__ __forceinline__ void partial_t_body(const Problem& P, float* __restrict__ part_o,
+                                               float* __restrict__ part_m, float* __restrict__ part_l,
+                                               uint64_t* __restrict__ tagged = nullptr, uint32_t tag = 0) {
     constexpr int GROUP = 64;
     using Lay = Layout<GROUP>;
     constexpr int G = Lay::G;
@@ -455,8 +458,8 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
                 mo[(warp * 8 + c1) * DH + dlo + 1] = oacc[i][3];
             }
         }
-        finish_partial<HT, GROUP>(P, smem, tid, warp, lane, split, b, hk, h0, nh, with_new, scale2,
-                                  err_flag, part_o, part_m, part_l);
+        finish_partial<HT, GROUP, TAGGED>(P, smem, tid, warp, lane, split, b, hk, h0, nh, with_new,
+                                          scale2, err_flag, part_o, part_m, part_l, tagged, tag);
     }
     __syncthreads();
     if (tid == CWARPS * 32 && *(volatile int*)err_flag) {
@@ -465,6 +468,30 @@ partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part
             (void)mbar_wait(&full[s], (last / STAGES) & 1);
         }
     }
+}
+
+template <int HT, int PARTS>
+__global__ void __launch_bounds__(THREADS, KVQ_MMA_MINBLOCKS)
+partial_kernel_t(Problem P, float* __restrict__ part_o, float* __restrict__ part_m,
+                 float* __restrict__ part_l) {
+    partial_t_body<HT, PARTS>(P, part_o, part_m, part_l);
+}
+
+// The whole sequence-split step in one launch: the split stage with its
+// partial tagged into the region's store, then the merge of the unit's
+// splits, the exchange of the ranks' records and the final merge by the
+// unit's last CTAs (kvq_fused.cuh).
+template <int HT, int PARTS>
+__global__ void __launch_bounds__(THREADS, KVQ_MMA_MINBLOCKS)
+partial_kernel_tf(Problem P, const __grid_constant__ fused::Fused F) {
+    static_assert(THREADS == fused::TAIL_THREADS, "the tail is written for the split stage's CTA size");
+    // this step's number: the unit's count in the region + 1 (every CTA of
+    // the unit reads it before it writes anything tagged with it)
+    const uint32_t unit = blockIdx.z * gridDim.y + blockIdx.y;
+    const uint32_t e = fused::ld_relaxed_gpu(fused::epoch_word(F, unit)) + 1u;
+    partial_t_body<HT, PARTS, true>(P, nullptr, nullptr, nullptr, fused::partials(F), e);
+    extern __shared__ __align__(128) unsigned char smem_tail[];
+    fused::tail<HT>(P, F, e, smem_tail);
 }
 
 }  // namespace mma4

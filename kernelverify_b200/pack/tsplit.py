@@ -12,12 +12,17 @@ and every rank merges them with `kvq_lse_merge`:
 
 Batch x KV-head work is never split across ranks; only T is.
 
-Two transports move the partials. "nccl": one all_gather_into_tensor of the
-ranks' fp32 records (O, m, l) and kvq_lse_merge_records. "peer": every rank's
-record stays in an exchange region in its own GPU memory, mapped into the
-peers over CUDA IPC, and kvq_peer_merge publishes, waits (bounded) and merges
-in one kernel reading the peers' records over NVLink -- no collective, so a
-whole step can be captured in a CUDA graph.
+Three transports move the partials. "nccl": one all_gather_into_tensor of
+the ranks' fp32 records (O, m, l) and kvq_lse_merge_records. "peer": every
+rank's record stays in an exchange region in its own GPU memory, mapped into
+the peers over CUDA IPC, and kvq_peer_merge publishes, waits (bounded) and
+merges in one kernel reading the peers' records over NVLink -- no collective,
+so a whole step can be captured in a CUDA graph. "fused": the whole step is
+ONE kernel per rank (kvq_tsplit_decode): the split stage's last CTAs of each
+cache head merge its splits, store each head row's record into every rank's
+region, and once every rank's record of the row is there (each word carries
+the step number; the wait is bounded) merge the records into the output --
+for the tensor-core kernel's 4-bit group-64 format.
 """
 
 from __future__ import annotations
@@ -52,7 +57,8 @@ class PeerExchange:
     every peer's, mapped over CUDA IPC. Create it on every rank of `group`
     together; close() it on every rank together."""
 
-    def __init__(self, rows: int, head_dim: int, device, group=None, timeout_us: int = 2_000_000):
+    def __init__(self, rows: int, head_dim: int, device, group=None, timeout_us: int = 2_000_000,
+                 layout: str = "peer"):
         import torch
         from kernelverify_b200 import _native
         lib = _native.lib()
@@ -63,7 +69,12 @@ class PeerExchange:
         if self.world > _native.KVQ_PEER_MAX_RANKS:
             raise ValueError(f"the peer transport serves at most {_native.KVQ_PEER_MAX_RANKS} ranks")
         self.device = torch.device(device)
-        self.nbytes = lib.kvq_peer_region_bytes(rows, head_dim)
+        # "peer": kvq_peer_merge's layout; "fused": kvq_tsplit_decode's
+        self.layout = layout
+        self.nbytes = (lib.kvq_peer_region_bytes(rows, head_dim) if layout == "peer"
+                       else lib.kvq_tsplit_region_bytes(rows, head_dim, self.world))
+        if not self.nbytes:
+            raise ValueError(f"no {layout} region for {rows} rows of head_dim {head_dim}")
         handle = (ctypes.c_char * _native.KVQ_PEER_HANDLE_BYTES)()
         own = ctypes.c_void_p()
         with torch.cuda.device(self.device):
@@ -107,7 +118,9 @@ class PeerExchange:
             _dtype_code(out.dtype), out.data_ptr(), self.timeout_us, s.cuda_stream))
 
     def status(self) -> int:
-        """0, or 1 when a peer's flag did not arrive in time."""
+        """0; 1 when a peer's flag (or record) did not arrive in time; 2
+        (peer layout) a merge named the wrong parity; 3 (fused layout) a
+        unit's partials did not all arrive in time."""
         import torch
         from kernelverify_b200 import _native
         v = ctypes.c_uint32()
@@ -157,8 +170,9 @@ class SequenceSplitDecoder:
     `group` is a torch.distributed process group (None: a single rank). The
     local cache tensors hold only this rank's rows ([HKV, T_local, ...] or
     [B, HKV, T_local, ...]); positions are local to them. `transport` is
-    "nccl" (one all-gather of fp32 records, then kvq_lse_merge_records) or
-    "peer" (kvq_peer_merge over the ranks' exchange regions).
+    "nccl" (one all-gather of fp32 records, then kvq_lse_merge_records),
+    "peer" (kvq_peer_merge over the ranks' exchange regions) or "fused" (the
+    whole step as one kvq_tsplit_decode launch per rank, one rank included).
     """
 
     b_rows: int
@@ -172,15 +186,16 @@ class SequenceSplitDecoder:
     def __post_init__(self):
         import torch
         from kernelverify_b200.pack.kv_attention import Workspace, record_floats, record_views
-        if self.transport not in ("nccl", "peer"):
-            raise ValueError(f"transport {self.transport!r} is not 'nccl' or 'peer'")
+        if self.transport not in ("nccl", "peer", "fused"):
+            raise ValueError(f"transport {self.transport!r} is not 'nccl', 'peer' or 'fused'")
         self.world = 1 if self.group is None else torch.distributed.get_world_size(self.group)
         self.rank = 0 if self.group is None else torch.distributed.get_rank(self.group)
         rows = self.b_rows * self.n_heads
         self.workspace = Workspace()
         self._dtype = None
-        if self.transport == "peer":
-            self.exchange = PeerExchange(rows, self.head_dim, self.device, self.group)
+        if self.transport in ("peer", "fused"):
+            self.exchange = PeerExchange(rows, self.head_dim, self.device, self.group,
+                                         layout=self.transport)
             return
         n = record_floats(rows, self.head_dim)
         self.records = torch.empty((self.world, n), dtype=torch.float32, device=self.device)
@@ -231,10 +246,36 @@ class SequenceSplitDecoder:
         return kva.lse_merge_records(self.records, self.b_rows, self.n_heads, self.head_dim,
                                      out_dtype, out=out)
 
+    def fused(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
+              bits: int, t_local: int, out=None):
+        """The step as one kvq_tsplit_decode launch on this rank."""
+        import torch
+        from kernelverify_b200 import _native
+        from kernelverify_b200.pack import kv_attention as kva
+        if out is None:
+            out = torch.empty((self.b_rows, self.n_heads, self.head_dim), dtype=q.dtype,
+                              device=self.device)
+        kva._check_buffers(self.device, ("out", out, (self.b_rows, self.n_heads, self.head_dim),
+                                         q.dtype))
+        a = kva._args(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
+                      bits=bits, t_cached=t_local, t_begin=0, t_end=t_local,
+                      has_new_entry=owns_new_entry(self.world, self.rank))
+        ex = self.exchange
+        _native.check(_native.lib().kvq_tsplit_decode(
+            a, ex._array, ex.nbytes, self.world, self.rank, out.data_ptr(), ex.timeout_us,
+            torch.cuda.current_stream(q.device).cuda_stream))
+        return out
+
     def step(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
              bits: int, t_local: int, out=None):
         """out [B, H, DH] in q's dtype, identical on every rank. On a single
-        rank the split is the whole sequence: one kvq_decode."""
+        rank the split is the whole sequence: one kvq_decode (or, with the
+        fused transport, one kvq_tsplit_decode)."""
+        if self.transport == "fused":
+            res = self.fused(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
+                             bits=bits, t_local=t_local, out=out)
+            self.steps += 1
+            return res
         if self.world == 1:
             from kernelverify_b200.pack import kv_attention as kva
             res = kva.decode(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v,
@@ -250,16 +291,17 @@ class SequenceSplitDecoder:
     def capture(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
                 bits: int, t_local: int, out, pool=None) -> CapturedStep:
         """This step on these tensors as CUDA graphs; `.replay()` reruns it on
-        whatever they then hold. With the peer transport, or with one rank,
-        the graphs hold the whole step (one graph per record parity for the
-        peer transport). With NCCL on more ranks they hold the partial only and
+        whatever they then hold. With the fused transport one graph holds the
+        whole step (its step count lives in the exchange regions). With the
+        peer transport, or with one rank, the graphs hold the whole step (one
+        graph per record parity for the peer transport). With NCCL on more ranks they hold the partial only and
         the all-gather and merge run eagerly after each replay: a collective
         inside a graph is outside the process group's timeout. Run one eager
         `step` first (it sets the kernels' attributes and sizes the workspace)."""
         import torch
         self._dtype = q.dtype
         args = (q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v)
-        if self.world == 1:
+        if self.world == 1 or self.transport == "fused":
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, pool=pool):
                 self.step(*args, bits=bits, t_local=t_local, out=out)
@@ -284,6 +326,6 @@ class SequenceSplitDecoder:
         return CapturedStep(self, (g,), finish=self.group is not None)
 
     def close(self) -> None:
-        """Release the peer transport's regions (on every rank together)."""
-        if self.transport == "peer":
+        """Release the peer or fused transport's regions (on every rank together)."""
+        if self.transport in ("peer", "fused"):
             self.exchange.close()

@@ -183,3 +183,36 @@ def test_plan_kernel_names_the_kernel_without_a_device(lib):
     assert lib.kvq_plan_kernel(ctypes.byref(_args(t_stride=130))) == CC
     assert lib.kvq_plan_kernel(ctypes.byref(_args(n_heads=32, n_kv_heads=2))) == CC
     assert lib.kvq_plan_kernel(ctypes.byref(_args(bits=5))) == _native.KVQ_ERR_INVALID
+
+
+def test_tsplit_region_layout_and_format_gate_without_a_device(lib):
+    """The one-kernel sequence split: its region is the 256-byte control
+    block, a per-row u32 array (step counts), a partial store of
+    min(64 rows, max(16384, 2 rows))
+    rows and two parities x world records of rows, each row head_dim + 2
+    tagged 8-byte words, each block 256-aligned; it serves the 4-bit group-64
+    tensor-core format only, and refuses other formats and bad ranks before
+    any device work."""
+    def a256(x):
+        return (x + 255) // 256 * 256
+    for rows, world in [(64, 8), (64, 1), (3, 2), (2048, 4), (9000, 2)]:
+        part = min(64 * rows, max(16384, 2 * rows))
+        want = 256 + a256(4 * rows) + a256(8 * 130 * part) + 2 * world * a256(8 * 130 * rows)
+        assert lib.kvq_tsplit_region_bytes(rows, 128, world) == want
+    assert lib.kvq_tsplit_region_bytes(64, 128, 0) == 0
+    assert lib.kvq_tsplit_region_bytes(64, 128, 9) == 0
+    assert lib.kvq_tsplit_region_bytes(64, 64, 1) == 0
+    assert lib.kvq_tsplit_supported(ctypes.byref(_args())) == 1
+    assert lib.kvq_tsplit_supported(ctypes.byref(_args(n_heads=64, n_kv_heads=8))) == 1
+    for over in (dict(bits=8), dict(group_size=32), dict(head_dim=64), dict(dtype=1),
+                 dict(t_stride=130), dict(bits=5)):
+        assert lib.kvq_tsplit_supported(ctypes.byref(_args(**over))) == 0, over
+    a = _args()
+    regions = (ctypes.c_void_p * 1)(1 << 20)
+    nbytes = lib.kvq_tsplit_region_bytes(8, 128, 1)
+    st = lib.kvq_tsplit_decode(ctypes.byref(_args(bits=8)), regions, nbytes, 1, 0, 8192, 0, None)
+    assert st == _native.KVQ_ERR_UNSUPPORTED and b"4-bit group-64" in lib.kvq_last_error()
+    st = lib.kvq_tsplit_decode(ctypes.byref(a), regions, nbytes, 2, 2, 8192, 0, None)
+    assert st == _native.KVQ_ERR_INVALID and b"rank" in lib.kvq_last_error()
+    st = lib.kvq_tsplit_decode(ctypes.byref(a), regions, nbytes - 256, 1, 0, 8192, 0, None)
+    assert st == _native.KVQ_ERR_INVALID and b"kvq_tsplit_region_bytes" in lib.kvq_last_error()

@@ -1,7 +1,8 @@
 """The sequence split on two GPUs, one process per GPU (skipped with fewer):
-both transports -- NCCL all-gather of the partial records, and the peer
-merge over CUDA-IPC-mapped exchange regions -- give the single-GPU oracle's
-verdict, eagerly and replayed from CUDA graphs."""
+all three transports -- NCCL all-gather of the partial records, the peer
+merge over CUDA-IPC-mapped exchange regions, and the one-kernel step that
+stores each head row's record into every rank's region -- give the
+single-GPU oracle's verdict, eagerly and replayed from CUDA graphs."""
 
 from __future__ import annotations
 
@@ -45,7 +46,7 @@ def _rank_main(rank, world, port, path):
         lo, hi = shard_bounds(t, world, rank)
         dev = [to_dev(x, f"cuda:{rank}") for x in
                (q, *pack(kc[:, lo:hi], 4), *pack(vc[:, lo:hi], 4), nk, nv)]
-        for transport in ("nccl", "peer"):
+        for transport in ("nccl", "peer", "fused"):
             dec = SequenceSplitDecoder(1, 64, 128, torch.device("cuda", rank),
                                        group=dist.group.WORLD, transport=transport)
             out = torch.empty_like(dev[0])
@@ -61,8 +62,8 @@ def _rank_main(rank, world, port, path):
                 torch.cuda.synchronize()
                 v = kv.verify_output(inputs, out.cpu().numpy())
                 status.append(f"{transport}-graph {'ok' if v.ok else v}")
-            if transport == "peer":
-                status.append(f"peer-status {dec.exchange.status()}")
+            if transport in ("peer", "fused"):
+                status.append(f"{transport}-status {dec.exchange.status()}")
             del step
             dec.close()
             dist.barrier()
@@ -89,4 +90,5 @@ def test_two_gpu_sequence_split_both_transports(tmp_path):
             p.kill()
     for r in range(world):
         lines = open(f"{path}.{r}").read().splitlines() if os.path.exists(f"{path}.{r}") else ["missing"]
-        assert lines and all(x.endswith(" ok") or x == "peer-status 0" for x in lines), (r, lines)
+        assert lines and all(x.endswith(" ok") or x in ("peer-status 0", "fused-status 0")
+                             for x in lines), (r, lines)
