@@ -334,29 +334,53 @@ int noalloc_scratch(void** out) {
 
 namespace kvq {
 
+// The merges are launched as programmatic dependents of the kernel before
+// them on the stream (the split stage): their CTAs are launched while it
+// streams and wait in pdl_wait() for its completion, which hides the launch
+// gap between the two.
+template <typename TO, bool NORMALIZE>
+static cudaError_t launch_merge_pdl(unsigned blocks, const float* part_o, const float* part_m,
+                                   const float* part_l, uint32_t n_parts, uint32_t rows,
+                                   uint32_t head_dim, uint64_t o_stride, uint64_t ml_stride, TO* out,
+                                   float* out_m, float* out_l, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(MERGE_THREADS);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, merge_kernel<TO, NORMALIZE>, part_o, part_m, part_l, n_parts,
+                              rows, head_dim, o_stride, ml_stride, out, out_m, out_l);
+}
+
 cudaError_t launch_merge(const float* part_o, const float* part_m, const float* part_l,
                          uint32_t n_parts, uint32_t rows, uint32_t head_dim, uint64_t o_stride,
                          uint64_t ml_stride, int out_dtype, void* out, cudaStream_t stream) {
     const unsigned blocks = rows;
+    cudaError_t e;
     if (out_dtype == KVQ_F16)
-        merge_kernel<__half, true><<<blocks, MERGE_THREADS, 0, stream>>>(
-            part_o, part_m, part_l, n_parts, rows, head_dim, o_stride, ml_stride,
-            static_cast<__half*>(out), nullptr, nullptr);
+        e = launch_merge_pdl<__half, true>(blocks, part_o, part_m, part_l, n_parts, rows, head_dim,
+                                           o_stride, ml_stride, static_cast<__half*>(out), nullptr,
+                                           nullptr, stream);
     else
-        merge_kernel<float, true><<<blocks, MERGE_THREADS, 0, stream>>>(
-            part_o, part_m, part_l, n_parts, rows, head_dim, o_stride, ml_stride,
-            static_cast<float*>(out), nullptr, nullptr);
-    return cudaGetLastError();
+        e = launch_merge_pdl<float, true>(blocks, part_o, part_m, part_l, n_parts, rows, head_dim,
+                                          o_stride, ml_stride, static_cast<float*>(out), nullptr,
+                                          nullptr, stream);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_merge_partial(const float* part_o, const float* part_m, const float* part_l,
                                  uint32_t n_parts, uint32_t rows, uint32_t head_dim,
                                  float* out_o, float* out_m, float* out_l, cudaStream_t stream) {
     const unsigned blocks = rows;
-    merge_kernel<float, false><<<blocks, MERGE_THREADS, 0, stream>>>(
-        part_o, part_m, part_l, n_parts, rows, head_dim, (uint64_t)rows * head_dim, rows, out_o,
-        out_m, out_l);
-    return cudaGetLastError();
+    const cudaError_t e = launch_merge_pdl<float, false>(
+        blocks, part_o, part_m, part_l, n_parts, rows, head_dim, (uint64_t)rows * head_dim, rows,
+        out_o, out_m, out_l, stream);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace kvq

@@ -95,6 +95,20 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Programmatic dependent launch (sm_90 and later). A kernel launched right
+// after this one with the programmatic-stream-serialization attribute may
+// start once every CTA of this grid has executed launch_dependents or exited
+// (the tensor-core split stages do so when their stream ends, so the merge
+// that follows is launched while their last CTAs finish; triggering earlier
+// put merge CTAs beside still-streaming ones and cost more than it hid); the
+// dependent calls pdl_wait() before it reads anything this grid
+// wrote -- the wait returns once this grid has completed and its memory is
+// visible. Both are no-ops for a kernel launched without that attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Launch-independent description of one decode problem, built on the host
 // from kvq_args (plain values; passed to kernels by value).
 struct Problem {

@@ -458,6 +458,9 @@ __device__ __forceinline__ void partial_t_body(const Problem& P, float* __restri
                 mo[(warp * 8 + c1) * DH + dlo + 1] = oacc[i][3];
             }
         }
+        // the stream is done: the merge after this grid may launch now (it
+        // waits for the grid's completion before it reads a partial)
+        pdl_launch_dependents();
         finish_partial<HT, GROUP, TAGGED>(P, smem, tid, warp, lane, split, b, hk, h0, nh, with_new,
                                           scale2, err_flag, part_o, part_m, part_l, tagged, tag);
     }

@@ -256,6 +256,10 @@ merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
     __shared__ float s_l[MERGE_MAX_PARTS];
     __shared__ float s_red[2][MERGE_WARPS];
     __shared__ float s_o[MERGE_WARPS][MERGE_MAX_DH];
+    // the partials come from the kernel before this one, which may still be
+    // running when this grid starts: wait for it, and read them through L2
+    // (the read-only path may keep lines from before the wait)
+    pdl_wait();
     const uint32_t row = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int per_lane = (int)head_dim / 32;
@@ -270,13 +274,13 @@ merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
         const float* o = orow + p * o_stride;
 #pragma unroll
         for (int k = 0; k < MERGE_MAX_DH / 32; ++k)
-            ov0[u][k] = (p < n_parts && k < per_lane) ? o[32 * k] : 0.0f;
+            ov0[u][k] = (p < n_parts && k < per_lane) ? __ldcg(o + 32 * k) : 0.0f;
     }
     float m = -INFINITY;
     for (uint32_t p = tid; p < n_parts; p += MERGE_THREADS) {
-        const float v = part_m[p * ml_stride + row];
+        const float v = __ldcg(part_m + p * ml_stride + row);
         s_w[p] = v;
-        s_l[p] = part_l[p * ml_stride + row];
+        s_l[p] = __ldcg(part_l + p * ml_stride + row);
         m = fmaxf(m, v);
     }
     m = warp_max(m);
@@ -322,7 +326,7 @@ merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
             const float* o = orow + p * o_stride;
 #pragma unroll
             for (int k = 0; k < MERGE_MAX_DH / 32; ++k)
-                ov[j][k] = (k < per_lane && wv[j] != 0.0f) ? o[32 * k] : 0.0f;
+                ov[j][k] = (k < per_lane && wv[j] != 0.0f) ? __ldcg(o + 32 * k) : 0.0f;
         }
 #pragma unroll
         for (int j = 0; j < MERGE_UNROLL; ++j)
