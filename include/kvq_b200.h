@@ -243,6 +243,18 @@ const char* kvq_peer_last_error(void);
  * tensor-core kernel's 4-bit group-64 format, and geometries whose merging
  * CTAs leave room for the rest on the device.
  */
+/*
+ * Copy `bytes` between device memory and pinned (page-locked, mapped) host
+ * memory, either way round, with one small kernel on `stream`: the GPU reads
+ * or writes the host side through its mapping. For per-token staging of a
+ * decode step's inputs and output, where a copy engine's fixed latency (about
+ * 6 us per transfer measured on a B200) is most of the cost. Both pointers
+ * 16-byte aligned; host memory must be pinned (cudaHostAlloc / torch
+ * pin_memory). No reference counterpart (the reference's unified memory needs
+ * no copies).
+ */
+int kvq_stage_copy(void* dst, const void* src, size_t bytes, void* stream);
+
 size_t kvq_tsplit_region_bytes(uint32_t rows, uint32_t head_dim, uint32_t world);
 int kvq_tsplit_supported(const kvq_args* a);
 int kvq_tsplit_decode(const kvq_args* a, void* const* regions, size_t region_bytes, uint32_t world,

@@ -29,7 +29,7 @@ EXPORTS = ("kvq_workspace_bytes", "kvq_decode", "kvq_decode_partial", "kvq_split
            "kvq_peer_region_bytes", "kvq_peer_record_offset", "kvq_peer_alloc", "kvq_peer_open",
            "kvq_peer_close", "kvq_peer_free", "kvq_peer_merge", "kvq_peer_status",
            "kvq_peer_last_error", "kvq_tsplit_region_bytes", "kvq_tsplit_supported",
-           "kvq_tsplit_decode")
+           "kvq_tsplit_decode", "kvq_stage_copy")
 
 
 class NativeUnavailable(RuntimeError):
@@ -96,6 +96,7 @@ def _declare(lib) -> None:
         "kvq_tsplit_region_bytes": (SZ, [U32, U32, U32]),
         "kvq_tsplit_supported": (I, [AP]),
         "kvq_tsplit_decode": (I, [AP, P, SZ, U32, U32, P, U64, P]),
+        "kvq_stage_copy": (I, [P, P, SZ, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -717,4 +717,44 @@ int kvq_tsplit_decode(const kvq_args* a, void* const* regions, size_t region_byt
     return KVQ_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Staging copies for per-token host<->device traffic
+// ---------------------------------------------------------------------------
+namespace {
+// One CTA per 64 KiB, 16 bytes per thread per step: the GPU reads (or
+// writes) the host side directly through its mapping, so a copy of a few KB
+// costs a kernel launch and one bus round trip rather than a copy engine's
+// fixed latency.
+__global__ void __launch_bounds__(256) stage_copy_kernel(uint4* __restrict__ dst,
+                                                        const uint4* __restrict__ src, size_t n16,
+                                                        unsigned char* __restrict__ dst_tail,
+                                                        const unsigned char* __restrict__ src_tail,
+                                                        uint32_t tail) {
+    const size_t per_cta = 4096;   // 16-byte words per CTA
+    const size_t lo = (size_t)blockIdx.x * per_cta;
+    const size_t hi = lo + per_cta < n16 ? lo + per_cta : n16;
+    for (size_t i = lo + threadIdx.x; i < hi; i += blockDim.x) dst[i] = src[i];
+    if (blockIdx.x == 0 && threadIdx.x < tail) dst_tail[threadIdx.x] = src_tail[threadIdx.x];
+}
+}  // namespace
+
+int kvq_stage_copy(void* dst, const void* src, size_t bytes, void* stream) {
+    g_error.clear();
+    if (bytes == 0) return KVQ_OK;
+    if (!dst || !src) return fail(KVQ_ERR_INVALID, "kvq_stage_copy: a pointer is NULL");
+    if (!aligned(dst, 16) || !aligned(src, 16))
+        return fail(KVQ_ERR_INVALID, "kvq_stage_copy: both pointers must be 16-byte aligned");
+    const int rc = device_ok();
+    if (rc) return rc;
+    const size_t n16 = bytes / 16;
+    const uint32_t tail = (uint32_t)(bytes % 16);
+    const unsigned blocks = (unsigned)((n16 + 4095) / 4096 > 0 ? (n16 + 4095) / 4096 : 1);
+    stage_copy_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint4*>(dst), static_cast<const uint4*>(src), n16,
+        static_cast<unsigned char*>(dst) + n16 * 16, static_cast<const unsigned char*>(src) + n16 * 16,
+        tail);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? KVQ_OK : cuda_fail(e, "staging copy launch");
+}
+
 }  // extern "C"

@@ -269,6 +269,169 @@ def decode(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, 
     return out
 
 
+def decode_launch(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *, bits,
+                  out, t_cached=None, seq_lens=None, workspace: Workspace | None = None):
+    """The step of `decode` on these exact tensors, validated and planned
+    once: returns launch(stream) that enqueues kvq_decode with the argument
+    block built here (the tensors' contents may change between calls, not
+    their addresses). For serving loops that call the same step every token
+    (`HostStep`)."""
+    torch = _torch()
+    a = _args(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, bits=bits,
+              t_cached=t_cached, seq_lens=seq_lens)
+    _check_buffers(q.device, ("out", out, q.shape, q.dtype))
+    lib = _native.lib()
+    need = lib.kvq_workspace_bytes(a)
+    ws = workspace if workspace is not None else Workspace()
+    buf, have = ws.get(need, q.device)
+    ws_ptr = buf.data_ptr() if buf is not None else None
+    out_ptr = out.data_ptr()
+    keep = (q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, out, seq_lens, buf)
+
+    def launch(stream=None):
+        s = stream if stream is not None else torch.cuda.current_stream(q.device)
+        _native.check(lib.kvq_decode(a, out_ptr, ws_ptr, have, s.cuda_stream))
+        return keep[9]
+
+    return launch
+
+
+_cuda_driver = None
+
+
+def _graph_launcher(graph, stream):
+    """A call that launches `graph` on `stream` and waits for it through the
+    CUDA driver directly (cuGraphLaunch, cuStreamSynchronize: the executable
+    graph is a driver object whichever runtime made it), or None when the
+    driver or the graph's handle cannot be had -- the caller then replays
+    through torch."""
+    import ctypes
+    global _cuda_driver
+    try:
+        if _cuda_driver is None:
+            drv = ctypes.CDLL("libcuda.so.1")
+            drv.cuGraphLaunch.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+            drv.cuGraphLaunch.restype = ctypes.c_int
+            drv.cuStreamSynchronize.argtypes = [ctypes.c_void_p]
+            drv.cuStreamSynchronize.restype = ctypes.c_int
+            _cuda_driver = drv
+        exec_handle = graph.raw_cuda_graph_exec()
+        exec_handle = ctypes.c_void_p(int(exec_handle) if not isinstance(exec_handle, int)
+                                      else exec_handle)
+    except (OSError, AttributeError, TypeError, RuntimeError):
+        return None
+    drv, s = _cuda_driver, ctypes.c_void_p(stream.cuda_stream)
+
+    def launch():
+        rc = drv.cuGraphLaunch(exec_handle, s)
+        if rc == 0:
+            rc = drv.cuStreamSynchronize(s)
+        if rc != 0:
+            raise RuntimeError(f"CUDA driver error {rc} launching a captured decode step")
+
+    return launch
+
+
+class HostStep:
+    """A decode step fed from host memory and returning to it -- the serving
+    loop's shape, where each token's q, new_k and new_v arrive on the host
+    and its output is wanted back there.
+
+    The three inputs share one pinned staging buffer (`q`, `new_k`, `new_v`
+    are views the caller may write into directly) and one device buffer, so a
+    step makes one host-to-device copy; the output comes back with one
+    device-to-host copy into the pinned `out` (both are `kvq_stage_copy`
+    kernels, cheaper than copy-engine transfers at these sizes). `make_launch(q_dev, new_k_dev,
+    new_v_dev, out_dev)` is called once with the device views and returns
+    launch(stream), which enqueues the device step on them (`decode_launch`,
+    or a sequence-split decoder's `launch`). With `graph=True` the copies and the step are captured once as
+    a CUDA graph after one eager step, so each call is one graph launch and
+    one wait. A call returns once the output is in `out`: its duration is the
+    token's latency."""
+
+    def __init__(self, make_launch, q_shape, kv_shape, dtype, device, graph: bool = True):
+        import math
+        torch = _torch()
+        self.device = torch.device(device)
+        esz = torch.empty((), dtype=dtype).element_size()
+        align = 16 // esz                      # each segment starts on 16 bytes
+        n_q, n_kv = math.prod(q_shape), math.prod(kv_shape)
+        off_k = -(-n_q // align) * align
+        off_v = off_k + -(-n_kv // align) * align
+        total = off_v + n_kv
+        self._host = torch.empty(total, dtype=dtype, pin_memory=True)
+        self._dev = torch.empty(total, dtype=dtype, device=self.device)
+        self.q = self._host[:n_q].view(q_shape)
+        self.new_k = self._host[off_k:off_k + n_kv].view(kv_shape)
+        self.new_v = self._host[off_v:off_v + n_kv].view(kv_shape)
+        self.out = torch.empty(q_shape, dtype=dtype, pin_memory=True)
+        dq = self._dev[:n_q].view(q_shape)
+        dk = self._dev[off_k:off_k + n_kv].view(kv_shape)
+        dv = self._dev[off_v:off_v + n_kv].view(kv_shape)
+        self._dout = torch.empty(q_shape, dtype=dtype, device=self.device)
+        self.h2d_bytes = total * esz
+        self.d2h_bytes = self.out.numel() * esz
+        self._stream = torch.cuda.Stream(self.device)
+        self._done = torch.cuda.Event()
+        with torch.cuda.stream(self._stream):
+            launch = make_launch(dq, dk, dv, self._dout)
+
+        lib = _native.lib()
+        h_in, d_in, n_in = self._host.data_ptr(), self._dev.data_ptr(), self.h2d_bytes
+        h_out, d_out, n_out = self.out.data_ptr(), self._dout.data_ptr(), self.d2h_bytes
+
+        def body():
+            # the staging copies are kernels reading / writing the pinned
+            # buffers through their mapping (kvq_stage_copy): a few KB each,
+            # where a copy engine's fixed latency would dominate
+            s = self._stream.cuda_stream
+            _native.check(lib.kvq_stage_copy(d_in, h_in, n_in, s))
+            launch(self._stream)
+            _native.check(lib.kvq_stage_copy(h_out, d_out, n_out, s))
+
+        self._body = body
+        with torch.cuda.stream(self._stream):
+            body()                            # sets the kernels' attributes
+        self._stream.synchronize()
+        self._graph = None
+        self._launch_graph = None
+        if graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self._stream):
+                body()
+            self._graph = g
+            self._launch_graph = _graph_launcher(g, self._stream)
+        # numpy views of the pinned staging: a host copy into them costs a
+        # memcpy, not a torch dispatch
+        self._np = (self.q.numpy(), self.new_k.numpy(), self.new_v.numpy())
+
+    def __call__(self, q=None, new_k=None, new_v=None):
+        """One step; q / new_k / new_v (host tensors or arrays), when given,
+        are copied into the staging views first. Returns the pinned `out`,
+        valid until the next call."""
+        import numpy as np
+        for src, dst in zip((q, new_k, new_v), self._np):
+            if src is not None:
+                np.copyto(dst, src if isinstance(src, np.ndarray) else src.numpy(), casting="no")
+        if self._launch_graph is not None:
+            self._launch_graph()
+            return self.out
+        torch = _torch()
+        with torch.cuda.stream(self._stream):
+            if self._graph is not None:
+                self._graph.replay()
+            else:
+                self._body()
+            self._done.record(self._stream)
+        self._done.synchronize()
+        return self.out
+
+    def close(self) -> None:
+        """Release the captured graph (before the tensors it uses go)."""
+        self._launch_graph = None
+        self._graph = None
+
+
 def decode_partial(q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
                    bits, t_begin, t_end, has_new_entry, t_cached=None, seq_lens=None,
                    part_o=None, part_m=None, part_l=None, workspace: Workspace | None = None,

@@ -266,6 +266,37 @@ class SequenceSplitDecoder:
             torch.cuda.current_stream(q.device).cuda_stream))
         return out
 
+    def launch(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
+               bits: int, t_local: int, out):
+        """The step on these exact tensors as launch(stream) (for `HostStep`):
+        with the fused transport the argument block is built once and each
+        call is one kvq_tsplit_decode; otherwise each call is `step`. Every
+        rank must call it every step."""
+        import torch
+        from kernelverify_b200 import _native
+        from kernelverify_b200.pack import kv_attention as kva
+        args = (q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v)
+        if self.transport != "fused":
+            def eager(stream=None):
+                with torch.cuda.stream(stream if stream is not None
+                                       else torch.cuda.current_stream(self.device)):
+                    return self.step(*args, bits=bits, t_local=t_local, out=out)
+            return eager
+        kva._check_buffers(self.device, ("out", out, (self.b_rows, self.n_heads, self.head_dim),
+                                         q.dtype))
+        a = kva._args(*args, bits=bits, t_cached=t_local, t_begin=0, t_end=t_local,
+                      has_new_entry=owns_new_entry(self.world, self.rank))
+        lib, ex, out_ptr = _native.lib(), self.exchange, out.data_ptr()
+
+        def fused(stream=None):
+            s = stream if stream is not None else torch.cuda.current_stream(self.device)
+            _native.check(lib.kvq_tsplit_decode(a, ex._array, ex.nbytes, self.world, self.rank,
+                                                out_ptr, ex.timeout_us, s.cuda_stream))
+            self.steps += 1
+            return out
+        fused.keep = args
+        return fused
+
     def step(self, q, k_wq, k_scales, k_biases, v_wq, v_scales, v_biases, new_k, new_v, *,
              bits: int, t_local: int, out=None):
         """out [B, H, DH] in q's dtype, identical on every rank. On a single
