@@ -411,6 +411,8 @@ def run_ours(args) -> dict | None:
     # config 5 on more than one rank adds the merge of the ranks' records; the
     # fused sequence split is one kernel
     fused = args.config == 5 and args.transport == "fused"
+    if fused:
+        n_splits = lib.kvq_tsplit_split_count(margs[0])
     launches_per_step = 1 if fused else 2 + (1 if args.config == 5 and world > 1 else 0)
 
     sampler = ClockSampler(local)

@@ -257,6 +257,8 @@ int kvq_stage_copy(void* dst, const void* src, size_t bytes, void* stream);
 
 size_t kvq_tsplit_region_bytes(uint32_t rows, uint32_t head_dim, uint32_t world);
 int kvq_tsplit_supported(const kvq_args* a);
+/* splits per unit kvq_tsplit_decode plans for a (0 when it does not serve a) */
+uint32_t kvq_tsplit_split_count(const kvq_args* a);
 int kvq_tsplit_decode(const kvq_args* a, void* const* regions, size_t region_bytes, uint32_t world,
                       uint32_t rank, void* out, uint64_t timeout_us, void* stream);
 

@@ -28,7 +28,7 @@ EXPORTS = ("kvq_workspace_bytes", "kvq_decode", "kvq_decode_partial", "kvq_split
            "kvq_dequant", "kvq_quantize", "kvq_cache_append", "kvq_supports", "kvq_plan_kernel", "kvq_last_error", "kvq_abi_version",
            "kvq_peer_region_bytes", "kvq_peer_record_offset", "kvq_peer_alloc", "kvq_peer_open",
            "kvq_peer_close", "kvq_peer_free", "kvq_peer_merge", "kvq_peer_status",
-           "kvq_peer_last_error", "kvq_tsplit_region_bytes", "kvq_tsplit_supported",
+           "kvq_peer_last_error", "kvq_tsplit_region_bytes", "kvq_tsplit_supported", "kvq_tsplit_split_count",
            "kvq_tsplit_decode", "kvq_stage_copy")
 
 
@@ -95,6 +95,7 @@ def _declare(lib) -> None:
         "kvq_peer_last_error": (ctypes.c_char_p, []),
         "kvq_tsplit_region_bytes": (SZ, [U32, U32, U32]),
         "kvq_tsplit_supported": (I, [AP]),
+        "kvq_tsplit_split_count": (U32, [AP]),
         "kvq_tsplit_decode": (I, [AP, P, SZ, U32, U32, P, U64, P]),
         "kvq_stage_copy": (I, [P, P, SZ, P]),
     }

@@ -647,6 +647,37 @@ static bool tsplit_plan_ok(const kvq_args* a, const Plan& pl) {
     return pl.kernel == KERNEL_MMA4 && a->bits == 4 && a->group_size == 64;
 }
 
+// The one-kernel step's split plan: for two CTAs per SM, not the three that
+// fit -- with the merge in the same launch, fewer and longer splits measured
+// faster at every shard size on a B200 (T = 16384 .. 131072, 8 cache heads:
+// fewer partials to merge, fewer streaming CTAs beside each merging one) --
+// and within the region's partial store (at most part_rows / rows splits).
+static void tsplit_replan(const kvq_args* a, Plan* pl) {
+    const uint32_t end = a->t_end < a->t_cached ? a->t_end : a->t_cached;
+    const uint64_t span = end > a->t_begin ? end - a->t_begin : 0;
+    const uint64_t units = (uint64_t)a->b_rows * a->n_kv_heads * pl->P.head_tiles;
+    const uint64_t stage = (uint64_t)kvq::mma4_stage_positions();
+    mma4_splits(span, units, 2, &pl->P.chunk, &pl->P.n_splits, stage, kMmaRamp);
+    const uint64_t cap = kvq::fused::part_rows(pl->rows) / pl->rows;
+    if (pl->P.n_splits > cap) {
+        const uint64_t chunk = ((span + cap - 1) / cap + stage - 1) / stage * stage;
+        pl->P.chunk = (uint32_t)chunk;
+        pl->P.n_splits = (uint32_t)((span + chunk - 1) / chunk);
+    }
+}
+
+uint32_t kvq_tsplit_split_count(const kvq_args* a) {
+    std::string keep = g_error;
+    Plan pl;
+    uint32_t n = 0;
+    if (plan(a, &pl) == KVQ_OK && tsplit_plan_ok(a, pl)) {
+        tsplit_replan(a, &pl);
+        n = pl.P.n_splits;
+    }
+    g_error = keep;
+    return n;
+}
+
 size_t kvq_tsplit_region_bytes(uint32_t rows, uint32_t head_dim, uint32_t world) {
     if (rows == 0 || head_dim != kvq::fused::DH || world == 0 || world > KVQ_PEER_MAX_RANKS) return 0;
     return (size_t)kvq::fused::region_layout(rows, world).total;
@@ -682,16 +713,7 @@ int kvq_tsplit_decode(const kvq_args* a, void* const* regions, size_t region_byt
     if (region_bytes < L.total)
         return fail(KVQ_ERR_INVALID, "regions of %zu bytes are smaller than the %llu this step "
                     "needs (kvq_tsplit_region_bytes)", region_bytes, (unsigned long long)L.total);
-    // the partials live in the region's store: at most part_rows / rows splits
-    const uint64_t cap = L.part_rows / pl.rows;
-    if (pl.P.n_splits > cap) {
-        const uint32_t end = a->t_end < a->t_cached ? a->t_end : a->t_cached;
-        const uint64_t span = end > a->t_begin ? end - a->t_begin : 0;
-        const uint64_t stage = (uint64_t)kvq::mma4_stage_positions();
-        const uint64_t chunk = ((span + cap - 1) / cap + stage - 1) / stage * stage;
-        pl.P.chunk = (uint32_t)chunk;
-        pl.P.n_splits = (uint32_t)((span + chunk - 1) / chunk);
-    }
+    tsplit_replan(a, &pl);
     rc = device_ok();
     if (rc) return rc;
     // the merging CTAs wait for the rest of their unit: they must leave room

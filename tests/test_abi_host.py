@@ -204,6 +204,11 @@ def test_tsplit_region_layout_and_format_gate_without_a_device(lib):
     assert lib.kvq_tsplit_region_bytes(64, 64, 1) == 0
     assert lib.kvq_tsplit_supported(ctypes.byref(_args())) == 1
     assert lib.kvq_tsplit_supported(ctypes.byref(_args(n_heads=64, n_kv_heads=8))) == 1
+    # config 5 on one rank without a device: 8 units planned for two CTAs on
+    # each of the fallback 148 SMs -> 37 splits
+    c5 = _args(n_heads=64, n_kv_heads=8, t_cached=131072, t_stride=131072)
+    assert lib.kvq_tsplit_split_count(ctypes.byref(c5)) == 37
+    assert lib.kvq_tsplit_split_count(ctypes.byref(_args(bits=8))) == 0
     for over in (dict(bits=8), dict(group_size=32), dict(head_dim=64), dict(dtype=1),
                  dict(t_stride=130), dict(bits=5)):
         assert lib.kvq_tsplit_supported(ctypes.byref(_args(**over))) == 0, over
