@@ -343,6 +343,9 @@ static cudaError_t launch_merge_pdl(unsigned blocks, const float* part_o, const 
                                    const float* part_l, uint32_t n_parts, uint32_t rows,
                                    uint32_t head_dim, uint64_t o_stride, uint64_t ml_stride, TO* out,
                                    float* out_m, float* out_l, cudaStream_t stream) {
+    // the split stage's sizes take the one-round-trip merge
+    const bool small = head_dim == 128 && n_parts <= (uint32_t)MERGE_SMALL_PARTS &&
+                       aligned(part_o, 16) && o_stride % 4 == 0;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(blocks);
     cfg.blockDim = dim3(MERGE_THREADS);
@@ -353,6 +356,9 @@ static cudaError_t launch_merge_pdl(unsigned blocks, const float* part_o, const 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (small)
+        return cudaLaunchKernelEx(&cfg, merge_small_kernel<TO, NORMALIZE>, part_o, part_m, part_l,
+                                  n_parts, rows, o_stride, ml_stride, out, out_m, out_l);
     return cudaLaunchKernelEx(&cfg, merge_kernel<TO, NORMALIZE>, part_o, part_m, part_l, n_parts,
                               rows, head_dim, o_stride, ml_stride, out, out_m, out_l);
 }

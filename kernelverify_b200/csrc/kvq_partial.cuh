@@ -356,4 +356,107 @@ merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
     }
 }
 
+// The merge at the split stage's sizes (head_dim 128, at most 64 parts, O
+// rows 16-byte aligned): every load of a row -- each warp's parts' O columns
+// (a float4 per lane) and their m and l -- is requested at once, one round
+// trip, instead of the general kernel's dependent phases. Warp w folds parts
+// w, w + 8, ... under its own running maximum; the eight warps then meet in
+// shared memory. Same results as merge_kernel up to the order of the fp32
+// sums; an empty part (m = -inf) adds nothing, a NaN m poisons the row.
+constexpr int MERGE_SMALL_PARTS = 64;
+
+template <typename TO, bool NORMALIZE>
+__global__ void __launch_bounds__(MERGE_THREADS)
+merge_small_kernel(const float* __restrict__ part_o, const float* __restrict__ part_m,
+                   const float* __restrict__ part_l, uint32_t n_parts, uint32_t rows,
+                   uint64_t o_stride, uint64_t ml_stride, TO* __restrict__ out,
+                   float* __restrict__ out_m, float* __restrict__ out_l) {
+    constexpr int DH = 128, PER_WARP = MERGE_SMALL_PARTS / MERGE_WARPS;
+    __shared__ float s_m[MERGE_WARPS], s_l[MERGE_WARPS];
+    __shared__ float4 s_o[MERGE_WARPS][DH / 4];
+    // the partials come from the kernel before this one (see merge_kernel)
+    pdl_wait();
+    const uint32_t row = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float4 o[PER_WARP];
+    float mv[PER_WARP], lv[PER_WARP];
+#pragma unroll
+    for (int i = 0; i < PER_WARP; ++i) {
+        const uint32_t p = warp + i * MERGE_WARPS;
+        if (p < n_parts) {
+            o[i] = __ldcg(reinterpret_cast<const float4*>(part_o + p * o_stride + (size_t)row * DH) + lane);
+            mv[i] = __ldcg(part_m + p * ml_stride + row);
+            lv[i] = __ldcg(part_l + p * ml_stride + row);
+        } else {
+            o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            mv[i] = -INFINITY;
+            lv[i] = 0.0f;
+        }
+    }
+    float M = -INFINITY;
+    bool poisoned = false;
+#pragma unroll
+    for (int i = 0; i < PER_WARP; ++i) {
+        M = fmaxf(M, mv[i]);
+        poisoned |= mv[i] != mv[i];
+    }
+    float L = 0.0f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < PER_WARP; ++i) {
+        const float w = mv[i] == -INFINITY ? 0.0f : expf(mv[i] - M);
+        if (w != 0.0f) {
+            L = fmaf(lv[i], w, L);
+            acc.x = fmaf(o[i].x, w, acc.x);
+            acc.y = fmaf(o[i].y, w, acc.y);
+            acc.z = fmaf(o[i].z, w, acc.z);
+            acc.w = fmaf(o[i].w, w, acc.w);
+        }
+    }
+    if (poisoned) M = L = __int_as_float(0x7fc00000);
+    if (lane == 0) {
+        s_m[warp] = M;
+        s_l[warp] = L;
+    }
+    s_o[warp][lane] = acc;
+    __syncthreads();
+    if (warp != 0) return;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < MERGE_WARPS; ++w) m = fmaxf(m, s_m[w]);
+    float lt = 0.0f;
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < MERGE_WARPS; ++w) {
+        if (s_m[w] == -INFINITY) continue;
+        const float c = expf(s_m[w] - m);
+        const float4 x = s_o[w][lane];
+        lt = fmaf(s_l[w], c, lt);
+        r.x = fmaf(x.x, c, r.x);
+        r.y = fmaf(x.y, c, r.y);
+        r.z = fmaf(x.z, c, r.z);
+        r.w = fmaf(x.w, c, r.w);
+    }
+    TO* dst = out + (size_t)row * DH + 4 * lane;
+    if constexpr (NORMALIZE) {
+        dst[0] = from_f32<TO>(r.x / lt);
+        dst[1] = from_f32<TO>(r.y / lt);
+        dst[2] = from_f32<TO>(r.z / lt);
+        dst[3] = from_f32<TO>(r.w / lt);
+    } else {
+        // no part at all (m = -inf, l = 0): a zero row; a poisoned one keeps
+        // NaN in m as well, so a later merge of this record stays poisoned
+        const bool empty = m == -INFINITY && lt == 0.0f;
+        if (lt != lt) m = lt;
+        dst[0] = empty ? 0.0f : r.x;
+        dst[1] = empty ? 0.0f : r.y;
+        dst[2] = empty ? 0.0f : r.z;
+        dst[3] = empty ? 0.0f : r.w;
+        if (lane == 0) {
+            out_m[row] = m;
+            out_l[row] = lt;
+        }
+    }
+}
+
 }  // namespace kvq
