@@ -250,7 +250,8 @@ const char* kvq_peer_last_error(void);
  * decode step's inputs and output, where a copy engine's fixed latency (about
  * 6 us per transfer measured on a B200) is most of the cost. Both pointers
  * 16-byte aligned; host memory must be pinned (cudaHostAlloc / torch
- * pin_memory). No reference counterpart (the reference's unified memory needs
+ * pin_memory): pageable host memory is refused with KVQ_ERR_INVALID. No
+ * reference counterpart (the reference's unified memory needs
  * no copies).
  */
 int kvq_stage_copy(void* dst, const void* src, size_t bytes, void* stream);

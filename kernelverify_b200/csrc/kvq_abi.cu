@@ -774,6 +774,17 @@ int kvq_stage_copy(void* dst, const void* src, size_t bytes, void* stream) {
         return fail(KVQ_ERR_INVALID, "kvq_stage_copy: both pointers must be 16-byte aligned");
     const int rc = device_ok();
     if (rc) return rc;
+    // the GPU dereferences both sides: ordinary (pageable) host memory is not
+    // mapped into its address space and would fault the device, so it is
+    // refused here
+    for (const void* p : {static_cast<const void*>(dst), src}) {
+        cudaPointerAttributes at{};
+        const cudaError_t e = cudaPointerGetAttributes(&at, p);
+        if (e != cudaSuccess) return cuda_fail(e, "kvq_stage_copy: pointer query");
+        if (at.type == cudaMemoryTypeUnregistered)
+            return fail(KVQ_ERR_INVALID, "kvq_stage_copy: %p is pageable host memory; pin it "
+                        "(cudaHostAlloc / torch pin_memory) or pass device memory", p);
+    }
     const size_t n16 = bytes / 16;
     const uint32_t tail = (uint32_t)(bytes % 16);
     const unsigned blocks = (unsigned)((n16 + 4095) / 4096 > 0 ? (n16 + 4095) / 4096 : 1);

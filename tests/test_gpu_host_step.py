@@ -82,3 +82,25 @@ def test_host_step_over_the_fused_sequence_split(native):
     finally:
         step.close()
         dec.close()
+
+
+def test_stage_copy_both_ways_and_pageable_memory_refused(native):
+    """kvq_stage_copy: pinned -> device and device -> pinned, sizes with and
+    without a tail under 16 bytes, bit for bit; pageable host memory is
+    refused with a status before anything runs."""
+    import torch
+    from kernelverify_b200 import _native
+    lib = _native.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    for nbytes in (16, 4096 + 6, 20480, 70000 * 16 + 2):
+        src = torch.randint(0, 256, (nbytes,), dtype=torch.uint8).pin_memory()
+        dev = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+        back = torch.zeros(nbytes, dtype=torch.uint8).pin_memory()
+        _native.check(lib.kvq_stage_copy(dev.data_ptr(), src.data_ptr(), nbytes, s))
+        _native.check(lib.kvq_stage_copy(back.data_ptr(), dev.data_ptr(), nbytes, s))
+        torch.cuda.synchronize()
+        assert torch.equal(dev.cpu(), src) and torch.equal(back, src)
+    pageable = torch.zeros(4096, dtype=torch.uint8)
+    dev = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    st = lib.kvq_stage_copy(dev.data_ptr(), pageable.data_ptr(), 4096, s)
+    assert st == _native.KVQ_ERR_INVALID and b"pageable" in lib.kvq_last_error()
