@@ -570,7 +570,8 @@ def run_ours(args) -> dict | None:
     else:
         value = step_kv / (step_ms * 1e-3) / 1e9
         scaling, workload = "strong", "config5-long-context-tsplit"
-    traffic_key = f"partial_kernel_config{args.config}_n{world}"
+    traffic_key = (f"fused_kernel_config5_n{world}" if fused
+                   else f"partial_kernel_config{args.config}_n{world}")
     line = {
         "metric": METRIC,
         "value": round(value, 1),
