@@ -120,3 +120,15 @@ def test_a_rank_that_leaves_makes_the_collective_fail_not_hang(tmp_path):
     status = _spawn(2, tmp_path, leave_early=True)
     assert status[1] == "missing"
     assert status[0].startswith("error"), status
+
+
+def test_decoder_rejects_unknown_transports_and_unserved_geometry():
+    """Host checks of the sequence-split decoder, before any device work: an
+    unknown transport, and a fused region for a head_dim the one-kernel step
+    does not serve (kvq_tsplit_region_bytes is 0 there)."""
+    import pytest
+    from kernelverify_b200.pack.tsplit import SequenceSplitDecoder
+    with pytest.raises(ValueError, match="transport"):
+        SequenceSplitDecoder(1, 8, 128, "cpu", transport="bogus")
+    with pytest.raises(ValueError, match="no fused region"):
+        SequenceSplitDecoder(1, 8, 64, "cpu", transport="fused")
