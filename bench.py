@@ -616,7 +616,7 @@ def run_ours(args) -> dict | None:
             "ratio": round(value / line["cpu_baseline"]["value"], 1),
             "cores": line["cpu_baseline"]["cores"],
             "note": "value / cpu_baseline.value (GB/s over GB/s); vs_baseline stays null: "
-                    "BASELINE.md publishes no number for this metric"}
+                    "no published number exists for this metric"}
     if dist is not None:
         dist.destroy_process_group()
     return line
